@@ -1,0 +1,509 @@
+/*
+ * gxo.c — CPU oracle for the Gyro routed-MoE layer. TEST INFRASTRUCTURE ONLY (see gxo.h).
+ *
+ * Built twice by oracle/Makefile:
+ *   liboracle.so       -O2 -ffp-contract=off, serial: the parity checker.
+ *   liboracle_fast.so  -O3 -DGXO_THREADS -pthread: the timed CPU baseline (the reference's
+ *                      own CPU engine is Zig, and no Zig toolchain exists on these machines).
+ * Every function names the reference lines it restates.
+ */
+#include "gxo.h"
+
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef GXO_THREADS
+#include <pthread.h>
+#include <stdatomic.h>
+#include <unistd.h>
+#endif
+
+static float g_codebook[4096]; /* f32 expansion of the table, src/kernels.zig:15-23 */
+static int g_codebook_ready = 0;
+
+int gxo_set_codebook(const void *table, size_t bytes) {
+    if (!table || bytes != 8192) return -1;
+    const uint8_t *b = (const uint8_t *)table;
+    for (int i = 0; i < 4096; ++i)
+        g_codebook[i] = gxo_fp16_to_fp32((uint16_t)(b[2 * i] | (b[2 * i + 1] << 8)));
+    g_codebook_ready = 1;
+    return 0;
+}
+
+int gxo_max_threads(void) {
+#ifdef GXO_THREADS
+    long n = sysconf(_SC_NPROCESSORS_ONLN);
+    return n > 0 ? (int)n : 1;
+#else
+    return 1;
+#endif
+}
+
+/* Chunked parallel-for in the manner of src/pool.zig:84-114: an atomic cursor hands out
+ * [start, start + chunk) ranges; the calling thread participates. */
+typedef void (*range_fn)(void *ctx, size_t start, size_t end);
+#ifdef GXO_THREADS
+typedef struct pool_job {
+    range_fn fn;
+    void *ctx;
+    size_t count, chunk;
+    atomic_size_t next;
+} pool_job;
+
+static void *pool_drain(void *arg) {
+    pool_job *job = (pool_job *)arg;
+    for (;;) {
+        size_t start = atomic_fetch_add_explicit(&job->next, job->chunk, memory_order_relaxed);
+        if (start >= job->count) break;
+        size_t end = start + job->chunk < job->count ? start + job->chunk : job->count;
+        job->fn(job->ctx, start, end);
+    }
+    return NULL;
+}
+#endif
+
+static void pool_run(int threads, size_t count, size_t chunk, range_fn fn, void *ctx) {
+    if (count == 0) return;
+    if (chunk == 0) chunk = 1;
+#ifdef GXO_THREADS
+    if (threads > 1 && count > chunk) {
+        pool_job job = {fn, ctx, count, chunk, 0};
+        pthread_t tid[256];
+        int started = 0;
+        for (int i = 0; i < threads - 1 && i < 256; ++i)
+            if (pthread_create(&tid[i], NULL, pool_drain, &job) == 0) started++;
+        pool_drain(&job);
+        for (int i = 0; i < started; ++i) pthread_join(tid[i], NULL);
+        return;
+    }
+#else
+    (void)threads;
+#endif
+    fn(ctx, 0, count);
+}
+
+/* src/gyro.zig:32-41 */
+int gxo_type_info(uint32_t type_id, int *k, int *steps, int *block_bytes) {
+    int kk, ss, bb;
+    switch (type_id) {
+        case 144: kk = 8; ss = 32; bb = 34; break; /* TQ2_T */
+        case 145: kk = 6; ss = 32; bb = 26; break; /* TQK6 */
+        case 146: kk = 7; ss = 32; bb = 30; break; /* TQK7 */
+        case 147: kk = 5; ss = 64; bb = 42; break; /* TQP5 */
+        case 148: kk = 6; ss = 64; bb = 50; break; /* TQP6 */
+        case 149: kk = 7; ss = 64; bb = 58; break; /* TQP7 */
+        case 150: kk = 5; ss = 32; bb = 22; break; /* TQK5 */
+        case 151: kk = 4; ss = 32; bb = 18; break; /* TQK4 */
+        default: return -1;
+    }
+    if (k) *k = kk;
+    if (steps) *steps = ss;
+    if (block_bytes) *block_bytes = bb;
+    return 0;
+}
+
+static float bits_to_f32(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
+
+/* src/gyro.zig:128-141: exact conversion of every binary16 pattern, subnormals included. */
+float gxo_fp16_to_fp32(uint16_t half) {
+    uint32_t sign = (uint32_t)(half & 0x8000u) << 16;
+    uint32_t exponent = (half >> 10) & 31u;
+    uint32_t mantissa = half & 1023u;
+    if (exponent == 31) return bits_to_f32(sign | 0x7f800000u | (mantissa << 13));
+    if (exponent != 0) return bits_to_f32(sign | ((exponent + 112u) << 23) | (mantissa << 13));
+    if (mantissa == 0) return bits_to_f32(sign);
+    uint32_t out_exp = 113;
+    while ((mantissa & 1024u) == 0) { mantissa <<= 1; out_exp -= 1; }
+    return bits_to_f32(sign | (out_exp << 23) | ((mantissa & 1023u) << 13));
+}
+
+/* src/gyro.zig:107-117. TQ2_T: previous byte (circular) : this byte. Otherwise a 16-bit
+ * window at bit (steps-1-step)*K of the circular LSB-first stream. */
+uint32_t gxo_state(uint32_t type_id, const uint8_t *stream, int stream_len, int step) {
+    if (type_id == 144) return ((uint32_t)stream[(step + 31) % 32] << 8) | stream[step];
+    int k, steps;
+    gxo_type_info(type_id, &k, &steps, NULL);
+    uint32_t offset = (uint32_t)(steps - 1 - step) * (uint32_t)k;
+    uint32_t byte = offset >> 3;
+    uint32_t word = (uint32_t)stream[byte] |
+                    ((uint32_t)stream[(byte + 1) % (uint32_t)stream_len] << 8) |
+                    ((uint32_t)stream[(byte + 2) % (uint32_t)stream_len] << 16);
+    return (word >> (offset & 7)) & 0xffffu;
+}
+
+/* src/gyro.zig:81-105 (strict): w = d * CB[...] as one binary32 multiply. */
+int gxo_decode_row(uint32_t type_id, int state_bits, const uint8_t *src, size_t src_len,
+                   float *dst, size_t n) {
+    if (state_bits < 0) return -2;
+    if (state_bits != 15) return -3;
+    int k, steps, bb;
+    if (gxo_type_info(type_id, &k, &steps, &bb)) return -1;
+    if (n % 128) return -4;
+    if (src_len != n / 128 * (size_t)bb) return -5;
+    size_t out = 0;
+    for (size_t off = 0; off < src_len; off += (size_t)bb) {
+        const uint8_t *block = src + off;
+        float scale = gxo_fp16_to_fp32((uint16_t)(block[0] | (block[1] << 8)));
+        const uint8_t *stream = block + 2;
+        int pairs = steps == 64 ? 1 : 2;
+        for (int step = 0; step < steps; ++step) {
+            uint32_t state = gxo_state(type_id, stream, bb - 2, step);
+            uint32_t hash = (state & 0x7fffu) * 0x9e3779b1u;
+            for (int pair = 0; pair < pairs; ++pair) {
+                uint32_t index = pair == 0 ? hash >> 21 : (hash >> 10) & 2047u;
+                volatile float a = scale * g_codebook[index * 2];
+                volatile float b = scale * g_codebook[index * 2 + 1];
+                dst[out] = a;
+                dst[out + 1] = b;
+                out += 2;
+            }
+        }
+    }
+    return 0;
+}
+
+/* src/gyro.zig:143-150 */
+static int validate_transform(size_t n, size_t block, const int8_t *signs) {
+    if (block == 0 || (block & (block - 1))) return -1;
+    if (n % block) return -4;
+    if (signs)
+        for (size_t i = 0; i < n; ++i)
+            if (signs[i] != 1 && signs[i] != -1) return -7;
+    return 0;
+}
+
+/* src/gyro.zig:152-172: strict butterflies, then one multiply by 1/sqrt(b) per value. */
+static void hadamard(float *v, size_t n, size_t block) {
+    const float norm = 1.0f / sqrtf((float)block);
+    for (size_t start = 0; start < n; start += block) {
+        float *b = v + start;
+        for (size_t width = 1; width < block; width *= 2)
+            for (size_t s = 0; s < block; s += 2 * width)
+                for (size_t j = 0; j < width; ++j) {
+                    float p = b[s + j], q = b[s + j + width];
+                    b[s + j] = p + q;
+                    b[s + j + width] = p - q;
+                }
+        for (size_t j = 0; j < block; ++j) b[j] *= norm;
+    }
+}
+
+/* src/gyro.zig:177-184 */
+int gxo_rotate(float *v, size_t n, size_t block, const int8_t *signs) {
+    int rc = validate_transform(n, block, signs);
+    if (rc) return rc;
+    if (signs) for (size_t i = 0; i < n; ++i) v[i] *= (float)signs[i];
+    hadamard(v, n, block);
+    return 0;
+}
+
+/* src/gyro.zig:188-195 */
+int gxo_unrotate(float *v, size_t n, size_t block, const int8_t *signs) {
+    int rc = validate_transform(n, block, signs);
+    if (rc) return rc;
+    hadamard(v, n, block);
+    if (signs) for (size_t i = 0; i < n; ++i) v[i] *= (float)signs[i];
+    return 0;
+}
+
+/* src/kernels.zig:317-338 */
+void gxo_rotate_f32(float *x, size_t n, size_t block, const float *signs) {
+    if (signs) for (size_t i = 0; i < n; ++i) x[i] *= signs[i];
+    hadamard(x, n, block);
+}
+
+/* src/kernels.zig:56-67 (f32 and Gyro types only: the non-expert types are out of scope). */
+size_t gxo_row_bytes(uint32_t type_id, size_t cols) {
+    if (type_id == 0) return cols * 4;
+    int bb;
+    if (gxo_type_info(type_id, NULL, NULL, &bb) || cols % 128) return 0;
+    return cols / 128 * (size_t)bb;
+}
+
+/* 8-lane vector reduction of the Zig @reduce(.Add) on a V8. */
+static float reduce8(const float a[8]) {
+    return ((a[0] + a[4]) + (a[2] + a[6])) + ((a[1] + a[5]) + (a[3] + a[7]));
+}
+
+/* src/kernels.zig:72-84 */
+static float dot_f32(const uint8_t *row, const float *x, size_t n) {
+    float acc[8] = {0};
+    size_t i = 0;
+    for (; i + 8 <= n; i += 8)
+        for (int j = 0; j < 8; ++j) {
+            float w;
+            memcpy(&w, row + (i + j) * 4, 4);
+            acc[j] += w * x[i + j];
+        }
+    float sum = reduce8(acc);
+    for (; i < n; ++i) { float w; memcpy(&w, row + i * 4, 4); sum += w * x[i]; }
+    return sum;
+}
+
+/* src/kernels.zig:253-261 */
+static float dot_dense(const float *a, const float *b, size_t n) {
+    float acc[8] = {0};
+    size_t i = 0;
+    for (; i + 8 <= n; i += 8)
+        for (int j = 0; j < 8; ++j) acc[j] += a[i + j] * b[i + j];
+    float sum = reduce8(acc);
+    for (; i < n; ++i) sum += a[i] * b[i];
+    return sum;
+}
+
+/* src/kernels.zig:136-159: one block in the stored basis (fast-path decode, w = d * cb). */
+static void decode_block(uint32_t type_id, int steps, int bb, const uint8_t *block, float *out) {
+    const float scale = gxo_fp16_to_fp32((uint16_t)(block[0] | (block[1] << 8)));
+    const uint8_t *stream = block + 2;
+    if (steps == 32) {
+        for (int step = 0; step < 32; ++step) {
+            uint32_t state = gxo_state(type_id, stream, bb - 2, step);
+            uint32_t h = (state & 0x7fffu) * 0x9e3779b1u;
+            uint32_t a = (h >> 21) * 2, b = ((h >> 10) & 2047u) * 2;
+            out[step * 4 + 0] = scale * g_codebook[a];
+            out[step * 4 + 1] = scale * g_codebook[a + 1];
+            out[step * 4 + 2] = scale * g_codebook[b];
+            out[step * 4 + 3] = scale * g_codebook[b + 1];
+        }
+    } else {
+        for (int step = 0; step < 64; ++step) {
+            uint32_t state = gxo_state(type_id, stream, bb - 2, step);
+            uint32_t h = (state & 0x7fffu) * 0x9e3779b1u;
+            uint32_t a = (h >> 21) * 2;
+            out[step * 2 + 0] = scale * g_codebook[a];
+            out[step * 2 + 1] = scale * g_codebook[a + 1];
+        }
+    }
+}
+
+/* src/kernels.zig:161-183: fused TQ2_T dot, per block a 4-lane accumulator times the scale. */
+static float dot_tq2(const uint8_t *row, const float *x, size_t cols) {
+    float total = 0;
+    for (size_t bi = 0; bi < cols / 128; ++bi) {
+        const uint8_t *block = row + bi * 34;
+        const float scale = gxo_fp16_to_fp32((uint16_t)(block[0] | (block[1] << 8)));
+        const uint8_t *stream = block + 2;
+        const float *xb = x + bi * 128;
+        float acc[4] = {0, 0, 0, 0};
+        for (int step = 0; step < 32; ++step) {
+            uint32_t state = ((uint32_t)stream[(step + 31) & 31] << 8) | stream[step];
+            uint32_t h = (state & 0x7fffu) * 0x9e3779b1u;
+            uint32_t a = (h >> 21) * 2, b = ((h >> 10) & 2047u) * 2;
+            acc[0] += g_codebook[a] * xb[step * 4 + 0];
+            acc[1] += g_codebook[a + 1] * xb[step * 4 + 1];
+            acc[2] += g_codebook[b] * xb[step * 4 + 2];
+            acc[3] += g_codebook[b + 1] * xb[step * 4 + 3];
+        }
+        total += scale * ((acc[0] + acc[2]) + (acc[1] + acc[3]));
+    }
+    return total;
+}
+
+/* src/kernels.zig:185-199 */
+static float dot_gyro_generic(uint32_t type_id, const uint8_t *row, const float *x, size_t cols) {
+    int steps, bb;
+    gxo_type_info(type_id, NULL, &steps, &bb);
+    float total = 0, tmp[128];
+    for (size_t bi = 0; bi < cols / 128; ++bi) {
+        decode_block(type_id, steps, bb, row + bi * (size_t)bb, tmp);
+        float acc[8] = {0};
+        for (int i = 0; i < 128; i += 8)
+            for (int j = 0; j < 8; ++j) acc[j] += tmp[i + j] * x[bi * 128 + i + j];
+        total += reduce8(acc);
+    }
+    return total;
+}
+
+/* src/kernels.zig:201-210 */
+float gxo_dot_row(uint32_t type_id, const uint8_t *row, const float *x, size_t cols) {
+    if (type_id == 0) return dot_f32(row, x, cols);
+    if (type_id == 144) return dot_tq2(row, x, cols);
+    return dot_gyro_generic(type_id, row, x, cols);
+}
+
+/* src/kernels.zig:213-235 (Gyro branch) */
+void gxo_decode_row_fast(uint32_t type_id, const uint8_t *row, float *out, size_t cols) {
+    int steps, bb;
+    gxo_type_info(type_id, NULL, &steps, &bb);
+    for (size_t b = 0; b < cols / 128; ++b) decode_block(type_id, steps, bb, row + b * (size_t)bb, out + b * 128);
+}
+
+/* src/kernels.zig:340-349 */
+void gxo_softmax(float *x, size_t n) {
+    float m = -INFINITY;
+    for (size_t i = 0; i < n; ++i) m = x[i] > m ? x[i] : m;
+    float sum = 0;
+    for (size_t i = 0; i < n; ++i) { x[i] = expf(x[i] - m); sum += x[i]; }
+    for (size_t i = 0; i < n; ++i) x[i] /= sum;
+}
+
+/* src/engine.zig:671-686: insertion top-k; ties prefer the lower index. */
+void gxo_topk(const float *values, size_t n, uint32_t *ids, float *weights, size_t k) {
+    const uint32_t none = 0xffffffffu;
+    for (size_t j = 0; j < k; ++j) { ids[j] = none; weights[j] = -INFINITY; }
+    for (size_t i = 0; i < n; ++i) {
+        float v = values[i];
+        if (v <= weights[k - 1] && ids[k - 1] != none) continue;
+        size_t pos = k - 1;
+        while (pos > 0 && (v > weights[pos - 1] || ids[pos - 1] == none)) {
+            weights[pos] = weights[pos - 1];
+            ids[pos] = ids[pos - 1];
+            pos -= 1;
+        }
+        weights[pos] = v;
+        ids[pos] = (uint32_t)i;
+    }
+}
+
+/* src/kernels.zig:307-309 */
+static float silu(float x) { return x / (1.0f + expf(-x)); }
+
+/* Shared state of one gxo_moe_ffn call for the parallel ranges. */
+typedef struct ffn_ctx {
+    const gxo_layer *l;
+    const float *x, *xh;
+    size_t n, E, F, U, NE, gate_row, down_row;
+    float *router, *act, *act_up, *down;
+    const uint32_t *start, *order;
+} ffn_ctx;
+
+/* Router rows: kernels.matmul, src/engine.zig:526 -> src/kernels.zig:239-268. */
+static void router_range(void *p, size_t a, size_t b) {
+    ffn_ctx *c = (ffn_ctx *)p;
+    for (size_t r = a; r < b; ++r)
+        for (size_t t = 0; t < c->n; ++t)
+            c->router[t * c->NE + r] =
+                dot_f32((const uint8_t *)(c->l->router + r * c->E), c->x + t * c->E, c->E);
+}
+
+/* Phase 1, one task per (expert, row), src/engine.zig:568-602. */
+static void gate_up_range(void *p, size_t a, size_t b) {
+    ffn_ctx *c = (ffn_ctx *)p;
+    const size_t E = c->E, F = c->F, U = c->U;
+    float *wbuf = malloc(sizeof(float) * E);
+    for (size_t task = a; task < b; ++task) {
+        size_t e = task / F, row = task % F;
+        uint32_t first = c->start[e], last = c->start[e + 1];
+        if (first == last) continue;
+        const uint8_t *g = c->l->gate + (e * F + row) * c->gate_row;
+        const uint8_t *u = c->l->up + (e * F + row) * c->gate_row;
+        if (last - first == 1) {
+            uint32_t slot = c->order[first];
+            const float *xs = c->xh + (slot / U) * E;
+            c->act[slot * F + row] = gxo_dot_row(c->l->type_id, g, xs, E);
+            c->act_up[slot * F + row] = gxo_dot_row(c->l->type_id, u, xs, E);
+            continue;
+        }
+        gxo_decode_row_fast(c->l->type_id, g, wbuf, E);
+        for (uint32_t i = first; i < last; ++i) {
+            uint32_t slot = c->order[i];
+            c->act[slot * F + row] = dot_dense(wbuf, c->xh + (slot / U) * E, E);
+        }
+        gxo_decode_row_fast(c->l->type_id, u, wbuf, E);
+        for (uint32_t i = first; i < last; ++i) {
+            uint32_t slot = c->order[i];
+            c->act_up[slot * F + row] = dot_dense(wbuf, c->xh + (slot / U) * E, E);
+        }
+    }
+    free(wbuf);
+}
+
+/* Phase 2, one task per (expert, output row), src/engine.zig:609-633. */
+static void down_range(void *p, size_t a, size_t b) {
+    ffn_ctx *c = (ffn_ctx *)p;
+    const size_t E = c->E, F = c->F;
+    float *wbuf = malloc(sizeof(float) * F);
+    for (size_t task = a; task < b; ++task) {
+        size_t e = task / E, row = task % E;
+        uint32_t first = c->start[e], last = c->start[e + 1];
+        if (first == last) continue;
+        const uint8_t *d = c->l->down + (e * E + row) * c->down_row;
+        if (last - first == 1) {
+            uint32_t slot = c->order[first];
+            c->down[slot * E + row] = gxo_dot_row(c->l->type_id, d, c->act + slot * F, F);
+            continue;
+        }
+        gxo_decode_row_fast(c->l->type_id, d, wbuf, F);
+        for (uint32_t i = first; i < last; ++i) {
+            uint32_t slot = c->order[i];
+            c->down[slot * E + row] = dot_dense(wbuf, c->act + slot * F, F);
+        }
+    }
+    free(wbuf);
+}
+
+/* src/engine.zig:520-642 */
+int gxo_moe_ffn(const gxo_layer *l, const float *x, size_t n, float *out,
+                uint32_t *ids, float *weights, int threads) {
+    if (!l || !x || !out || !ids || !weights || !g_codebook_ready) return -1;
+    const size_t E = l->n_embd, F = l->n_ff, U = l->n_used, NE = l->n_expert;
+    size_t gate_row = gxo_row_bytes(l->type_id, E), down_row = gxo_row_bytes(l->type_id, F);
+    if (l->type_id == 0 || !gate_row || !down_row || U == 0 || U > NE || NE > 512 || n == 0)
+        return -1;
+    float *router = malloc(sizeof(float) * n * NE);
+    float *xh = malloc(sizeof(float) * n * E);
+    float *act = malloc(sizeof(float) * n * U * F);
+    float *act_up = malloc(sizeof(float) * n * U * F);
+    float *down = malloc(sizeof(float) * n * U * E);
+    uint32_t *order = malloc(sizeof(uint32_t) * n * U);
+    if (!router || !xh || !act || !act_up || !down || !order) {
+        free(router); free(xh); free(act); free(act_up); free(down); free(order);
+        return -1;
+    }
+    uint32_t start[513];
+    ffn_ctx c = {l, x, xh, n, E, F, U, NE, gate_row, down_row, router, act, act_up, down, start, order};
+    /* Router, chunk as kernels.matmul picks it (pool.chunkFor(rows, 8)). */
+    size_t router_chunk = threads > 1 ? NE / ((size_t)threads * 4) : NE;
+    pool_run(threads, NE, router_chunk > 8 ? router_chunk : 8, router_range, &c);
+    /* Softmax, top-k, renormalisation, src/engine.zig:527-540. The optional bias is a
+     * harness hook (skewed expert popularity) with no reference counterpart. */
+    for (size_t t = 0; t < n; ++t) {
+        float *probs = router + t * NE;
+        if (l->router_bias) for (size_t e = 0; e < NE; ++e) probs[e] += l->router_bias[e];
+        gxo_softmax(probs, NE);
+        uint32_t *id = ids + t * U;
+        float *w = weights + t * U;
+        gxo_topk(probs, NE, id, w, U);
+        float sum = 0;
+        for (size_t j = 0; j < U; ++j) sum += w[j];
+        sum = sum > 6.103515625e-5f ? sum : 6.103515625e-5f;
+        for (size_t j = 0; j < U; ++j) {
+            w[j] /= sum;
+            if (l->expert_weights_scale != 0 && l->expert_weights_scale != 1) w[j] *= l->expert_weights_scale;
+        }
+    }
+    /* Rotated expert input shared by gate and up, src/engine.zig:547-551. */
+    memcpy(xh, x, sizeof(float) * n * E);
+    if (l->gate_signs) for (size_t t = 0; t < n; ++t) gxo_rotate_f32(xh + t * E, E, 128, l->gate_signs);
+    /* Counting sort of slots by expert, src/engine.zig:553-564. */
+    memset(out, 0, sizeof(float) * n * E);
+    memset(start, 0, sizeof(start));
+    for (size_t i = 0; i < n * U; ++i) start[ids[i] + 1] += 1;
+    for (size_t e = 0; e < NE; ++e) start[e + 1] += start[e];
+    uint32_t fill[513];
+    memcpy(fill, start, sizeof(fill));
+    for (size_t i = 0; i < n * U; ++i) order[fill[ids[i]]++] = (uint32_t)i;
+    /* Phase 1: gate/up, chunk 16, src/engine.zig:568. */
+    pool_run(threads, NE * F, 16, gate_up_range, &c);
+    /* SwiGLU and down-input rotation, src/engine.zig:603-607. */
+    for (size_t slot = 0; slot < n * U; ++slot) {
+        float *a = act + slot * F;
+        const float *up = act_up + slot * F;
+        for (size_t i = 0; i < F; ++i) a[i] = silu(a[i]) * up[i];
+        if (l->down_signs) gxo_rotate_f32(a, F, 128, l->down_signs);
+    }
+    /* Phase 2: down, chunk 64, src/engine.zig:609. */
+    pool_run(threads, NE * E, 64, down_range, &c);
+    /* Weighted sum, src/engine.zig:634-641. */
+    for (size_t t = 0; t < n; ++t) {
+        float *o = out + t * E;
+        for (size_t k = 0; k < U; ++k) {
+            size_t slot = t * U + k;
+            float wgt = weights[slot];
+            const float *v = down + slot * E;
+            for (size_t i = 0; i < E; ++i) o[i] += wgt * v[i];
+        }
+    }
+    free(router); free(xh); free(act); free(act_up); free(down); free(order);
+    return 0;
+}

@@ -1,0 +1,169 @@
+"""ctypes front end of the CPU oracle (oracle/gxo.c).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and bench.py's
+cpu_baseline / reference arm, always as the checker or the timed CPU baseline, never as the
+product. It restates the reference CPU engine of mattneel/gyro-dx (src/gyro.zig,
+src/kernels.zig, src/engine.zig:520-686); see gxo.h for the line-by-line mapping.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+ROOT = HERE.parent
+CODEBOOK = ROOT / "gyro-dx_b200" / "gyro_moe" / "data" / "gyro_codebook.f16"
+
+_F32P = ctypes.POINTER(ctypes.c_float)
+_U32P = ctypes.POINTER(ctypes.c_uint32)
+
+
+class _Layer(ctypes.Structure):
+    _fields_ = [
+        ("type_id", ctypes.c_uint32),
+        ("n_expert", ctypes.c_uint32),
+        ("n_embd", ctypes.c_uint32),
+        ("n_ff", ctypes.c_uint32),
+        ("n_used", ctypes.c_uint32),
+        ("expert_weights_scale", ctypes.c_float),
+        ("gate", ctypes.c_void_p),
+        ("up", ctypes.c_void_p),
+        ("down", ctypes.c_void_p),
+        ("router", ctypes.c_void_p),
+        ("gate_signs", ctypes.c_void_p),
+        ("down_signs", ctypes.c_void_p),
+        ("router_bias", ctypes.c_void_p),
+    ]
+
+
+def build(force: bool = False) -> None:
+    """Compiles liboracle.so / liboracle_fast.so (and oracle/_ref when the reference exists)."""
+    targets = ["all"]
+    if Path("/root/reference/third_party/agention-gyro/src/tq_ref.c").exists():
+        targets.append("ref")
+    cmd = ["make", "-s", "-C", str(HERE)] + (["-B"] if force else []) + targets
+    subprocess.run(cmd, check=True)
+
+
+_LIBS: dict[str, ctypes.CDLL] = {}
+
+
+def lib(fast: bool = False) -> ctypes.CDLL:
+    name = "liboracle_fast.so" if fast else "liboracle.so"
+    if name in _LIBS:
+        return _LIBS[name]
+    path = HERE / name
+    if not path.exists():
+        build()
+    L = ctypes.CDLL(str(path))
+    L.gxo_set_codebook.argtypes = [ctypes.c_void_p, ctypes.c_size_t]
+    L.gxo_type_info.argtypes = [ctypes.c_uint32] + [ctypes.POINTER(ctypes.c_int)] * 3
+    L.gxo_fp16_to_fp32.argtypes = [ctypes.c_uint16]
+    L.gxo_fp16_to_fp32.restype = ctypes.c_float
+    L.gxo_state.argtypes = [ctypes.c_uint32, ctypes.c_void_p, ctypes.c_int, ctypes.c_int]
+    L.gxo_state.restype = ctypes.c_uint32
+    L.gxo_decode_row.argtypes = [ctypes.c_uint32, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t,
+                                 _F32P, ctypes.c_size_t]
+    L.gxo_rotate.argtypes = [_F32P, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_void_p]
+    L.gxo_unrotate.argtypes = L.gxo_rotate.argtypes
+    L.gxo_rotate_f32.argtypes = [_F32P, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_void_p]
+    L.gxo_rotate_f32.restype = None
+    L.gxo_dot_row.argtypes = [ctypes.c_uint32, ctypes.c_void_p, _F32P, ctypes.c_size_t]
+    L.gxo_dot_row.restype = ctypes.c_float
+    L.gxo_softmax.argtypes = [_F32P, ctypes.c_size_t]
+    L.gxo_softmax.restype = None
+    L.gxo_topk.argtypes = [_F32P, ctypes.c_size_t, _U32P, _F32P, ctypes.c_size_t]
+    L.gxo_topk.restype = None
+    L.gxo_moe_ffn.argtypes = [ctypes.POINTER(_Layer), _F32P, ctypes.c_size_t, _F32P, _U32P, _F32P,
+                              ctypes.c_int]
+    L.gxo_max_threads.restype = ctypes.c_int
+    table = CODEBOOK.read_bytes()
+    if L.gxo_set_codebook(table, len(table)) != 0:
+        raise RuntimeError("oracle rejected the codebook")
+    _LIBS[name] = L
+    return L
+
+
+def _f32p(a: np.ndarray):
+    return a.ctypes.data_as(_F32P)
+
+
+def type_info(type_id: int):
+    k, s, b = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    if lib().gxo_type_info(type_id, ctypes.byref(k), ctypes.byref(s), ctypes.byref(b)) != 0:
+        raise ValueError(f"unknown Gyro type {type_id}")
+    return k.value, s.value, b.value
+
+
+def decode_row(type_id: int, packed: bytes | np.ndarray, n: int, state_bits: int = 15) -> np.ndarray:
+    """Strict decode (src/gyro.zig:81-105). Raises ValueError with the gyro.Error code."""
+    src = np.frombuffer(bytes(packed), dtype=np.uint8)
+    out = np.empty(n, dtype=np.float32)
+    rc = lib().gxo_decode_row(type_id, state_bits, src.ctypes.data, src.size, _f32p(out), n)
+    if rc != 0:
+        raise ValueError(rc)
+    return out
+
+
+def rotate(values: np.ndarray, block: int, signs: np.ndarray | None, inverse: bool = False) -> np.ndarray:
+    v = np.ascontiguousarray(values, dtype=np.float32).copy()
+    s = None if signs is None else np.ascontiguousarray(signs, dtype=np.int8)
+    fn = lib().gxo_unrotate if inverse else lib().gxo_rotate
+    rc = fn(_f32p(v), v.size, block, None if s is None else s.ctypes.data)
+    if rc != 0:
+        raise ValueError(rc)
+    return v
+
+
+def moe_ffn(layer: dict, x: np.ndarray, threads: int = 1, fast: bool = False):
+    """src/engine.zig:520-642 on f32 tokens x [n, E]; returns (out [n,E], ids [n,U], w [n,U])."""
+    L = lib(fast)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    n, E = x.shape
+    U = layer["n_used"]
+    keep = []
+
+    def ptr(a, dtype):
+        if a is None:
+            return None
+        a = np.ascontiguousarray(a, dtype=dtype)
+        keep.append(a)
+        return a.ctypes.data
+
+    desc = _Layer(layer["type_id"], layer["n_expert"], E, layer["n_ff"], U,
+                  layer.get("expert_weights_scale", 0.0),
+                  ptr(layer["gate"], np.uint8), ptr(layer["up"], np.uint8), ptr(layer["down"], np.uint8),
+                  ptr(layer["router"], np.float32), ptr(layer.get("gate_signs"), np.float32),
+                  ptr(layer.get("down_signs"), np.float32), ptr(layer.get("router_bias"), np.float32))
+    out = np.empty((n, E), dtype=np.float32)
+    ids = np.empty((n, U), dtype=np.uint32)
+    w = np.empty((n, U), dtype=np.float32)
+    rc = L.gxo_moe_ffn(ctypes.byref(desc), _f32p(x), n, _f32p(out), ids.ctypes.data_as(_U32P), _f32p(w), threads)
+    if rc != 0:
+        raise RuntimeError(f"gxo_moe_ffn failed ({rc})")
+    return out, ids, w
+
+
+def max_threads() -> int:
+    return int(lib(True).gxo_max_threads())
+
+
+def ref_lib() -> ctypes.CDLL | None:
+    """The reference's own C decoder compiled from its sources (oracle/_ref), if built."""
+    path = HERE / "_ref" / "libtq_ref.so"
+    if not path.exists():
+        return None
+    R = ctypes.CDLL(str(path))
+    R.tq_dequantize_row.argtypes = [ctypes.c_int, ctypes.c_void_p, _F32P, ctypes.c_int64]
+    R.tq_hadamard_rotate.argtypes = [_F32P, ctypes.c_int64, ctypes.c_int, ctypes.c_void_p]
+    R.tq_hadamard_unrotate.argtypes = R.tq_hadamard_rotate.argtypes
+    return R
+
+
+if __name__ == "__main__":
+    build(force=bool(os.environ.get("FORCE")))
+    print("oracle built; threads:", max_threads())
