@@ -1,0 +1,325 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 routed-MoE layer (Gyro trellis experts) through its C ABI.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload decode]
+
+Workload "decode" (default): a 40-layer stack of the config-0 routed
+layer (hidden 2048, 256 experts of gate/up [512x2048] and down [2048x512] TQ2_T, top-8,
+router f32 ~N(0, 0.02)), independent seeded weights per layer (8.56 GB of packed experts
+resident in HBM), batch-1 greedy decode: each step pushes one fresh bf16 token ~N(0,1) through
+all 40 layers with x_{l+1} = x_l + MoE_l(x_l) (residual stand-in for the hyper-connection mixer).
+A step touches 40 x 8 distinct experts = 267 MB of packed weights, more than the 126 MB L2, and
+consecutive steps route differently, so no step is served from L2.
+
+One JSON line on rank 0. value = tokens/s over the whole job (device-timed with CUDA events on
+the library's stream, max over ranks); e2e = the same through gx_stack_forward_host with host
+buffers; roofline = the gate/up decode GEMV (the dominant kernel), algorithmic bytes per launch
+over its event-timed duration in the final timed step; cpu_baseline = the CPU oracle (restated
+reference engine) on the host cores, on a bounded sample. With N > 1 GPUs each rank runs an
+independent replica on its own tokens ("replicas": decode does not exchange data).
+
+--impl reference times the reference's CPU engine (restated in oracle/, the reference's Zig code
+cannot be built here) on the same workload with all host threads; rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "gyro-dx_b200"))
+
+import numpy as np  # noqa: E402
+
+METRIC = "routed-MoE layer tok/s (decode & prefill) at 1/2/4/8 B200; HBM GB/s % peak"
+N_LAYERS = 40
+E, F, NE, U = 2048, 512, 256, 8
+TYPE_ID = 144
+EXPERT_BYTES = 835_584                        # gate + up + down of one TQ2_T expert
+GATE_UP_BYTES = 2 * 278_528
+ROUTER_BYTES = NE * E * 4
+LAYER_SEED = 1000
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=128)
+    p.add_argument("--warmup", type=int, default=8)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--workload", choices=["decode"], default="decode")
+    p.add_argument("--layers", type=int, default=N_LAYERS)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--cpu-seconds", type=float, default=15.0)
+    return p.parse_args()
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def make_layers(n_layers: int):
+    from gyro_moe import synth
+    for l in range(n_layers):
+        yield synth.make_layer(LAYER_SEED + l)
+
+
+def step_tokens(n_steps: int, n_tok: int, rank: int) -> np.ndarray:
+    from gyro_moe import synth
+    x = np.random.default_rng(7 + 1000 * rank).standard_normal((n_steps, n_tok, E)).astype(np.float32)
+    return synth.bf16_bits(x.reshape(-1, E)).reshape(n_steps, n_tok, E)
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=self.file, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        self.file.flush()
+        rows = [l.split(",") for l in Path(self.file.name).read_text().splitlines() if l.strip()]
+        os.unlink(self.file.name)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+                for name, v in zip(names, r[5:9]):
+                    if v.strip().lower() == "active":
+                        reasons.add(name)
+            except (ValueError, IndexError):
+                continue
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_baseline(layers, seconds: float) -> dict:
+    """The restated reference CPU engine (oracle/, fast build, all host threads) on a bounded
+    sample: whole tokens through the 40-layer stack until `seconds` have passed."""
+    from oracle import oracle
+    from gyro_moe import synth
+    threads = oracle.max_threads()
+    rng = np.random.default_rng(99)
+    done, t0 = 0, time.perf_counter()
+    while True:
+        x = synth.bf16_round(rng.standard_normal((1, E)).astype(np.float32))
+        for layer in layers:
+            out, _, _ = oracle.moe_ffn(layer, x, threads=threads, fast=True)
+            x = x + out
+        done += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or done >= 64:
+            break
+    return {"value": done / el, "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"{done} tokens x {len(layers)} layers, batch 1, {el:.1f} s on {threads} threads"}
+
+
+def run_reference(args):
+    """Reference arm: the CPU engine restated in oracle/ (the reference's own CPU engine is Zig,
+    which is absent), all host threads, each step one token through the 40-layer stack."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import oracle
+    from gyro_moe import synth
+    layers = list(make_layers(args.layers))
+    threads = oracle.max_threads()
+    xs = step_tokens(args.warmup + args.steps, 1, 0)
+    times = []
+    for i in range(args.warmup + args.steps):
+        x = (xs[i].astype(np.uint32) << 16).view(np.float32)
+        t0 = time.perf_counter()
+        for layer in layers:
+            out, _, _ = oracle.moe_ffn(layer, x, threads=threads, fast=True)
+            x = x + out
+        if i >= args.warmup:
+            times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = args.steps / total
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded; shapes of BASELINE.json config 1)",
+        "config": {"workload": "decode: 40-layer stack of the config-0 routed layer, batch 1",
+                   "layers": args.layers, "n_tok": 1, "hidden": E, "experts": NE, "top_k": U, "ffn": F,
+                   "type": "TQ2_T", "parallelism": "host threads"},
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
+                         "sample": f"{args.steps} steps x 1 token x {args.layers} layers (oracle/ restatement of "
+                                   "src/engine.zig:520-642; the reference's Zig engine cannot be built here)"},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    import torch
+    from gyro_moe import abi
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    n_tok = 1
+    K, W = args.steps, args.warmup
+
+    ctx = abi.Context(device=local, max_tokens=max(n_tok, 1), max_layers=args.layers, flags=abi.GX_FLAG_PROFILE)
+    keep_host = (rank == 0 and world == 1 and not args.no_cpu_baseline)
+    host_layers = []
+    for l, layer in enumerate(make_layers(args.layers)):
+        ctx.upload_layer(l, layer)
+        if keep_host:
+            host_layers.append(layer)
+    xs_host = step_tokens(W + K, n_tok, rank)
+    xs = torch.from_numpy(xs_host.view(np.int16)).to(dev).view(torch.bfloat16)
+    y = torch.empty((n_tok, E), dtype=torch.float32, device=dev)
+    stream = torch.cuda.ExternalStream(ctx.stream(), device=dev)
+
+    for i in range(W):
+        ctx.stack_forward(0, args.layers, xs[i], y)
+    torch.cuda.synchronize(dev)
+
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as clocks:
+        with torch.cuda.stream(stream):
+            start.record(stream)
+        for i in range(K):
+            ctx.stack_forward(0, args.layers, xs[W + i], y)
+        with torch.cuda.stream(stream):
+            end.record(stream)
+        end.synchronize()
+    torch.cuda.synchronize(dev)
+    if dist:
+        dist.barrier()
+    ms = start.elapsed_time(end)
+    t = ctx.timings()  # phase times of the final timed step (events inside the captured graph)
+    ms_t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if dist:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+
+    # End to end: host bf16 token in (pinned staging inside the library), host f32 out.
+    e2e_steps = min(K, 64)
+    torch.cuda.synchronize(dev)
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        ctx.stack_forward_host(0, args.layers, xs_host[W + i], out_dtype=np.float32)
+    e2e_s = time.perf_counter() - t0
+    e2e_t = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
+    if dist:
+        dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
+    e2e_s = float(e2e_t.item())
+
+    pk = peaks()
+    layers = max(t.layers, 1)
+    gate_up_s = t.gate_up_ns / layers * 1e-9
+    down_s = t.down_ns / layers * 1e-9
+    router_s = t.router_ns / layers * 1e-9
+    achieved = GATE_UP_BYTES * 8 / gate_up_s / 1e9 if gate_up_s > 0 else None
+    experts_gbs = EXPERT_BYTES * 8 / (gate_up_s + down_s) / 1e9 if gate_up_s > 0 else None
+    traffic = None
+    tfile = ROOT / "profiles" / "traffic.json"
+    if tfile.exists():
+        traffic = json.loads(tfile.read_text()).get("gate_up_kernel_decode_per_launch")
+    value = K * n_tok * world / (ms_max / 1e3)
+    line = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": ms_max / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (seeded; shapes and distributions of BASELINE.json config 1)",
+        "config": {"workload": "decode: 40-layer stack of the config-0 routed layer (BASELINE.json configs[1]), "
+                               "batch 1, fresh token per step",
+                   "layers": args.layers, "n_tok": n_tok, "hidden": E, "experts": NE, "top_k": U, "ffn": F,
+                   "type": "TQ2_T", "expert_bytes_resident": args.layers * NE * EXPERT_BYTES,
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "l2": "inputs larger than L2: each step reads 40 x 8 distinct experts (267 MB)"},
+        "roofline": {
+            "kernel": "gate_up_kernel (fused Gyro decode + gate/up GEMV + SwiGLU)",
+            "bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+            "frac": achieved / pk["hbm_gbs"] if achieved else None, "traffic": traffic,
+            "algorithmic_bytes_per_launch": GATE_UP_BYTES * 8,
+            "launch_us": gate_up_s * 1e6, "peak_source": f"{pk['source']} (MEASURED_PEAKS.json hbm_gbs, burst copy)",
+            "experts_phase_gbs": experts_gbs,
+            "experts_phase_frac": experts_gbs / pk["hbm_gbs"] if experts_gbs else None,
+            "per_layer_us": {"router": router_s * 1e6, "gate_up": gate_up_s * 1e6, "down": down_s * 1e6},
+            "layer_bytes": EXPERT_BYTES * 8 + ROUTER_BYTES,
+            "layer_gbs": (EXPERT_BYTES * 8 + ROUTER_BYTES) / (router_s + gate_up_s + down_s) / 1e9 if gate_up_s else None,
+        },
+        "e2e": {"value": e2e_steps * n_tok * world / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": n_tok * E * 2,
+                "d2h_bytes_per_step": n_tok * E * 4, "steps": e2e_steps,
+                "api": "gx_stack_forward_host (host bf16 in, host f32 out)"},
+        "gpu_launches": K * args.layers * 3,
+        "clocks": clocks.summary(),
+    }
+    if keep_host:
+        line["cpu_baseline"] = cpu_baseline(host_layers, args.cpu_seconds)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

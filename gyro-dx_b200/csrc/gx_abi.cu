@@ -1,0 +1,718 @@
+// gx_abi.cu — the C ABI of include/gyro_moe.h: context, HBM arena upload, forward calls,
+// tickets and timeouts. One CUDA stream per context; work is asynchronous and ordered.
+#include <cuda_runtime.h>
+
+#include <chrono>
+#include <cstring>
+#include <map>
+#include <thread>
+#include <tuple>
+#include <vector>
+
+#include "../../include/gyro_moe.h"
+#include "gx_internal.h"
+#include "gx_tile.h"
+
+namespace {
+
+constexpr int kEvents = 64;
+
+struct Layer {
+    bool ready = false;
+    uint32_t type = 0, n_expert = 0, local_experts = 0, first_expert = 0, E = 0, F = 0, U = 0;
+    float scale = 0.f;
+    uint8_t *arena = nullptr;
+    uint64_t bytes = 0;
+    uint8_t *gate = nullptr, *up = nullptr, *down = nullptr;
+    uint64_t gate_expert_bytes = 0, down_expert_bytes = 0;
+    float *router = nullptr, *bias = nullptr, *gate_signs = nullptr, *down_signs = nullptr;
+};
+
+struct Matrix {
+    uint32_t type = 0, rows = 0, cols = 0;
+    uint8_t *tiles = nullptr;
+};
+
+using GraphKey = std::tuple<uint32_t, uint32_t, uint32_t, uint32_t, uint32_t>;
+
+}  // namespace
+
+struct gx_context {
+    int device = 0;
+    uint32_t rank = 0, world = 1, max_tokens = 0, max_layers = 0, flags = 0;
+    int sm_count = 0;
+    cudaStream_t stream = nullptr;
+    uint32_t *codebook = nullptr;  // 2048 words = 4096 fp16
+    std::vector<Layer> layers;
+    std::vector<Matrix> mats;
+    // scratch sized for max_tokens
+    float *logits = nullptr, *weights = nullptr, *act = nullptr, *xbuf[2] = {nullptr, nullptr};
+    uint32_t *ids = nullptr;
+    unsigned *counter = nullptr;
+    int *err = nullptr;
+    void *x_stage = nullptr, *y_stage = nullptr;     // device staging (graphs, host calls)
+    void *h_in = nullptr, *h_out = nullptr;          // pinned host staging
+    size_t stage_bytes = 0;
+    cudaEvent_t events[kEvents] = {};
+    uint64_t submitted = 0;
+    std::vector<cudaEvent_t> prof;   // 4 per layer slot: start, router done, gate/up done, down done
+    uint32_t prof_layers = 0;        // layers recorded by the most recent forward call
+    std::map<GraphKey, std::pair<cudaGraph_t, cudaGraphExec_t>> graphs;
+    bool broken = false;
+};
+
+namespace {
+
+gx_result fail_cuda(gx_context *c, cudaError_t e) {
+    if (e == cudaSuccess) return GX_OK;
+    if (e == cudaErrorMemoryAllocation) {
+        cudaGetLastError();
+        return GX_E_OUTOFMEMORY;
+    }
+    if (e == cudaErrorInvalidValue) {
+        cudaGetLastError();
+        return GX_E_INVALIDARG;
+    }
+    if (c) c->broken = true;
+    return GX_E_DEVICE;
+}
+
+#define GX_CUDA(expr)                                  \
+    do {                                               \
+        cudaError_t gx_e_ = (expr);                    \
+        if (gx_e_ != cudaSuccess) return fail_cuda(c, gx_e_); \
+    } while (0)
+
+uint64_t align256(uint64_t v) { return (v + 255) & ~uint64_t(255); }
+
+bool known_type(uint32_t t) { return gx::type_k(t) != 0; }
+
+// Waits for an event with a wall-clock limit; checks the kernels' error word when done.
+gx_result wait_event(gx_context *c, cudaEvent_t ev, uint32_t timeout_ms) {
+    const auto start = std::chrono::steady_clock::now();
+    for (;;) {
+        cudaError_t q = cudaEventQuery(ev);
+        if (q == cudaSuccess) break;
+        if (q != cudaErrorNotReady) return fail_cuda(c, q);
+        const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - start).count();
+        if ((uint64_t)ms >= timeout_ms) return GX_E_TIMEOUT;
+        std::this_thread::sleep_for(std::chrono::microseconds(20));
+    }
+    int err = 0;
+    cudaError_t e = cudaMemcpy(&err, c->err, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return fail_cuda(c, e);
+    if (err != 0) {
+        cudaMemset(c->err, 0, sizeof(int));
+        return GX_E_KERNEL;
+    }
+    return GX_OK;
+}
+
+gx_result record_ticket(gx_context *c, uint64_t *out_ticket) {
+    const uint64_t t = ++c->submitted;
+    GX_CUDA(cudaEventRecord(c->events[t % kEvents], c->stream));
+    if (out_ticket) *out_ticket = t;
+    return GX_OK;
+}
+
+gx_result sync_all(gx_context *c, uint32_t timeout_ms) {
+    uint64_t t = 0;
+    gx_result r = record_ticket(c, &t);
+    if (r != GX_OK) return r;
+    return wait_event(c, c->events[t % kEvents], timeout_ms);
+}
+
+gx_result ensure_scratch(gx_context *c) {
+    const size_t T = c->max_tokens ? c->max_tokens : 1;
+    // Sized for the largest shapes the ABI accepts: E <= 4096, F <= 1024, NE <= 512, U <= 16.
+    const size_t E = 4096, F = 1024, NE = 512, U = 16;
+    GX_CUDA(cudaMalloc(&c->logits, T * NE * sizeof(float)));
+    GX_CUDA(cudaMalloc(&c->weights, T * U * sizeof(float)));
+    GX_CUDA(cudaMalloc(&c->ids, T * U * sizeof(uint32_t)));
+    GX_CUDA(cudaMalloc(&c->act, T * U * F * sizeof(float)));
+    GX_CUDA(cudaMalloc(&c->xbuf[0], T * E * sizeof(float)));
+    GX_CUDA(cudaMalloc(&c->xbuf[1], T * E * sizeof(float)));
+    c->stage_bytes = T * E * sizeof(float);
+    GX_CUDA(cudaMalloc(&c->x_stage, c->stage_bytes));
+    GX_CUDA(cudaMalloc(&c->y_stage, c->stage_bytes));
+    GX_CUDA(cudaMallocHost(&c->h_in, c->stage_bytes));
+    GX_CUDA(cudaMallocHost(&c->h_out, c->stage_bytes + T * U * 8));
+    GX_CUDA(cudaMalloc(&c->counter, sizeof(unsigned)));
+    GX_CUDA(cudaMemset(c->counter, 0, sizeof(unsigned)));
+    GX_CUDA(cudaMalloc(&c->err, sizeof(int)));
+    GX_CUDA(cudaMemset(c->err, 0, sizeof(int)));
+    return GX_OK;
+}
+
+void release_all(gx_context *c) {
+    for (auto &kv : c->graphs) {
+        if (kv.second.second) cudaGraphExecDestroy(kv.second.second);
+        if (kv.second.first) cudaGraphDestroy(kv.second.first);
+    }
+    c->graphs.clear();
+    for (auto &l : c->layers) if (l.arena) cudaFree(l.arena);
+    for (auto &m : c->mats) if (m.tiles) cudaFree(m.tiles);
+    void *dev[] = {c->codebook, c->logits, c->weights, c->ids, c->act, c->xbuf[0], c->xbuf[1],
+                   c->x_stage, c->y_stage, c->counter, c->err};
+    for (void *p : dev) if (p) cudaFree(p);
+    if (c->h_in) cudaFreeHost(c->h_in);
+    if (c->h_out) cudaFreeHost(c->h_out);
+    for (auto &e : c->events) if (e) cudaEventDestroy(e);
+    for (auto &e : c->prof) if (e) cudaEventDestroy(e);
+    c->prof.clear();
+    if (c->stream) cudaStreamDestroy(c->stream);
+}
+
+size_t dtype_size(uint32_t dt) { return dt == GX_BF16 ? 2 : 4; }
+
+// One routed layer: router + top-k, gate/up + SwiGLU, down + combine (+ residual).
+// prof_slot >= 0 records the phase events of layer slot prof_slot (GX_FLAG_PROFILE).
+gx_result enqueue_layer(gx_context *c, const Layer &L, const void *x, uint32_t x_dtype, uint32_t n_tok,
+                        const void *resid, uint32_t resid_dtype, void *out, uint32_t out_dtype, int prof_slot) {
+    cudaEvent_t *ev = prof_slot >= 0 ? &c->prof[4 * (size_t)prof_slot] : nullptr;
+    if (ev) GX_CUDA(cudaEventRecord(ev[0], c->stream));
+    gx::RouterArgs ra{};
+    ra.W = L.router;
+    ra.bias = L.bias;
+    ra.x = x;
+    ra.x_bf16 = x_dtype == GX_BF16;
+    ra.n_tok = (int)n_tok;
+    ra.NE = (int)L.n_expert;
+    ra.E = (int)L.E;
+    ra.U = (int)L.U;
+    ra.scale = L.scale;
+    ra.logits = c->logits;
+    ra.ids = c->ids;
+    ra.weights = c->weights;
+    ra.counter = c->counter;
+    ra.err = c->err;
+    GX_CUDA(gx::launch_router(ra, c->stream));
+    if (ev) GX_CUDA(cudaEventRecord(ev[1], c->stream));
+
+    gx::GateUpArgs ga{};
+    ga.type = L.type;
+    ga.gate = L.gate;
+    ga.up = L.up;
+    ga.expert_bytes = L.gate_expert_bytes;
+    ga.x = x;
+    ga.x_bf16 = x_dtype == GX_BF16;
+    ga.signs = L.gate_signs;
+    ga.ids = c->ids;
+    ga.act = c->act;
+    ga.codebook = c->codebook;
+    ga.E = (int)L.E;
+    ga.F = (int)L.F;
+    ga.U = (int)L.U;
+    ga.n_slots = (int)(n_tok * L.U);
+    ga.n_expert = (int)L.local_experts;
+    ga.err = c->err;
+    GX_CUDA(gx::launch_gate_up(ga, c->sm_count, c->stream));
+    if (ev) GX_CUDA(cudaEventRecord(ev[2], c->stream));
+
+    gx::DownArgs da{};
+    da.type = L.type;
+    da.down = L.down;
+    da.expert_bytes = L.down_expert_bytes;
+    da.act = c->act;
+    da.signs = L.down_signs;
+    da.ids = c->ids;
+    da.weights = c->weights;
+    da.resid = resid;
+    da.resid_bf16 = resid_dtype == GX_BF16;
+    da.out = out;
+    da.out_bf16 = out_dtype == GX_BF16;
+    da.codebook = c->codebook;
+    da.E = (int)L.E;
+    da.F = (int)L.F;
+    da.U = (int)L.U;
+    da.n_tok = (int)n_tok;
+    da.n_expert = (int)L.local_experts;
+    da.err = c->err;
+    GX_CUDA(gx::launch_down(da, c->sm_count, c->stream));
+    if (ev) GX_CUDA(cudaEventRecord(ev[3], c->stream));
+    return GX_OK;
+}
+
+gx_result check_forward(gx_context *c, uint32_t layer, uint32_t x_dtype, uint32_t n_tok, uint32_t y_dtype) {
+    if (!c) return GX_E_INVALIDARG;
+    if (c->broken) return GX_E_DEVICE;
+    if (layer >= c->layers.size() || !c->layers[layer].ready) return GX_E_STATE;
+    if ((x_dtype != GX_F32 && x_dtype != GX_BF16) || (y_dtype != GX_F32 && y_dtype != GX_BF16)) return GX_E_INVALIDARG;
+    if (n_tok > c->max_tokens) return GX_E_INVALIDARG;
+    return GX_OK;
+}
+
+gx_result stack_enqueue(gx_context *c, uint32_t first, uint32_t n_layers, const void *x, uint32_t x_dtype,
+                        uint32_t n_tok, void *y, uint32_t y_dtype) {
+    const void *cur = x;
+    uint32_t cur_dtype = x_dtype;
+    if (c->flags & GX_FLAG_PROFILE) c->prof_layers = n_layers;
+    for (uint32_t i = 0; i < n_layers; ++i) {
+        const Layer &L = c->layers[first + i];
+        const bool last = i + 1 == n_layers;
+        void *out = last ? y : c->xbuf[i & 1];
+        const uint32_t out_dtype = last ? y_dtype : GX_F32;
+        const int slot = (c->flags & GX_FLAG_PROFILE) ? (int)i : -1;
+        gx_result r = enqueue_layer(c, L, cur, cur_dtype, n_tok, cur, cur_dtype, out, out_dtype, slot);
+        if (r != GX_OK) return r;
+        cur = out;
+        cur_dtype = out_dtype;
+    }
+    return GX_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+GX_API gx_result gx_create(const gx_options *o, gx_context **out) {
+    if (!o || !out || !o->codebook || o->codebook_bytes != 8192 || o->world == 0 || o->rank >= o->world ||
+        o->max_tokens == 0 || o->max_layers == 0 || o->max_tokens > (1u << 20))
+        return GX_E_INVALIDARG;
+    if (o->world > 1) return GX_E_UNSUPPORTED;
+    *out = nullptr;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || (int)o->device >= n) return GX_E_INVALIDARG;
+    cudaDeviceProp prop{};
+    if (cudaGetDeviceProperties(&prop, (int)o->device) != cudaSuccess) return GX_E_DEVICE;
+    if (prop.major != 10) return GX_E_UNSUPPORTED;
+    gx_context *c = new (std::nothrow) gx_context();
+    if (!c) return GX_E_OUTOFMEMORY;
+    c->device = (int)o->device;
+    c->rank = o->rank;
+    c->world = o->world;
+    c->max_tokens = o->max_tokens;
+    c->max_layers = o->max_layers;
+    c->flags = o->flags;
+    c->sm_count = prop.multiProcessorCount;
+    c->layers.resize(o->max_layers);
+    gx_result r = GX_OK;
+    do {
+        if (cudaSetDevice(c->device) != cudaSuccess) { r = GX_E_DEVICE; break; }
+        if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) { r = GX_E_DEVICE; break; }
+        bool ok = true;
+        for (auto &e : c->events) ok = ok && cudaEventCreateWithFlags(&e, cudaEventDisableTiming) == cudaSuccess;
+        c->prof.assign(4 * (size_t)c->max_layers, nullptr);
+        for (auto &e : c->prof) ok = ok && cudaEventCreate(&e) == cudaSuccess;
+        if (!ok) { r = GX_E_DEVICE; break; }
+        if (cudaMalloc(&c->codebook, 8192) != cudaSuccess) { r = GX_E_OUTOFMEMORY; break; }
+        if (cudaMemcpy(c->codebook, o->codebook, 8192, cudaMemcpyHostToDevice) != cudaSuccess) { r = GX_E_DEVICE; break; }
+        r = ensure_scratch(c);
+    } while (false);
+    if (r != GX_OK) {
+        release_all(c);
+        delete c;
+        return r;
+    }
+    *out = c;
+    return GX_OK;
+}
+
+GX_API gx_result gx_get_caps(gx_context *c, gx_caps *caps) {
+    if (!c || !caps) return GX_E_INVALIDARG;
+    std::memset(caps, 0, sizeof(*caps));
+    cudaDeviceProp prop{};
+    GX_CUDA(cudaGetDeviceProperties(&prop, c->device));
+    size_t free_b = 0, total_b = 0;
+    GX_CUDA(cudaSetDevice(c->device));
+    GX_CUDA(cudaMemGetInfo(&free_b, &total_b));
+    caps->abi_version = GX_ABI_VERSION;
+    caps->sm_count = (uint32_t)prop.multiProcessorCount;
+    caps->cc_major = (uint32_t)prop.major;
+    caps->cc_minor = (uint32_t)prop.minor;
+    caps->rank = c->rank;
+    caps->world = c->world;
+    caps->max_tokens = c->max_tokens;
+    caps->max_layers = c->max_layers;
+    caps->hbm_bytes = total_b;
+    caps->free_bytes = free_b;
+    caps->l2_bytes = (uint64_t)prop.l2CacheSize;
+    for (auto &l : c->layers) caps->arena_bytes += l.bytes;
+    for (auto &m : c->mats) caps->arena_bytes += (uint64_t)m.rows / 8 * (m.cols / 128) * gx::tile_bytes(m.type);
+    std::strncpy(caps->device_name, prop.name, sizeof(caps->device_name) - 1);
+    return GX_OK;
+}
+
+GX_API gx_result gx_upload_layer(gx_context *c, uint32_t layer, const gx_layer_desc *d, uint32_t timeout_ms) {
+    if (!c || !d) return GX_E_INVALIDARG;
+    if (c->broken) return GX_E_DEVICE;
+    if (layer >= c->layers.size()) return GX_E_INVALIDARG;
+    if (!known_type(d->type_id) || d->n_expert == 0 || d->n_expert > 512 || d->n_embd == 0 || d->n_embd % 128 ||
+        d->n_embd > 4096 || d->n_ff == 0 || d->n_ff % 128 || d->n_ff > 1024 || d->n_used == 0 || d->n_used > 16 ||
+        d->n_used > d->n_expert || !d->gate || !d->up || !d->down || !d->router)
+        return GX_E_INVALIDARG;
+    if (d->n_used * (d->n_ff / 128) > 64) return GX_E_UNSUPPORTED;
+    if (d->n_expert % c->world) return GX_E_INVALIDARG;
+    const uint64_t bb = (uint64_t)gx::type_block_bytes(d->type_id);
+    const uint64_t E = d->n_embd, F = d->n_ff, NE = d->n_expert;
+    const uint64_t gate_row = E / 128 * bb, down_row = F / 128 * bb;
+    if (d->gate_bytes != NE * F * gate_row || d->up_bytes != NE * F * gate_row || d->down_bytes != NE * E * down_row)
+        return GX_E_INVALIDARG;
+    if (d->up_signs && (!d->gate_signs || std::memcmp(d->up_signs, d->gate_signs, E * sizeof(float)) != 0))
+        return GX_E_INVALIDARG;  // gate and up share one rotated input (src/gpu_engine.zig:404)
+    if (d->up_signs == nullptr && d->gate_signs != nullptr) return GX_E_INVALIDARG;
+    const float *signs[2] = {d->gate_signs, d->down_signs};
+    const uint64_t widths[2] = {E, F};
+    for (int s = 0; s < 2; ++s)
+        if (signs[s])
+            for (uint64_t i = 0; i < widths[s]; ++i)
+                if (signs[s][i] != 1.0f && signs[s][i] != -1.0f) return GX_E_INVALIDARG;
+
+    GX_CUDA(cudaSetDevice(c->device));
+    Layer &L = c->layers[layer];
+    if (L.arena) {
+        gx_result r = sync_all(c, timeout_ms);
+        if (r != GX_OK) return r;
+        cudaFree(L.arena);
+        L = Layer{};
+    }
+    const uint64_t NEl = NE / c->world, first = c->rank * NEl;
+    const uint64_t gate_local = NEl * F * gate_row, down_local = NEl * E * down_row;
+    uint64_t off = 0;
+    const uint64_t o_gate = off; off = align256(off + gate_local);
+    const uint64_t o_up = off; off = align256(off + gate_local);
+    const uint64_t o_down = off; off = align256(off + down_local);
+    const uint64_t o_router = off; off = align256(off + NE * E * 4);
+    const uint64_t o_bias = off; off = align256(off + NE * 4);
+    const uint64_t o_gs = off; off = align256(off + E * 4);
+    const uint64_t o_ds = off; off = align256(off + F * 4);
+    uint8_t *arena = nullptr;
+    GX_CUDA(cudaMalloc(&arena, off));
+    uint8_t *raw = nullptr;
+    cudaError_t e = cudaMalloc(&raw, gate_local > down_local ? gate_local : down_local);
+    if (e != cudaSuccess) {
+        cudaFree(arena);
+        return fail_cuda(c, e);
+    }
+    struct Part { const void *src; uint64_t row_bytes, rows, cols, dst; };
+    const Part parts[3] = {
+        {static_cast<const uint8_t *>(d->gate) + first * F * gate_row, gate_row, NEl * F, E, o_gate},
+        {static_cast<const uint8_t *>(d->up) + first * F * gate_row, gate_row, NEl * F, E, o_up},
+        {static_cast<const uint8_t *>(d->down) + first * E * down_row, down_row, NEl * E, F, o_down},
+    };
+    for (const Part &p : parts) {
+        if (e == cudaSuccess) e = cudaMemcpyAsync(raw, p.src, p.rows * p.row_bytes, cudaMemcpyHostToDevice, c->stream);
+        if (e == cudaSuccess)
+            e = gx::launch_repack(d->type_id, raw, p.row_bytes, (uint32_t)p.rows, (uint32_t)p.cols, arena + p.dst, c->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    }
+    if (e == cudaSuccess) e = cudaMemcpyAsync(arena + o_router, d->router, NE * E * 4, cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess) {
+        if (d->router_bias) e = cudaMemcpyAsync(arena + o_bias, d->router_bias, NE * 4, cudaMemcpyHostToDevice, c->stream);
+        else e = cudaMemsetAsync(arena + o_bias, 0, NE * 4, c->stream);
+    }
+    if (e == cudaSuccess && d->gate_signs)
+        e = cudaMemcpyAsync(arena + o_gs, d->gate_signs, E * 4, cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess && d->down_signs)
+        e = cudaMemcpyAsync(arena + o_ds, d->down_signs, F * 4, cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    cudaFree(raw);
+    if (e != cudaSuccess) {
+        cudaFree(arena);
+        return fail_cuda(c, e);
+    }
+    L.ready = true;
+    L.type = d->type_id;
+    L.n_expert = (uint32_t)NE;
+    L.local_experts = (uint32_t)NEl;
+    L.first_expert = (uint32_t)first;
+    L.E = (uint32_t)E;
+    L.F = (uint32_t)F;
+    L.U = d->n_used;
+    L.scale = d->expert_weights_scale;
+    L.arena = arena;
+    L.bytes = off;
+    L.gate = arena + o_gate;
+    L.up = arena + o_up;
+    L.down = arena + o_down;
+    L.gate_expert_bytes = F * gate_row;
+    L.down_expert_bytes = E * down_row;
+    L.router = reinterpret_cast<float *>(arena + o_router);
+    L.bias = reinterpret_cast<float *>(arena + o_bias);
+    L.gate_signs = d->gate_signs ? reinterpret_cast<float *>(arena + o_gs) : nullptr;
+    L.down_signs = d->down_signs ? reinterpret_cast<float *>(arena + o_ds) : nullptr;
+    // A re-uploaded layer invalidates captured stacks.
+    for (auto &kv : c->graphs) {
+        cudaGraphExecDestroy(kv.second.second);
+        cudaGraphDestroy(kv.second.first);
+    }
+    c->graphs.clear();
+    return GX_OK;
+}
+
+GX_API gx_result gx_moe_forward(gx_context *c, uint32_t layer, const void *x, uint32_t x_dtype, uint32_t n_tok,
+                                void *y, uint32_t y_dtype, uint32_t *ids, float *weights, uint64_t *out_ticket) {
+    gx_result r = check_forward(c, layer, x_dtype, n_tok, y_dtype);
+    if (r != GX_OK) return r;
+    if (n_tok > 0 && (!x || !y)) return GX_E_INVALIDARG;
+    // Vector loads need 16-byte aligned activations; outputs are written as 4-byte words.
+    if (((uintptr_t)x & 15) || ((uintptr_t)y & 3) || ((uintptr_t)ids & 3) || ((uintptr_t)weights & 3))
+        return GX_E_INVALIDARG;
+    GX_CUDA(cudaSetDevice(c->device));
+    const Layer &L = c->layers[layer];
+    if (n_tok > 0) {
+        const bool prof = (c->flags & GX_FLAG_PROFILE) != 0;
+        if (prof) c->prof_layers = 1;
+        r = enqueue_layer(c, L, x, x_dtype, n_tok, nullptr, GX_F32, y, y_dtype, prof ? 0 : -1);
+        if (r != GX_OK) return r;
+        if (ids) GX_CUDA(cudaMemcpyAsync(ids, c->ids, (size_t)n_tok * L.U * 4, cudaMemcpyDeviceToDevice, c->stream));
+        if (weights)
+            GX_CUDA(cudaMemcpyAsync(weights, c->weights, (size_t)n_tok * L.U * 4, cudaMemcpyDeviceToDevice, c->stream));
+    }
+    return record_ticket(c, out_ticket);
+}
+
+GX_API gx_result gx_moe_forward_host(gx_context *c, uint32_t layer, const void *x, uint32_t x_dtype, uint32_t n_tok,
+                                     void *y, uint32_t y_dtype, uint32_t *ids, float *weights, uint32_t timeout_ms) {
+    gx_result r = check_forward(c, layer, x_dtype, n_tok, y_dtype);
+    if (r != GX_OK) return r;
+    if (n_tok == 0) return GX_OK;
+    if (!x || !y) return GX_E_INVALIDARG;
+    GX_CUDA(cudaSetDevice(c->device));
+    const Layer &L = c->layers[layer];
+    const size_t in_b = (size_t)n_tok * L.E * dtype_size(x_dtype), out_b = (size_t)n_tok * L.E * dtype_size(y_dtype);
+    std::memcpy(c->h_in, x, in_b);
+    GX_CUDA(cudaMemcpyAsync(c->x_stage, c->h_in, in_b, cudaMemcpyHostToDevice, c->stream));
+    const bool prof = (c->flags & GX_FLAG_PROFILE) != 0;
+    if (prof) c->prof_layers = 1;
+    r = enqueue_layer(c, L, c->x_stage, x_dtype, n_tok, nullptr, GX_F32, c->y_stage, y_dtype, prof ? 0 : -1);
+    if (r != GX_OK) return r;
+    uint8_t *ho = static_cast<uint8_t *>(c->h_out);
+    const size_t sel_b = (size_t)n_tok * L.U * 4;
+    GX_CUDA(cudaMemcpyAsync(ho, c->y_stage, out_b, cudaMemcpyDeviceToHost, c->stream));
+    if (ids) GX_CUDA(cudaMemcpyAsync(ho + c->stage_bytes, c->ids, sel_b, cudaMemcpyDeviceToHost, c->stream));
+    if (weights) GX_CUDA(cudaMemcpyAsync(ho + c->stage_bytes + sel_b, c->weights, sel_b, cudaMemcpyDeviceToHost, c->stream));
+    r = sync_all(c, timeout_ms);
+    if (r != GX_OK) return r;
+    std::memcpy(y, ho, out_b);
+    if (ids) std::memcpy(ids, ho + c->stage_bytes, sel_b);
+    if (weights) std::memcpy(weights, ho + c->stage_bytes + sel_b, sel_b);
+    return GX_OK;
+}
+
+GX_API gx_result gx_stack_forward(gx_context *c, uint32_t first, uint32_t n_layers, const void *x, uint32_t x_dtype,
+                                  uint32_t n_tok, void *y, uint32_t y_dtype, uint64_t *out_ticket) {
+    if (!c || n_layers == 0 || (uint64_t)first + n_layers > c->layers.size()) return GX_E_INVALIDARG;
+    for (uint32_t i = 0; i < n_layers; ++i) {
+        gx_result r = check_forward(c, first + i, x_dtype, n_tok, y_dtype);
+        if (r != GX_OK) return r;
+        if (c->layers[first + i].E != c->layers[first].E) return GX_E_INVALIDARG;
+    }
+    if (n_tok == 0) return record_ticket(c, out_ticket);
+    if (!x || !y || ((uintptr_t)y & 3)) return GX_E_INVALIDARG;
+    GX_CUDA(cudaSetDevice(c->device));
+    const size_t E = c->layers[first].E;
+    const size_t in_b = n_tok * E * dtype_size(x_dtype), out_b = n_tok * E * dtype_size(y_dtype);
+    // The graph reads x_stage and writes y_stage; the caller's buffers are copied around it.
+    GX_CUDA(cudaMemcpyAsync(c->x_stage, x, in_b, cudaMemcpyDeviceToDevice, c->stream));
+    const GraphKey key{first, n_layers, n_tok, x_dtype, y_dtype};
+    auto it = c->graphs.find(key);
+    if (it == c->graphs.end()) {
+        // First call runs eagerly (sets kernel attributes), then the chain is captured.
+        gx_result r = stack_enqueue(c, first, n_layers, c->x_stage, x_dtype, n_tok, c->y_stage, y_dtype);
+        if (r != GX_OK) return r;
+        cudaGraph_t g = nullptr;
+        cudaGraphExec_t ge = nullptr;
+        GX_CUDA(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+        r = stack_enqueue(c, first, n_layers, c->x_stage, x_dtype, n_tok, c->y_stage, y_dtype);
+        cudaError_t e = cudaStreamEndCapture(c->stream, &g);
+        if (r != GX_OK) {
+            if (g) cudaGraphDestroy(g);
+            return r;
+        }
+        GX_CUDA(e);
+        e = cudaGraphInstantiate(&ge, g, 0);
+        if (e != cudaSuccess) {
+            cudaGraphDestroy(g);
+            return fail_cuda(c, e);
+        }
+        c->graphs[key] = {g, ge};
+    } else {
+        GX_CUDA(cudaGraphLaunch(it->second.second, c->stream));
+    }
+    GX_CUDA(cudaMemcpyAsync(y, c->y_stage, out_b, cudaMemcpyDeviceToDevice, c->stream));
+    return record_ticket(c, out_ticket);
+}
+
+GX_API gx_result gx_stack_forward_host(gx_context *c, uint32_t first, uint32_t n_layers, const void *x,
+                                       uint32_t x_dtype, uint32_t n_tok, void *y, uint32_t y_dtype,
+                                       uint32_t timeout_ms) {
+    if (!c || n_layers == 0 || (uint64_t)first + n_layers > c->layers.size()) return GX_E_INVALIDARG;
+    if (n_tok == 0) return GX_OK;
+    if (!x || !y || n_tok > c->max_tokens) return GX_E_INVALIDARG;
+    if (!c->layers[first].ready) return GX_E_STATE;
+    const size_t E = c->layers[first].E;
+    const size_t in_b = n_tok * E * dtype_size(x_dtype), out_b = n_tok * E * dtype_size(y_dtype);
+    std::memcpy(c->h_in, x, in_b);
+    GX_CUDA(cudaSetDevice(c->device));
+    GX_CUDA(cudaMemcpyAsync(c->xbuf[0], c->h_in, in_b, cudaMemcpyHostToDevice, c->stream));
+    // xbuf[0] holds the input only until the stack's staging copy has read it.
+    gx_result r = gx_stack_forward(c, first, n_layers, c->xbuf[0], x_dtype, n_tok, c->y_stage, y_dtype, nullptr);
+    if (r != GX_OK) return r;
+    GX_CUDA(cudaMemcpyAsync(c->h_out, c->y_stage, out_b, cudaMemcpyDeviceToHost, c->stream));
+    r = sync_all(c, timeout_ms);
+    if (r != GX_OK) return r;
+    std::memcpy(y, c->h_out, out_b);
+    return GX_OK;
+}
+
+GX_API gx_result gx_wait(gx_context *c, uint64_t ticket, uint32_t timeout_ms) {
+    if (!c) return GX_E_INVALIDARG;
+    if (ticket > c->submitted) return GX_E_INVALIDARG;
+    if (ticket == 0) return GX_OK;
+    GX_CUDA(cudaSetDevice(c->device));
+    return wait_event(c, c->events[ticket % kEvents], timeout_ms);
+}
+
+GX_API gx_result gx_poll(gx_context *c, uint64_t *out_completed) {
+    if (!c || !out_completed) return GX_E_INVALIDARG;
+    uint64_t done = c->submitted > kEvents ? c->submitted - kEvents : 0;
+    for (uint64_t t = c->submitted; t > done; --t) {
+        cudaError_t q = cudaEventQuery(c->events[t % kEvents]);
+        if (q == cudaSuccess) {
+            done = t;
+            break;
+        }
+        if (q != cudaErrorNotReady) return fail_cuda(c, q);
+    }
+    *out_completed = done;
+    return GX_OK;
+}
+
+GX_API gx_result gx_get_stream(gx_context *c, void **out_stream) {
+    if (!c || !out_stream) return GX_E_INVALIDARG;
+    *out_stream = c->stream;
+    return GX_OK;
+}
+
+GX_API gx_result gx_decode_blocks(gx_context *c, uint32_t type_id, const void *packed, uint64_t packed_bytes,
+                                  float *out, uint32_t value_count, const float *expected, float *max_abs_error,
+                                  uint32_t timeout_ms) {
+    // Argument rules of gd_validate_gyro (native/gyro_native.cpp:597-607).
+    if (!c || !packed || !out || !known_type(type_id) || value_count == 0 || value_count % 128 ||
+        value_count > 16777216u)
+        return GX_E_INVALIDARG;
+    const uint32_t blocks = value_count / 128;
+    if (packed_bytes != (uint64_t)blocks * gx::type_block_bytes(type_id)) return GX_E_INVALIDARG;
+    if (c->broken) return GX_E_DEVICE;
+    GX_CUDA(cudaSetDevice(c->device));
+    uint8_t *din = nullptr;
+    float *dout = nullptr;
+    GX_CUDA(cudaMalloc(&din, packed_bytes));
+    cudaError_t e = cudaMalloc(&dout, (size_t)value_count * 4);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(din, packed, packed_bytes, cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess)
+        e = gx::launch_decode_blocks(type_id, din, blocks, reinterpret_cast<const uint16_t *>(c->codebook), dout, c->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(out, dout, (size_t)value_count * 4, cudaMemcpyDeviceToHost, c->stream);
+    gx_result r = e == cudaSuccess ? sync_all(c, timeout_ms) : fail_cuda(c, e);
+    if (r != GX_E_TIMEOUT) {
+        cudaFree(din);
+        cudaFree(dout);
+    }
+    if (r != GX_OK) return r;
+    if (expected) {
+        float worst = 0.f;
+        bool same = true;
+        for (uint32_t i = 0; i < value_count; ++i) {
+            uint32_t a, b;
+            std::memcpy(&a, &out[i], 4);
+            std::memcpy(&b, &expected[i], 4);
+            if (a != b) {
+                same = false;
+                const float diff = out[i] > expected[i] ? out[i] - expected[i] : expected[i] - out[i];
+                if (!(diff <= worst)) worst = diff;
+            }
+        }
+        if (max_abs_error) *max_abs_error = worst;
+        if (!same) return GX_E_MISMATCH;
+    } else if (max_abs_error) {
+        *max_abs_error = 0.f;
+    }
+    return GX_OK;
+}
+
+GX_API gx_result gx_upload_matrix(gx_context *c, uint32_t type_id, uint32_t rows, uint32_t cols, const void *packed,
+                                  uint64_t packed_bytes, uint32_t *out_handle, uint32_t timeout_ms) {
+    if (!c || !packed || !out_handle || !known_type(type_id) || rows == 0 || rows % 8 || cols == 0 || cols % 128 ||
+        cols > 2048)
+        return GX_E_INVALIDARG;
+    const uint64_t row_bytes = (uint64_t)cols / 128 * gx::type_block_bytes(type_id);
+    if (packed_bytes != row_bytes * rows) return GX_E_INVALIDARG;
+    if (c->broken) return GX_E_DEVICE;
+    GX_CUDA(cudaSetDevice(c->device));
+    uint8_t *raw = nullptr, *tiles = nullptr;
+    GX_CUDA(cudaMalloc(&tiles, packed_bytes));
+    cudaError_t e = cudaMalloc(&raw, packed_bytes);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(raw, packed, packed_bytes, cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess) e = gx::launch_repack(type_id, raw, row_bytes, rows, cols, tiles, c->stream);
+    gx_result r = e == cudaSuccess ? sync_all(c, timeout_ms) : fail_cuda(c, e);
+    if (r != GX_E_TIMEOUT) cudaFree(raw);
+    if (r != GX_OK) {
+        if (r != GX_E_TIMEOUT) cudaFree(tiles);
+        return r;
+    }
+    Matrix m;
+    m.type = type_id;
+    m.rows = rows;
+    m.cols = cols;
+    m.tiles = tiles;
+    c->mats.push_back(m);
+    *out_handle = (uint32_t)(c->mats.size() - 1);
+    return GX_OK;
+}
+
+GX_API gx_result gx_matvec(gx_context *c, uint32_t handle, const float *x, uint32_t n_tok, float *y,
+                           uint64_t *out_ticket) {
+    if (!c || handle >= c->mats.size() || (n_tok && (!x || !y)) || n_tok > 64) return GX_E_INVALIDARG;
+    if (((uintptr_t)x & 15) || ((uintptr_t)y & 3)) return GX_E_INVALIDARG;
+    if (c->broken) return GX_E_DEVICE;
+    GX_CUDA(cudaSetDevice(c->device));
+    if (n_tok) {
+        const Matrix &m = c->mats[handle];
+        gx::MatvecArgs a{};
+        a.type = m.type;
+        a.tiles = m.tiles;
+        a.x = x;
+        a.y = y;
+        a.codebook = c->codebook;
+        a.rows = (int)m.rows;
+        a.cols = (int)m.cols;
+        a.n_tok = (int)n_tok;
+        a.err = c->err;
+        GX_CUDA(gx::launch_matvec(a, c->sm_count, c->stream));
+    }
+    return record_ticket(c, out_ticket);
+}
+
+GX_API gx_result gx_read_timings(gx_context *c, gx_timings *t) {
+    if (!c || !t) return GX_E_INVALIDARG;
+    std::memset(t, 0, sizeof(*t));
+    if (!(c->flags & GX_FLAG_PROFILE) || c->prof_layers == 0) return GX_OK;
+    GX_CUDA(cudaEventSynchronize(c->prof[4 * (size_t)(c->prof_layers - 1) + 3]));
+    for (uint32_t l = 0; l < c->prof_layers; ++l) {
+        const cudaEvent_t *ev = &c->prof[4 * (size_t)l];
+        float ms[3] = {0.f, 0.f, 0.f};
+        for (int k = 0; k < 3; ++k) GX_CUDA(cudaEventElapsedTime(&ms[k], ev[k], ev[k + 1]));
+        t->router_ns += (uint64_t)(ms[0] * 1e6);
+        t->gate_up_ns += (uint64_t)(ms[1] * 1e6);
+        t->down_ns += (uint64_t)(ms[2] * 1e6);
+    }
+    t->experts_ns = t->gate_up_ns + t->down_ns;
+    t->total_ns = t->router_ns + t->experts_ns;
+    t->layers = c->prof_layers;
+    return GX_OK;
+}
+
+GX_API gx_result gx_destroy(gx_context *c, uint32_t timeout_ms) {
+    if (!c) return GX_E_INVALIDARG;
+    if (!c->broken) {
+        cudaSetDevice(c->device);
+        gx_result r = sync_all(c, timeout_ms);
+        if (r == GX_E_TIMEOUT) return r;
+    }
+    release_all(c);
+    delete c;
+    return GX_OK;
+}
+
+}  // extern "C"

@@ -34,7 +34,9 @@ def packed_matrix(rng: np.random.Generator, type_id: int, rows: int, cols: int,
     1/sqrt(cols)); returns uint8 [rows, row_bytes]."""
     bb = BLOCK_BYTES[type_id]
     nb = cols // 128
-    data = np.frombuffer(rng.bytes(rows * nb * bb), dtype=np.uint8).reshape(rows, nb, bb).copy()
+    n = rows * nb * bb
+    raw = rng.bit_generator.random_raw((n + 7) // 8).view(np.uint8)[:n]
+    data = raw.reshape(rows, nb, bb)
     d = fp16_bits(1.0 / np.sqrt(cols) if scale is None else scale)
     data[:, :, 0] = d & 0xFF
     data[:, :, 1] = d >> 8

@@ -1,0 +1,208 @@
+/*
+ * gyro_moe.h — C ABI of the B200 (sm_100a) routed-expert MoE layer for Gyro trellis experts.
+ *
+ * Drop-in replacement, for the routed-MoE path, of the Direct3D 12 bridge of mattneel/gyro-dx:
+ * native/include/gyro_native.h:65-137 (mirrored in Zig by src/native_abi.zig:50-95 and wrapped
+ * by src/gpu.zig). The Zig caller is Engine.ffn (src/gpu_engine.zig:1052-1119); the tensors it
+ * hands over are the Matrix.data slices of src/model.zig:97-124 (stacked expert tensors, rows of
+ * packed 128-weight Gyro blocks), unchanged.
+ *
+ * Conventions kept from gyro_native.h:65-70:
+ *   - every call returns int32, negative = failure (GX_E_*), 0 = success;
+ *   - a context is used by one thread at a time (serialized access per context);
+ *   - every blocking call takes timeout_ms and returns GX_E_TIMEOUT instead of hanging;
+ *   - a failed or timed-out destroy keeps the handle valid for a retry;
+ *   - structs are plain C with fixed layouts (sizes asserted in the Zig mirror);
+ *   - work is enqueued asynchronously; tickets are monotonic u64 (gd_submit,
+ *     native/gyro_native.cpp:919-934) and become complete in order.
+ * Device pointers are CUDA device addresses of the context's device; host pointers are plain
+ * process memory (pinned or pageable).
+ */
+#ifndef GYRO_MOE_H
+#define GYRO_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(_WIN32) && defined(GX_EXPORTS)
+#define GX_API __declspec(dllexport)
+#elif defined(_WIN32)
+#define GX_API __declspec(dllimport)
+#else
+#define GX_API __attribute__((visibility("default")))
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GX_ABI_VERSION 1u
+
+typedef struct gx_context gx_context;
+typedef int32_t gx_result;
+
+enum {
+    GX_OK = 0,
+    GX_E_INVALIDARG = -1,   /* bad pointer, size, type id, layer index or shape */
+    GX_E_OUTOFMEMORY = -2,  /* device or pinned host allocation failed */
+    GX_E_TIMEOUT = -3,      /* a blocking call reached timeout_ms; the work is still queued */
+    GX_E_DEVICE = -4,       /* CUDA reported an error; the context should be destroyed */
+    GX_E_UNSUPPORTED = -5,  /* device is not sm_100 or the request is not supported */
+    GX_E_STATE = -6,        /* call out of order (layer not uploaded, context closed) */
+    GX_E_MISMATCH = -7,     /* gx_decode_blocks: an output differs from the expected bits */
+    GX_E_COMM = -8,         /* NCCL failure or peer loss in the expert-parallel group */
+    GX_E_KERNEL = -9        /* a kernel's bounded wait expired; its outputs are invalid */
+};
+
+/* Activation encodings (the type ids of src/kernels.zig:7-10). */
+enum { GX_F32 = 0, GX_BF16 = 30 };
+
+/* Options: mirrors the role of gd_options (native/include/gyro_native.h:25-31). */
+enum {
+    GX_FLAG_PROFILE = 1u      /* record per-phase device times (gx_read_timings) */
+};
+
+typedef struct gx_options {
+    uint32_t device;          /* CUDA device ordinal */
+    uint32_t rank;            /* expert-parallel rank in [0, world) */
+    uint32_t world;           /* expert-parallel group size; 1 = single GPU */
+    uint32_t max_tokens;      /* largest n_tok of one forward call on this rank */
+    uint32_t max_layers;      /* number of layer slots (gx_upload_layer indices) */
+    uint32_t flags;           /* GX_FLAG_* */
+    const void *codebook;     /* the normative 8192-byte table (src/gyro_codebook.f16) */
+    uint64_t codebook_bytes;  /* must be 8192 */
+    uint8_t nccl_id[128];     /* ncclUniqueId from rank 0 when world > 1, else ignored */
+} gx_options;                 /* 168 bytes */
+
+/* Replaces gd_caps (native/include/gyro_native.h:33-46). */
+typedef struct gx_caps {
+    uint32_t abi_version;
+    uint32_t sm_count;
+    uint32_t cc_major, cc_minor;
+    uint32_t rank, world;
+    uint32_t max_tokens, max_layers;
+    uint64_t hbm_bytes;       /* total device memory */
+    uint64_t free_bytes;      /* free device memory now */
+    uint64_t l2_bytes;
+    uint64_t arena_bytes;     /* bytes held by uploaded layers on this device */
+    char device_name[128];
+} gx_caps;                    /* 192 bytes */
+
+/* One routed-expert layer as the Zig host holds it (src/model.zig:97-124, :408-421). */
+typedef struct gx_layer_desc {
+    uint32_t type_id;             /* Gyro type of gate/up/down, 144..151 */
+    uint32_t n_expert;            /* experts in the layer (<= 512) */
+    uint32_t n_embd;              /* E: hidden width, multiple of 128 */
+    uint32_t n_ff;                /* F: expert FFN width, multiple of 128 */
+    uint32_t n_used;              /* U: experts per token (top-k), 1..16 */
+    float expert_weights_scale;   /* applied unless 0 or 1 (src/engine.zig:538) */
+    const void *gate;             /* [n_expert*F rows][E/128 blocks] packed, host memory */
+    const void *up;               /* same shape as gate */
+    const void *down;             /* [n_expert*E rows][F/128 blocks] packed, host memory */
+    uint64_t gate_bytes, up_bytes, down_bytes;
+    const float *router;          /* [n_expert][E] f32, host memory */
+    const float *gate_signs;      /* [E] +-1, or NULL when the experts are not rotated */
+    const float *up_signs;        /* must equal gate_signs (src/gpu_engine.zig:404) or be NULL */
+    const float *down_signs;      /* [F] +-1, or NULL */
+    const float *router_bias;     /* [n_expert] additive logit bias, or NULL (benchmark hook:
+                                     skewed expert popularity; no reference counterpart) */
+} gx_layer_desc;
+
+/* Per-phase device times, in nanoseconds, of the most recent forward call (gx_moe_forward*, or
+ * all layers of the most recent gx_stack_forward*) on a context created with GX_FLAG_PROFILE.
+ * Measured with CUDA events recorded on the context's stream between the kernels (inside the
+ * captured graph for stacks). Replaces gd_timestamp / gd_read_timestamps and the phase marks of
+ * Engine.mark (native/gyro_native.cpp:911-917, src/gpu_engine.zig:150-166). */
+typedef struct gx_timings {
+    uint64_t router_ns;     /* router GEMV + softmax/top-k */
+    uint64_t gate_up_ns;    /* fused decode gate/up GEMV + SwiGLU */
+    uint64_t down_ns;       /* fused decode down GEMV + weighted combine */
+    uint64_t experts_ns;    /* gate_up_ns + down_ns (+ dispatch/combine when world > 1) */
+    uint64_t total_ns;
+    uint64_t layers;        /* layers covered by these sums */
+} gx_timings;
+
+/* Opens a context on one device (replaces gd_create, native/include/gyro_native.h:71).
+ * With world > 1 every rank calls it with the same nccl_id; experts are then sharded:
+ * rank r owns experts [r*n_expert/world, (r+1)*n_expert/world). */
+GX_API gx_result gx_create(const gx_options *options, gx_context **out_context);
+
+/* Replaces gd_get_caps (native/include/gyro_native.h:72). */
+GX_API gx_result gx_get_caps(gx_context *context, gx_caps *out_caps);
+
+/* Copies one layer's router, signs and (local) experts from host memory into this device's
+ * HBM arena; the caller keeps ownership of its buffers. Replaces the resident-expert upload
+ * of Engine.setupExperts / loadBundle and the sign/codebook upload
+ * (src/gpu_engine.zig:447-458, :593-668). Blocking. */
+GX_API gx_result gx_upload_layer(gx_context *context, uint32_t layer, const gx_layer_desc *desc,
+                                 uint32_t timeout_ms);
+
+/* Routed-expert layer on device-resident activations, enqueued on the context's stream
+ * (replaces the dispatch chain of Engine.ffn, src/gpu_engine.zig:1059-1116, through
+ * gd_dispatch, native/gyro_native.cpp:891-900):
+ *   y[t] = sum_k w[t][k] * Down_e(act(Gate_e(Hx[t]), Up_e(Hx[t])))   (src/engine.zig:520-642)
+ * x: [n_tok][E] device, x_dtype GX_F32/GX_BF16; y: [n_tok][E] device, y_dtype GX_F32/GX_BF16.
+ * ids/weights: optional device outputs [n_tok][U] (the ffn_moe_topk observation), or NULL.
+ * out_ticket: optional; completes when y is written. With world > 1 this is a collective:
+ * every rank calls it for its own tokens (n_tok may differ, may be 0). */
+GX_API gx_result gx_moe_forward(gx_context *context, uint32_t layer, const void *x, uint32_t x_dtype,
+                                uint32_t n_tok, void *y, uint32_t y_dtype, uint32_t *ids, float *weights,
+                                uint64_t *out_ticket);
+
+/* Same on host buffers: copies x in and y (and ids/weights if non-NULL) out, then waits.
+ * This is the end-to-end call the host uses when its activations live in host memory. */
+GX_API gx_result gx_moe_forward_host(gx_context *context, uint32_t layer, const void *x, uint32_t x_dtype,
+                                     uint32_t n_tok, void *y, uint32_t y_dtype, uint32_t *ids,
+                                     float *weights, uint32_t timeout_ms);
+
+/* A stack of consecutive layers with a residual between them, x_{l+1} = x_l + MoE_l(x_l), for
+ * n_tok tokens (the benchmark stand-in for the hyper-connection mixer between layers, which
+ * lies outside this ABI). Device pointers; replayed from a CUDA graph after the first call
+ * with the same (first_layer, n_layers, n_tok, dtypes). */
+GX_API gx_result gx_stack_forward(gx_context *context, uint32_t first_layer, uint32_t n_layers,
+                                  const void *x, uint32_t x_dtype, uint32_t n_tok, void *y,
+                                  uint32_t y_dtype, uint64_t *out_ticket);
+GX_API gx_result gx_stack_forward_host(gx_context *context, uint32_t first_layer, uint32_t n_layers,
+                                       const void *x, uint32_t x_dtype, uint32_t n_tok, void *y,
+                                       uint32_t y_dtype, uint32_t timeout_ms);
+
+/* Ticket completion (replaces gd_wait_compute / gd_poll, native/include/gyro_native.h:84,126).
+ * gx_wait returns GX_E_TIMEOUT if the ticket is not complete after timeout_ms, GX_E_DEVICE on a
+ * CUDA error and GX_E_KERNEL if a kernel reported an expired bounded wait. */
+GX_API gx_result gx_wait(gx_context *context, uint64_t ticket, uint32_t timeout_ms);
+GX_API gx_result gx_poll(gx_context *context, uint64_t *out_completed);
+
+/* The context's CUDA stream (cudaStream_t), so the host can order its own work. */
+GX_API gx_result gx_get_stream(gx_context *context, void **out_stream);
+
+/* Gyro decode conformance hook (replaces gd_validate_gyro, native/gyro_native.cpp:597-730 and
+ * its shader shaders/gyro_decode.hlsl). Decodes value_count weights (a positive multiple of
+ * 128, at most 16777216) of packed blocks (host memory, exactly value_count/128 blocks of the
+ * type) into out (host, f32, stored basis, w = d * CB as one binary32 multiply). If expected is
+ * non-NULL the call returns GX_E_MISMATCH when any output differs bitwise and writes the
+ * largest absolute difference to max_abs_error (may be NULL). Blocking. */
+GX_API gx_result gx_decode_blocks(gx_context *context, uint32_t type_id, const void *packed,
+                                  uint64_t packed_bytes, float *out, uint32_t value_count,
+                                  const float *expected, float *max_abs_error, uint32_t timeout_ms);
+
+/* Standalone decode GEMV on one packed matrix, the per-slot product of moe_gyro
+ * (shaders/engine/moe.hlsl:108-211) and Engine.mv for Gyro weights:
+ *   y[t][r] = sum_c W[r][c] * x[t][c],  W [rows][cols] packed (reference layout, host),
+ * x [n_tok][cols] f32 device, y [n_tok][rows] f32 device, n_tok <= 64. gx_upload_matrix returns
+ * a handle (index) owned by the context. */
+GX_API gx_result gx_upload_matrix(gx_context *context, uint32_t type_id, uint32_t rows, uint32_t cols,
+                                  const void *packed, uint64_t packed_bytes, uint32_t *out_handle,
+                                  uint32_t timeout_ms);
+GX_API gx_result gx_matvec(gx_context *context, uint32_t handle, const float *x, uint32_t n_tok,
+                           float *y, uint64_t *out_ticket);
+
+GX_API gx_result gx_read_timings(gx_context *context, gx_timings *out_timings);
+
+/* Closes the context (replaces gd_destroy, native/include/gyro_native.h:137). Waits up to
+ * timeout_ms for queued work; on GX_E_TIMEOUT the context stays valid. */
+GX_API gx_result gx_destroy(gx_context *context, uint32_t timeout_ms);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GYRO_MOE_H */

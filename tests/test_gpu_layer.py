@@ -1,0 +1,178 @@
+"""GPU parity of the routed-MoE layer through the C ABI against the CPU oracle
+(src/engine.zig:520-642 restated). Tolerances are the north-star ones: relative RMS <= 1e-2 and
+cosine >= 0.9999 (tests/parity.py:28-44 metrics), top-k compared as per-token sets; the kernels
+actually land near 1e-6 relative, which the tighter checks below pin."""
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from oracle import oracle
+from gyro_moe import abi, metrics, synth
+from layer_case import small_layer
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).resolve().parent / "golden"
+REL_RMS, COSINE = 1e-2, 0.9999          # north-star layer tolerance
+TIGHT = 2e-5                            # what this implementation holds (fp16 hi/lo activations)
+
+torch = pytest.importorskip("torch")
+
+
+def check(ref, got, tight=TIGHT):
+    m = metrics.compare(ref, got)
+    assert m["rel_rms"] <= REL_RMS and m["cosine"] >= COSINE, m
+    assert m["rel_rms"] <= tight, m
+    return m
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    with abi.Context(device=0, max_tokens=64, max_layers=4) as c:
+        yield c
+
+
+def test_small_layer_matches_frozen_fixture(ctx):
+    layer, x = small_layer()
+    gold = json.loads((GOLDEN / "layer_small.json").read_text())
+    ctx.upload_layer(0, layer)
+    y, ids, w = ctx.forward_host(0, x, want_routing=True)
+    assert metrics.topk_sets(np.array(gold["ids"]), ids)["flips"] == 0
+    np.testing.assert_allclose(np.sort(w, 1), np.sort(np.array(gold["weights"], np.float32), 1), rtol=1e-5, atol=1e-7)
+    check(np.array(gold["out"], np.float32), y)
+
+
+@pytest.mark.parametrize("type_id", sorted(synth.BLOCK_BYTES))
+def test_small_layer_all_types(ctx, type_id):
+    layer, x = small_layer(seed=21 + type_id, type_id=type_id, n_tok=9)
+    ctx.upload_layer(1, layer)
+    want, wids, ww = oracle.moe_ffn(layer, x)
+    got, ids, w = ctx.forward_host(1, x, want_routing=True)
+    assert metrics.topk_sets(wids, ids)["flips"] == 0
+    check(want, got)
+
+
+def test_no_signs_and_weight_scale(ctx):
+    layer = synth.make_layer(5, n_expert=16, E=256, F=256, U=3, signs=False, expert_weights_scale=2.5)
+    x = synth.tokens(6, 4, E=256)
+    ctx.upload_layer(1, layer)
+    want, wids, ww = oracle.moe_ffn(layer, x)
+    got, ids, w = ctx.forward_host(1, x, want_routing=True)
+    assert metrics.topk_sets(wids, ids)["flips"] == 0
+    np.testing.assert_allclose(w.sum(1), 2.5, rtol=1e-5)
+    check(want, got)
+
+
+def test_config0_shape_one_token(ctx):
+    """Config 0: hidden 2048, 256 experts of gate/up [512x2048] and down [2048x512] TQ2_T, top-8,
+    router N(0, 0.02) f32, one f32 token ~N(0,1)."""
+    layer = synth.make_layer(0)
+    x = synth.tokens(1, 1)
+    ctx.upload_layer(2, layer)
+    want, wids, ww = oracle.moe_ffn(layer, x)
+    got, ids, w = ctx.forward_host(2, x, want_routing=True)
+    assert metrics.topk_sets(wids, ids)["flips"] == 0
+    np.testing.assert_allclose(w, ww, rtol=1e-5, atol=1e-7)
+    check(want, got)
+
+
+def test_config0_shape_batch_and_dtypes(ctx):
+    layer = synth.make_layer(0)
+    ctx.upload_layer(2, layer)
+    x = synth.tokens(7, 12, dtype="bf16")
+    want, wids, _ = oracle.moe_ffn(layer, x)
+    xb = synth.bf16_bits(x)
+    got, ids, _ = ctx.forward_host(2, xb, out_dtype=np.float32, want_routing=True)
+    assert metrics.topk_sets(wids, ids)["flips"] == 0
+    check(want, got)
+    # bf16 output: one rounding of the fp32 result
+    gb = ctx.forward_host(2, xb, out_dtype=np.uint16)
+    gbf = (gb.astype(np.uint32) << 16).view(np.float32)
+    check(want, gbf, tight=4e-3)
+
+
+def test_device_forward_matches_host_forward(ctx):
+    layer, x = small_layer(seed=9, n_tok=6)
+    ctx.upload_layer(3, layer)
+    host = ctx.forward_host(3, x)
+    xt = torch.from_numpy(x).cuda()
+    yt = torch.empty_like(xt)
+    ids = torch.empty((6, 4), dtype=torch.int32, device="cuda")
+    w = torch.empty((6, 4), dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    t = ctx.forward(3, xt, yt, ids, w)
+    ctx.wait(t)
+    assert np.array_equal(yt.cpu().numpy(), host)
+    assert ctx.poll() >= t
+
+
+def test_zipf_routing_with_empty_experts(ctx):
+    layer = synth.make_layer(3, n_expert=32, E=256, F=128, U=4, zipf=1.1)
+    layer["router_bias"][[1, 5, 9]] = -np.inf       # forced-empty experts
+    x = synth.tokens(4, 40, E=256)
+    ctx.upload_layer(1, layer)
+    want, wids, _ = oracle.moe_ffn(layer, x)
+    got, ids, _ = ctx.forward_host(1, x, want_routing=True)
+    assert not np.isin(ids, [1, 5, 9]).any()
+    assert metrics.topk_sets(wids, ids)["flips"] == 0
+    check(want, got)
+
+
+def test_stack_matches_oracle_chain(ctx):
+    layers = [synth.make_layer(40 + i, n_expert=16, E=256, F=128, U=4) for i in range(3)]
+    for i, l in enumerate(layers):
+        ctx.upload_layer(i, l)
+    x = synth.tokens(50, 2, E=256)
+    ref = x.copy()
+    for l in layers:
+        out, _, _ = oracle.moe_ffn(l, ref)
+        ref = ref + out
+    for _ in range(3):  # eager first call, then graph replays
+        got = ctx.stack_forward_host(0, 3, x)
+        check(ref, got, tight=5e-5)
+
+
+def test_forward_rejects_bad_calls(ctx):
+    import ctypes
+    lib, h = ctx.lib, ctx.handle
+    x = np.zeros((1, 256), np.float32)
+    y = np.zeros((1, 256), np.float32)
+    assert lib.gx_moe_forward_host(h, 99, x.ctypes.data, 0, 1, y.ctypes.data, 0, None, None, 1000) == -6
+    assert lib.gx_moe_forward_host(h, 0, x.ctypes.data, 7, 1, y.ctypes.data, 0, None, None, 1000) == -1
+    assert lib.gx_moe_forward_host(h, 0, x.ctypes.data, 0, 65, y.ctypes.data, 0, None, None, 1000) == -1
+    assert lib.gx_wait(h, 10 ** 9, 0) == -1
+
+
+def test_upload_rejects_bad_layers(ctx):
+    layer, _ = small_layer()
+    bad = dict(layer)
+    bad["up_signs"] = -layer["gate_signs"]          # gate and up must share signs
+    with pytest.raises(abi.GxError):
+        ctx.upload_layer(1, bad)
+    bad = dict(layer)
+    bad["gate"] = layer["gate"][:-1]                 # truncated expert tensor
+    with pytest.raises(abi.GxError):
+        ctx.upload_layer(1, bad)
+    bad = dict(layer)
+    bad["down_signs"] = layer["down_signs"] * 0      # signs must be +-1
+    with pytest.raises(abi.GxError):
+        ctx.upload_layer(1, bad)
+
+
+@pytest.mark.parametrize("type_id", sorted(synth.BLOCK_BYTES))
+@pytest.mark.parametrize("shape", [(512, 2048), (2048, 512)])
+def test_matvec_type_sweep(ctx, type_id, shape):
+    """Config 3: decode GEMV of every type at [512x2048] and [2048x512], batch 1, 4 and 16."""
+    rows, cols = shape
+    rng = np.random.default_rng(type_id * 7 + rows)
+    W = synth.packed_matrix(rng, type_id, rows, cols)
+    h = ctx.upload_matrix(type_id, rows, cols, W)
+    dense = np.stack([oracle.decode_row(type_id, W[r].tobytes(), cols) for r in range(rows)]).astype(np.float64)
+    for n in (1, 4, 16):
+        x = rng.standard_normal((n, cols)).astype(np.float32)
+        xt = torch.from_numpy(x).cuda()
+        yt = torch.empty((n, rows), dtype=torch.float32, device="cuda")
+        torch.cuda.synchronize()
+        ctx.wait(ctx.matvec(h, xt, yt))
+        check(x.astype(np.float64) @ dense.T, yt.cpu().numpy())
