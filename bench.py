@@ -7,7 +7,8 @@ Workload "decode" (default): a 40-layer stack of the con
 layer (hidden 2048, 256 experts of gate/up [512x2048] and down [2048x512] TQ2_T, top-8,
 router f32 ~N(0, 0.02)), independent seeded weights per layer (8.56 GB of packed experts
 resident in HBM), batch-1 greedy decode: each step pushes one fresh bf16 token ~N(0,1) through
-all 40 layers with x_{l+1} = x_l + MoE_l(x_l) (residual stand-in for the hyper-connection mixer).
+all 40 layers with x_{l+1} = x_l + MoE_l(RMSNorm(x_l)) (pre-norm residual stand-in for the
+hyper-connection mixer; the plain x + MoE(x) diverges within a few dozen random layers).
 A step touches 40 x 8 distinct experts = 267 MB of packed weights, more than the 126 MB L2, and
 consecutive steps route differently, so no step is served from L2.
 
@@ -142,9 +143,7 @@ def cpu_baseline(layers, seconds: float) -> dict:
     done, t0 = 0, time.perf_counter()
     while True:
         x = synth.bf16_round(rng.standard_normal((1, E)).astype(np.float32))
-        for layer in layers:
-            out, _, _ = oracle.moe_ffn(layer, x, threads=threads, fast=True)
-            x = x + out
+        oracle.stack(layers, x, threads=threads, fast=True)
         done += 1
         el = time.perf_counter() - t0
         if el >= seconds or done >= 64:
@@ -168,9 +167,7 @@ def run_reference(args):
     for i in range(args.warmup + args.steps):
         x = (xs[i].astype(np.uint32) << 16).view(np.float32)
         t0 = time.perf_counter()
-        for layer in layers:
-            out, _, _ = oracle.moe_ffn(layer, x, threads=threads, fast=True)
-            x = x + out
+        oracle.stack(layers, x, threads=threads, fast=True)
         if i >= args.warmup:
             times.append(time.perf_counter() - t0)
     total = sum(times)
@@ -210,7 +207,7 @@ def run_ours(args):
     n_tok = 1
     K, W = args.steps, args.warmup
 
-    ctx = abi.Context(device=local, max_tokens=max(n_tok, 1), max_layers=args.layers, flags=abi.GX_FLAG_PROFILE)
+    ctx = abi.Context(device=local, max_tokens=max(n_tok, 1), max_layers=args.layers)
     keep_host = (rank == 0 and world == 1 and not args.no_cpu_baseline)
     host_layers = []
     for l, layer in enumerate(make_layers(args.layers)):
@@ -223,7 +220,8 @@ def run_ours(args):
     stream = torch.cuda.ExternalStream(ctx.stream(), device=dev)
 
     for i in range(W):
-        ctx.stack_forward(0, args.layers, xs[i], y)
+        ticket = ctx.stack_forward(0, args.layers, xs[i], y)
+    ctx.wait(ticket)
     torch.cuda.synchronize(dev)
 
     start = torch.cuda.Event(enable_timing=True)
@@ -235,15 +233,30 @@ def run_ours(args):
         with torch.cuda.stream(stream):
             start.record(stream)
         for i in range(K):
-            ctx.stack_forward(0, args.layers, xs[W + i], y)
+            ticket = ctx.stack_forward(0, args.layers, xs[W + i], y)
         with torch.cuda.stream(stream):
             end.record(stream)
         end.synchronize()
+    ctx.wait(ticket)  # raises if a kernel reported an error during the timed steps
     torch.cuda.synchronize(dev)
     if dist:
         dist.barrier()
     ms = start.elapsed_time(end)
-    t = ctx.timings()  # phase times of the final timed step (events inside the captured graph)
+    # Kernel durations: the same steps replayed once more with phase events between the kernels
+    # (events separate the kernels, so the headline loop above runs without them).
+    ctx.set_flags(abi.GX_FLAG_PROFILE)
+    prof = []
+    for i in range(min(K, 8) + 1):
+        ctx.wait(ctx.stack_forward(0, args.layers, xs[W + i % K], y))
+        if i:
+            prof.append(ctx.timings())
+    ctx.set_flags(0)
+    t = abi.Timings()
+    for p in prof:
+        for f in ("router_ns", "gate_up_ns", "down_ns", "experts_ns", "total_ns", "layers"):
+            setattr(t, f, getattr(t, f) + getattr(p, f))
+    timing_source = (f"CUDA events on the library stream between the kernels of {len(prof)} replayed steps "
+                     f"({t.layers} layer launches) right after the timed region")
     ms_t = torch.tensor([ms], dtype=torch.float64, device=dev)
     if dist:
         dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
@@ -291,6 +304,7 @@ def run_ours(args):
             "frac": achieved / pk["hbm_gbs"] if achieved else None, "traffic": traffic,
             "algorithmic_bytes_per_launch": GATE_UP_BYTES * 8,
             "launch_us": gate_up_s * 1e6, "peak_source": f"{pk['source']} (MEASURED_PEAKS.json hbm_gbs, burst copy)",
+            "timing": timing_source,
             "experts_phase_gbs": experts_gbs,
             "experts_phase_frac": experts_gbs / pk["hbm_gbs"] if experts_gbs else None,
             "per_layer_us": {"router": router_s * 1e6, "gate_up": gate_up_s * 1e6, "down": down_s * 1e6},

@@ -3,6 +3,8 @@
 #include <cuda_runtime.h>
 
 #include <chrono>
+#include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <thread>
@@ -16,6 +18,8 @@
 namespace {
 
 constexpr int kEvents = 64;
+// RMSNorm epsilon of the stack's pre-norm residual x_{l+1} = x_l + MoE_l(RMSNorm(x_l)).
+constexpr float kStackNormEps = 1e-6f;
 
 struct Layer {
     bool ready = false;
@@ -33,7 +37,7 @@ struct Matrix {
     uint8_t *tiles = nullptr;
 };
 
-using GraphKey = std::tuple<uint32_t, uint32_t, uint32_t, uint32_t, uint32_t>;
+using GraphKey = std::tuple<uint32_t, uint32_t, uint32_t, uint32_t, uint32_t, uint32_t>;
 
 }  // namespace
 
@@ -47,8 +51,8 @@ struct gx_context {
     std::vector<Matrix> mats;
     // scratch sized for max_tokens
     float *logits = nullptr, *weights = nullptr, *act = nullptr, *xbuf[2] = {nullptr, nullptr};
+    float *xscale = nullptr, *ss = nullptr;
     uint32_t *ids = nullptr;
-    unsigned *counter = nullptr;
     int *err = nullptr;
     void *x_stage = nullptr, *y_stage = nullptr;     // device staging (graphs, host calls)
     void *h_in = nullptr, *h_out = nullptr;          // pinned host staging
@@ -63,7 +67,19 @@ struct gx_context {
 
 namespace {
 
-gx_result fail_cuda(gx_context *c, cudaError_t e) {
+// GX_DEBUG=1 in the environment prints the failing CUDA call to stderr.
+bool debug_enabled() {
+    static const bool on = [] {
+        const char *v = std::getenv("GX_DEBUG");
+        return v && v[0] && v[0] != '0';
+    }();
+    return on;
+}
+
+gx_result fail_cuda_at(gx_context *c, cudaError_t e, const char *what, int line) {
+    if (e != cudaSuccess && debug_enabled())
+        std::fprintf(stderr, "gyro_moe: %s failed at gx_abi.cu:%d: %s (%s)\n", what, line, cudaGetErrorName(e),
+                     cudaGetErrorString(e));
     if (e == cudaSuccess) return GX_OK;
     if (e == cudaErrorMemoryAllocation) {
         cudaGetLastError();
@@ -77,10 +93,11 @@ gx_result fail_cuda(gx_context *c, cudaError_t e) {
     return GX_E_DEVICE;
 }
 
-#define GX_CUDA(expr)                                  \
-    do {                                               \
-        cudaError_t gx_e_ = (expr);                    \
-        if (gx_e_ != cudaSuccess) return fail_cuda(c, gx_e_); \
+#define fail_cuda(c, e) fail_cuda_at((c), (e), "CUDA call", __LINE__)
+#define GX_CUDA(expr)                                                       \
+    do {                                                                    \
+        cudaError_t gx_e_ = (expr);                                         \
+        if (gx_e_ != cudaSuccess) return fail_cuda_at(c, gx_e_, #expr, __LINE__); \
     } while (0)
 
 uint64_t align256(uint64_t v) { return (v + 255) & ~uint64_t(255); }
@@ -102,6 +119,7 @@ gx_result wait_event(gx_context *c, cudaEvent_t ev, uint32_t timeout_ms) {
     cudaError_t e = cudaMemcpy(&err, c->err, sizeof(int), cudaMemcpyDeviceToHost);
     if (e != cudaSuccess) return fail_cuda(c, e);
     if (err != 0) {
+        if (debug_enabled()) std::fprintf(stderr, "gyro_moe: kernel error word %d (1 = expired wait, 2 = bad expert id)\n", err);
         cudaMemset(c->err, 0, sizeof(int));
         return GX_E_KERNEL;
     }
@@ -128,6 +146,8 @@ gx_result ensure_scratch(gx_context *c) {
     const size_t E = 4096, F = 1024, NE = 512, U = 16;
     GX_CUDA(cudaMalloc(&c->logits, T * NE * sizeof(float)));
     GX_CUDA(cudaMalloc(&c->weights, T * U * sizeof(float)));
+    GX_CUDA(cudaMalloc(&c->xscale, T * sizeof(float)));
+    GX_CUDA(cudaMalloc(&c->ss, T * sizeof(float)));
     GX_CUDA(cudaMalloc(&c->ids, T * U * sizeof(uint32_t)));
     GX_CUDA(cudaMalloc(&c->act, T * U * F * sizeof(float)));
     GX_CUDA(cudaMalloc(&c->xbuf[0], T * E * sizeof(float)));
@@ -137,8 +157,6 @@ gx_result ensure_scratch(gx_context *c) {
     GX_CUDA(cudaMalloc(&c->y_stage, c->stage_bytes));
     GX_CUDA(cudaMallocHost(&c->h_in, c->stage_bytes));
     GX_CUDA(cudaMallocHost(&c->h_out, c->stage_bytes + T * U * 8));
-    GX_CUDA(cudaMalloc(&c->counter, sizeof(unsigned)));
-    GX_CUDA(cudaMemset(c->counter, 0, sizeof(unsigned)));
     GX_CUDA(cudaMalloc(&c->err, sizeof(int)));
     GX_CUDA(cudaMemset(c->err, 0, sizeof(int)));
     return GX_OK;
@@ -152,8 +170,8 @@ void release_all(gx_context *c) {
     c->graphs.clear();
     for (auto &l : c->layers) if (l.arena) cudaFree(l.arena);
     for (auto &m : c->mats) if (m.tiles) cudaFree(m.tiles);
-    void *dev[] = {c->codebook, c->logits, c->weights, c->ids, c->act, c->xbuf[0], c->xbuf[1],
-                   c->x_stage, c->y_stage, c->counter, c->err};
+    void *dev[] = {c->codebook, c->logits, c->weights, c->xscale, c->ss, c->ids, c->act, c->xbuf[0], c->xbuf[1],
+                   c->x_stage, c->y_stage, c->err};
     for (void *p : dev) if (p) cudaFree(p);
     if (c->h_in) cudaFreeHost(c->h_in);
     if (c->h_out) cudaFreeHost(c->h_out);
@@ -166,11 +184,24 @@ void release_all(gx_context *c) {
 size_t dtype_size(uint32_t dt) { return dt == GX_BF16 ? 2 : 4; }
 
 // One routed layer: router + top-k, gate/up + SwiGLU, down + combine (+ residual).
+// Phase event: a plain record on the stream, or an event-record node (external record) while
+// the stream is being captured into a graph (a plain record there only orders graph nodes).
+cudaError_t record_phase(cudaEvent_t ev, cudaStream_t s) {
+    cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+    cudaError_t e = cudaStreamIsCapturing(s, &st);
+    if (e != cudaSuccess) return e;
+    return st == cudaStreamCaptureStatusActive ? cudaEventRecordWithFlags(ev, s, cudaEventRecordExternal)
+                                               : cudaEventRecord(ev, s);
+}
+
 // prof_slot >= 0 records the phase events of layer slot prof_slot (GX_FLAG_PROFILE).
+// norm_eps > 0 routes and feeds the experts RMSNorm(x) (unit weight); the residual stays x.
+// chained: the previous operation on the stream is this library's down kernel.
 gx_result enqueue_layer(gx_context *c, const Layer &L, const void *x, uint32_t x_dtype, uint32_t n_tok,
-                        const void *resid, uint32_t resid_dtype, void *out, uint32_t out_dtype, int prof_slot) {
+                        const void *resid, uint32_t resid_dtype, void *out, uint32_t out_dtype, int prof_slot,
+                        float norm_eps, bool chained) {
     cudaEvent_t *ev = prof_slot >= 0 ? &c->prof[4 * (size_t)prof_slot] : nullptr;
-    if (ev) GX_CUDA(cudaEventRecord(ev[0], c->stream));
+    if (ev) GX_CUDA(record_phase(ev[0], c->stream));
     gx::RouterArgs ra{};
     ra.W = L.router;
     ra.bias = L.bias;
@@ -181,13 +212,19 @@ gx_result enqueue_layer(gx_context *c, const Layer &L, const void *x, uint32_t x
     ra.E = (int)L.E;
     ra.U = (int)L.U;
     ra.scale = L.scale;
+    ra.norm_eps = norm_eps;
+    ra.ss = c->ss;
+    ra.xscale = c->xscale;
     ra.logits = c->logits;
     ra.ids = c->ids;
     ra.weights = c->weights;
-    ra.counter = c->counter;
     ra.err = c->err;
-    GX_CUDA(gx::launch_router(ra, c->stream));
-    if (ev) GX_CUDA(cudaEventRecord(ev[1], c->stream));
+    const bool fused = gx::gate_up_fuses_topk((int)L.E, (int)L.F, (int)L.U, (int)n_tok, c->sm_count);
+    // Programmatic overlap only between kernels of this chain: never across the phase events
+    // of a profiled call, and not for the first kernel of a call (its predecessor is a copy).
+    const bool pdl = ev == nullptr && chained;
+    GX_CUDA(gx::launch_router(ra, c->stream, pdl, !fused));
+    if (ev) GX_CUDA(record_phase(ev[1], c->stream));
 
     gx::GateUpArgs ga{};
     ga.type = L.type;
@@ -197,7 +234,17 @@ gx_result enqueue_layer(gx_context *c, const Layer &L, const void *x, uint32_t x
     ga.x = x;
     ga.x_bf16 = x_dtype == GX_BF16;
     ga.signs = L.gate_signs;
+    ga.xscale = norm_eps > 0.f ? c->xscale : nullptr;
     ga.ids = c->ids;
+    ga.fused_topk = fused;
+    ga.logits = c->logits;
+    ga.bias = L.bias;
+    ga.ss = c->ss;
+    ga.NE = (int)L.n_expert;
+    ga.norm_eps = norm_eps;
+    ga.wscale = L.scale;
+    ga.ids_out = c->ids;
+    ga.weights_out = c->weights;
     ga.act = c->act;
     ga.codebook = c->codebook;
     ga.E = (int)L.E;
@@ -206,8 +253,8 @@ gx_result enqueue_layer(gx_context *c, const Layer &L, const void *x, uint32_t x
     ga.n_slots = (int)(n_tok * L.U);
     ga.n_expert = (int)L.local_experts;
     ga.err = c->err;
-    GX_CUDA(gx::launch_gate_up(ga, c->sm_count, c->stream));
-    if (ev) GX_CUDA(cudaEventRecord(ev[2], c->stream));
+    GX_CUDA(gx::launch_gate_up(ga, c->sm_count, c->stream, ev == nullptr));
+    if (ev) GX_CUDA(record_phase(ev[2], c->stream));
 
     gx::DownArgs da{};
     da.type = L.type;
@@ -228,8 +275,8 @@ gx_result enqueue_layer(gx_context *c, const Layer &L, const void *x, uint32_t x
     da.n_tok = (int)n_tok;
     da.n_expert = (int)L.local_experts;
     da.err = c->err;
-    GX_CUDA(gx::launch_down(da, c->sm_count, c->stream));
-    if (ev) GX_CUDA(cudaEventRecord(ev[3], c->stream));
+    GX_CUDA(gx::launch_down(da, c->sm_count, c->stream, ev == nullptr));
+    if (ev) GX_CUDA(record_phase(ev[3], c->stream));
     return GX_OK;
 }
 
@@ -253,7 +300,8 @@ gx_result stack_enqueue(gx_context *c, uint32_t first, uint32_t n_layers, const 
         void *out = last ? y : c->xbuf[i & 1];
         const uint32_t out_dtype = last ? y_dtype : GX_F32;
         const int slot = (c->flags & GX_FLAG_PROFILE) ? (int)i : -1;
-        gx_result r = enqueue_layer(c, L, cur, cur_dtype, n_tok, cur, cur_dtype, out, out_dtype, slot);
+        gx_result r = enqueue_layer(c, L, cur, cur_dtype, n_tok, cur, cur_dtype, out, out_dtype, slot, kStackNormEps,
+                                    i > 0);
         if (r != GX_OK) return r;
         cur = out;
         cur_dtype = out_dtype;
@@ -453,7 +501,7 @@ GX_API gx_result gx_moe_forward(gx_context *c, uint32_t layer, const void *x, ui
     if (n_tok > 0) {
         const bool prof = (c->flags & GX_FLAG_PROFILE) != 0;
         if (prof) c->prof_layers = 1;
-        r = enqueue_layer(c, L, x, x_dtype, n_tok, nullptr, GX_F32, y, y_dtype, prof ? 0 : -1);
+        r = enqueue_layer(c, L, x, x_dtype, n_tok, nullptr, GX_F32, y, y_dtype, prof ? 0 : -1, 0.f, false);
         if (r != GX_OK) return r;
         if (ids) GX_CUDA(cudaMemcpyAsync(ids, c->ids, (size_t)n_tok * L.U * 4, cudaMemcpyDeviceToDevice, c->stream));
         if (weights)
@@ -475,7 +523,8 @@ GX_API gx_result gx_moe_forward_host(gx_context *c, uint32_t layer, const void *
     GX_CUDA(cudaMemcpyAsync(c->x_stage, c->h_in, in_b, cudaMemcpyHostToDevice, c->stream));
     const bool prof = (c->flags & GX_FLAG_PROFILE) != 0;
     if (prof) c->prof_layers = 1;
-    r = enqueue_layer(c, L, c->x_stage, x_dtype, n_tok, nullptr, GX_F32, c->y_stage, y_dtype, prof ? 0 : -1);
+    r = enqueue_layer(c, L, c->x_stage, x_dtype, n_tok, nullptr, GX_F32, c->y_stage, y_dtype, prof ? 0 : -1, 0.f,
+                      false);
     if (r != GX_OK) return r;
     uint8_t *ho = static_cast<uint8_t *>(c->h_out);
     const size_t sel_b = (size_t)n_tok * L.U * 4;
@@ -505,7 +554,7 @@ GX_API gx_result gx_stack_forward(gx_context *c, uint32_t first, uint32_t n_laye
     const size_t in_b = n_tok * E * dtype_size(x_dtype), out_b = n_tok * E * dtype_size(y_dtype);
     // The graph reads x_stage and writes y_stage; the caller's buffers are copied around it.
     GX_CUDA(cudaMemcpyAsync(c->x_stage, x, in_b, cudaMemcpyDeviceToDevice, c->stream));
-    const GraphKey key{first, n_layers, n_tok, x_dtype, y_dtype};
+    const GraphKey key{first, n_layers, n_tok, x_dtype, y_dtype, c->flags};
     auto it = c->graphs.find(key);
     if (it == c->graphs.end()) {
         // First call runs eagerly (sets kernel attributes), then the chain is captured.
@@ -700,6 +749,13 @@ GX_API gx_result gx_read_timings(gx_context *c, gx_timings *t) {
     t->experts_ns = t->gate_up_ns + t->down_ns;
     t->total_ns = t->router_ns + t->experts_ns;
     t->layers = c->prof_layers;
+    return GX_OK;
+}
+
+GX_API gx_result gx_set_flags(gx_context *c, uint32_t flags) {
+    if (!c || (flags & ~(uint32_t)GX_FLAG_PROFILE)) return GX_E_INVALIDARG;
+    c->flags = flags;
+    c->prof_layers = 0;
     return GX_OK;
 }
 

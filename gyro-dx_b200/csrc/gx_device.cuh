@@ -36,7 +36,11 @@ struct Codebook {
     static constexpr int WORDS = 2048 * NCOPY;
     static constexpr int BYTES = WORDS * 4;
 
+    // Consecutive threads write consecutive shared words (no bank conflicts); each reads its
+    // word's codebook entry from the L1-resident 8 KB global table. The loads of a thread are
+    // independent, so they overlap.
     __device__ static void stage(uint32_t *smem, const uint32_t *__restrict__ global_table, int tid, int nthreads) {
+#pragma unroll 16
         for (int w = tid; w < WORDS; w += nthreads) {
             const int idx = ((w >> 5) << LW) | (w & (W - 1));
             smem[w] = __ldg(global_table + idx);
@@ -131,6 +135,29 @@ __device__ __forceinline__ void fwht128_warp(float (&v)[4], int lane) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) v[j] *= norm;
 }
+
+// Programmatic dependent launch: a kernel launched with programmatic stream serialization
+// may start while its predecessor still runs; pdl_wait() blocks until the predecessor grid has
+// completed and its memory is visible. Every CTA calls pdl_wait() before it reads anything the
+// predecessor wrote or writes anything a predecessor reads. Without the launch attribute both
+// instructions are no-ops.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Optional phase trace (build with -DGX_TRACE): thread 0 of each CTA stores clock64 deltas from
+// the CTA's start at numbered points into gx_trace[kernel][cta][point]. Off in normal builds.
+#ifdef GX_TRACE
+constexpr int kTraceKernels = 4, kTraceCtas = 160, kTracePoints = 8;
+__device__ long long gx_trace[kTraceKernels][kTraceCtas][kTracePoints];  // this header has one includer
+#define GX_TRACE_START(k) const long long gx_t0_ = clock64(); const int gx_tk_ = (k)
+#define GX_TRACE_POINT(p)                                                                  \
+    do {                                                                                   \
+        if (threadIdx.x == 0 && blockIdx.x < kTraceCtas) gx_trace[gx_tk_][blockIdx.x][p] = clock64() - gx_t0_; \
+    } while (0)
+#else
+#define GX_TRACE_START(k) do {} while (0)
+#define GX_TRACE_POINT(p) do {} while (0)
+#endif
 
 __device__ __forceinline__ float load_act(const void *p, int bf16, size_t i) {
     if (bf16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(p)[i]);

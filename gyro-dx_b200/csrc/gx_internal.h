@@ -6,7 +6,8 @@
 
 namespace gx {
 
-// Shared-memory codebook copies used by the decode-GEMV kernels.
+// Shared-memory codebook copies of the decode-GEMV kernels (2 banks per copy, so at most two
+// lanes of a warp contend for a bank during a lookup).
 constexpr int kCodebookCopies = 16;
 
 struct RouterArgs {
@@ -16,10 +17,12 @@ struct RouterArgs {
     int x_bf16;
     int n_tok, NE, E, U;
     float scale;             // expert_weights_scale
-    float *logits;           // [n_tok][NE] scratch
+    float norm_eps;          // > 0: route RMSNorm(x) (unit weight)
+    float *ss;               // [n_tok] sum of squares of x (written when norm_eps > 0)
+    float *xscale;           // [n_tok] per-token input scale (written by topk_kernel)
+    float *logits;           // [n_tok][NE] scratch (raw W x, before scale and bias)
     uint32_t *ids;           // [n_tok][U]
     float *weights;          // [n_tok][U]
-    unsigned *counter;       // zero at rest; reset by the last CTA
     int *err;
 };
 
@@ -31,12 +34,26 @@ struct GateUpArgs {
     const void *x;           // [n_tok][E]
     int x_bf16;
     const float *signs;      // [E] or nullptr
-    const uint32_t *ids;     // [n_slots] local expert of each slot
+    const float *xscale;     // [n_tok] input scale from topk_kernel, or nullptr (unfused only)
+    const uint32_t *ids;     // [n_slots] local expert of each slot (unfused only)
     float *act;              // [n_slots][F] silu(gate) * up
     const uint32_t *codebook;// 2048 words in global memory
     int E, F, U, n_slots, n_expert;
     int *err;
+    // Fused selection (few tokens): each CTA selects the experts of its own tokens from the
+    // router's raw logits, and the CTA holding a token's first unit publishes ids/weights.
+    int fused_topk;
+    const float *logits;     // [n_tok][NE] raw W x
+    const float *bias;       // [NE] or nullptr
+    const float *ss;         // [n_tok] sum of squares of x (norm_eps > 0)
+    int NE;
+    float norm_eps, wscale;  // RMSNorm epsilon (0: none), expert_weights_scale
+    uint32_t *ids_out;       // [n_tok][U]
+    float *weights_out;      // [n_tok][U]
 };
+
+// Whether gate_up_kernel can select experts itself for n_tok tokens (at most 8 tokens per CTA).
+bool gate_up_fuses_topk(int E, int F, int U, int n_tok, int sm_count);
 
 struct DownArgs {
     uint32_t type;
@@ -65,9 +82,11 @@ struct MatvecArgs {
     int *err;
 };
 
-cudaError_t launch_router(const RouterArgs &a, cudaStream_t s);
-cudaError_t launch_gate_up(const GateUpArgs &a, int sm_count, cudaStream_t s);
-cudaError_t launch_down(const DownArgs &a, int sm_count, cudaStream_t s);
+// pdl: launch with programmatic stream serialization (overlap with the previous kernel).
+// with_topk: also launch the per-token selection kernel (when gate_up does not fuse it).
+cudaError_t launch_router(const RouterArgs &a, cudaStream_t s, bool pdl, bool with_topk);
+cudaError_t launch_gate_up(const GateUpArgs &a, int sm_count, cudaStream_t s, bool pdl);
+cudaError_t launch_down(const DownArgs &a, int sm_count, cudaStream_t s, bool pdl);
 cudaError_t launch_matvec(const MatvecArgs &a, int sm_count, cudaStream_t s);
 cudaError_t launch_repack(uint32_t type, const uint8_t *raw, uint64_t row_bytes, uint32_t rows,
                           uint32_t cols, uint8_t *tiles, cudaStream_t s);

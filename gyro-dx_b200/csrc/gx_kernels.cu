@@ -28,11 +28,9 @@
 
 namespace gx {
 
-using CB = Codebook<kCodebookCopies>;
-
 // One 8-row x 128-column tile against NG groups of 8 tokens. acc[g][0..1] accumulates, for
 // token (8g + lane/4), rows 2*(lane%4) and 2*(lane%4)+1 of the tile (scaled by d).
-template <uint32_t T, int NG>
+template <uint32_t T, int NG, int NC>
 __device__ __forceinline__ void tile_mma(const uint8_t *tile, const uint32_t *cb, uint32_t copy_off, int lane,
                                          const uint32_t (&A)[NG][8][4], float (&acc)[NG][2]) {
     uint32_t own[4];
@@ -45,22 +43,25 @@ __device__ __forceinline__ void tile_mma(const uint8_t *tile, const uint32_t *cb
     uint32_t b0[8], b1[8];
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
-        b0[c] = cb[CB::word(i0[c], copy_off)];
-        b1[c] = cb[CB::word(i1[c], copy_off)];
+        b0[c] = cb[Codebook<NC>::word(i0[c], copy_off)];
+        b1[c] = cb[Codebook<NC>::word(i1[c], copy_off)];
     }
-    float d[NG][4];
+    // Two independent accumulator chains (even / odd chunks) halve the mma dependency chain.
+    float d[2][NG][4];
 #pragma unroll
-    for (int g = 0; g < NG; ++g) d[g][0] = d[g][1] = d[g][2] = d[g][3] = 0.f;
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int g = 0; g < NG; ++g) d[h][g][0] = d[h][g][1] = d[h][g][2] = d[h][g][3] = 0.f;
 #pragma unroll
     for (int c = 0; c < 8; ++c)
 #pragma unroll
-        for (int g = 0; g < NG; ++g) mma16816(d[g], A[g][c], b0[c], b1[c]);
+        for (int g = 0; g < NG; ++g) mma16816(d[c & 1][g], A[g][c], b0[c], b1[c]);
     const uint32_t sc = *reinterpret_cast<const uint32_t *>(tile + tile_code_bytes(T) + 4 * (lane & 3));
     const float2 s = __half22float2(*reinterpret_cast<const __half2 *>(&sc));
 #pragma unroll
     for (int g = 0; g < NG; ++g) {
-        acc[g][0] += s.x * (d[g][0] + d[g][2]);
-        acc[g][1] += s.y * (d[g][1] + d[g][3]);
+        acc[g][0] += s.x * ((d[0][g][0] + d[1][g][0]) + (d[0][g][2] + d[1][g][2]));
+        acc[g][1] += s.y * ((d[0][g][1] + d[1][g][1]) + (d[0][g][3] + d[1][g][3]));
     }
 }
 
@@ -88,12 +89,12 @@ __device__ __forceinline__ void build_a_single(const float *xs, int lane, uint32
 
 // Rotated block of one activation row into xs (per-warp scratch of 128 floats):
 // xs = H128(signs * v) / sqrt(128) for v = src[base .. base+128).
-__device__ __forceinline__ void rotated_block_to_smem(const void *src, int bf16, size_t base, const float *signs,
-                                                      int sbase, float *xs, int lane) {
+__device__ __forceinline__ void rotated_block_to_smem(const void *src, int bf16, size_t base, float scale,
+                                                      const float *signs, int sbase, float *xs, int lane) {
     float v[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-        v[j] = load_act(src, bf16, base + 4 * lane + j);
+        v[j] = load_act(src, bf16, base + 4 * lane + j) * scale;
         if (signs) v[j] *= signs[sbase + 4 * lane + j];
     }
     if (signs) fwht128_warp(v, lane);
@@ -103,144 +104,261 @@ __device__ __forceinline__ void rotated_block_to_smem(const void *src, int bf16,
 }
 
 // ------------------------------------------------------------------------------------------
-// Router: one warp per expert row; the last CTA to finish runs the per-token selection.
+// Router GEMV (one warp per expert row) and expert selection.
 // ------------------------------------------------------------------------------------------
-__device__ void topk_token(const float *row, int NE, int U, float scale, uint32_t *ids, float *weights, int lane) {
+// Selection for one token (one warp): optional RMSNorm scale of x (src/kernels.zig:281-291 with
+// unit weight), logits = scale * (W x) + bias, softmax (src/kernels.zig:340-349), top-U with
+// lower-index ties (src/engine.zig:671-686), renormalisation by max(sum, 2^-14) and the optional
+// expert_weights_scale (src/engine.zig:533-539).
+__device__ void topk_token(const RouterArgs &a, int t, int lane) {
+    const float *row = a.logits + (size_t)t * a.NE;
+    const float scale = a.norm_eps > 0.f ? 1.0f / sqrtf(__ldcg(a.ss + t) / (float)a.E + a.norm_eps) : 1.f;
     float v[16];
-    float m = -INFINITY;
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
         const int i = lane + 32 * j;
-        v[j] = i < NE ? __ldcg(row + i) : -INFINITY;
-        m = fmaxf(m, v[j]);
+        v[j] = i < a.NE ? __ldcg(row + i) * scale + (a.bias ? __ldg(a.bias + i) : 0.f) : -INFINITY;
     }
+    float m = v[0];
+#pragma unroll
+    for (int j = 1; j < 16; ++j) m = fmaxf(m, v[j]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     float s = 0.f;
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
-        const int i = lane + 32 * j;
-        v[j] = i < NE ? expf(v[j] - m) : 0.f;
+        v[j] = (lane + 32 * j) < a.NE ? expf(v[j] - m) : 0.f;
         s += v[j];
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    // Selection key: probability bits (order-preserving for p >= 0) above the complemented
+    // index, so one unsigned max picks the largest probability and, among equal ones, the
+    // lowest index (the tie rule of src/engine.zig:671-686). Absent experts have key 0.
+    unsigned long long key[16];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) v[j] = (lane + 32 * j) < NE ? v[j] / s : -1.f;
-    float wk[16];
-    uint32_t ik[16];
-    for (int k = 0; k < U; ++k) {
-        float bv = -2.f;
-        uint32_t bi = 0xffffffffu;
+    for (int j = 0; j < 16; ++j) {
+        const int i = lane + 32 * j;
+        key[j] = i < a.NE ? ((unsigned long long)__float_as_uint(v[j] / s) << 32) | (0xffffffffu - (uint32_t)i) : 0ull;
+    }
+    float my_w = 0.f;
+    uint32_t my_id = 0;
+    for (int k = 0; k < a.U; ++k) {
+        unsigned long long b8[8];
 #pragma unroll
-        for (int j = 0; j < 16; ++j)
-            if (v[j] > bv) { bv = v[j]; bi = (uint32_t)(lane + 32 * j); }
+        for (int j = 0; j < 8; ++j) b8[j] = key[j] > key[j + 8] ? key[j] : key[j + 8];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) b8[j] = b8[j] > b8[j + 4] ? b8[j] : b8[j + 4];
+        b8[0] = b8[0] > b8[2] ? b8[0] : b8[2];
+        b8[1] = b8[1] > b8[3] ? b8[1] : b8[3];
+        unsigned long long best = b8[0] > b8[1] ? b8[0] : b8[1];
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+            const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+            best = other > best ? other : best;
         }
 #pragma unroll
         for (int j = 0; j < 16; ++j)
-            if ((uint32_t)(lane + 32 * j) == bi) v[j] = -1.f;
-        wk[k & 15] = bv;
-        ik[k & 15] = bi;
-    }
-    if (lane == 0) {
-        float total = 0.f;
-        for (int k = 0; k < U; ++k) total += wk[k];
-        total = fmaxf(total, 6.103515625e-5f);
-        for (int k = 0; k < U; ++k) {
-            float w = wk[k] / total;
-            if (scale != 0.f && scale != 1.f) w *= scale;
-            ids[k] = ik[k];
-            weights[k] = w;
+            if (key[j] == best) key[j] = 0ull;
+        if (lane == k) {
+            my_w = __uint_as_float((uint32_t)(best >> 32));
+            my_id = 0xffffffffu - (uint32_t)best;
         }
     }
+    // Renormalisation in selection order (src/engine.zig:533-539).
+    float total = 0.f;
+    for (int k = 0; k < a.U; ++k) total += __shfl_sync(0xffffffffu, my_w, k);
+    total = fmaxf(total, 6.103515625e-5f);
+    if (lane < a.U) {
+        float w = my_w / total;
+        if (a.scale != 0.f && a.scale != 1.f) w *= a.scale;
+        a.ids[(size_t)t * a.U + lane] = my_id;
+        a.weights[(size_t)t * a.U + lane] = w;
+    }
+    if (lane == 0) a.xscale[t] = scale;
 }
 
-__global__ void __launch_bounds__(64) router_kernel(RouterArgs a, int fused_topk) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, wpb = blockDim.x >> 5;
-    const int r = blockIdx.x * wpb + warp;
-    if (r < a.NE) {
-        const float *w = a.W + (size_t)r * a.E;
-        const float bias = a.bias ? a.bias[r] : 0.f;
-        for (int cbase = 0; cbase < a.E; cbase += 2048) {
-            float4 wv[16];
+// Block-wide selection for one token by a 512-thread CTA (thread i scores expert i): the same
+// arithmetic as topk_token, then every warp keeps its own top-U and warp 0 merges them.
+// Results go to sel_ids / sel_w (U entries) and *sel_scale; cand and red are shared scratch.
+__device__ void block_topk(const GateUpArgs &a, int t, uint32_t *sel_ids, float *sel_w, float *sel_scale,
+                           unsigned long long *cand, float *red) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const float scale = a.norm_eps > 0.f ? 1.0f / sqrtf(__ldcg(a.ss + t) / (float)a.E + a.norm_eps) : 1.f;
+    const bool live = tid < a.NE;
+    const float l = live ? __ldcg(a.logits + (size_t)t * a.NE + tid) * scale + (a.bias ? __ldg(a.bias + tid) : 0.f)
+                         : -INFINITY;
+    float m = l;
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                const int c = cbase + 128 * j + 4 * lane;
-                wv[j] = c < a.E ? __ldg(reinterpret_cast<const float4 *>(w + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    m = red[0];
+#pragma unroll
+    for (int w = 1; w < 16; ++w) m = fmaxf(m, red[w]);
+    __syncthreads();
+    const float e = live ? expf(l - m) : 0.f;
+    float s = e;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0) red[warp] = s;
+    __syncthreads();
+    s = 0.f;
+#pragma unroll
+    for (int w = 0; w < 16; ++w) s += red[w];
+    unsigned long long key = live ? ((unsigned long long)__float_as_uint(e / s) << 32) | (0xffffffffu - (uint32_t)tid) : 0ull;
+    unsigned long long mine = 0ull;
+    for (int k = 0; k < a.U; ++k) {
+        unsigned long long best = key;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+            best = other > best ? other : best;
+        }
+        if (key == best) key = 0ull;
+        if (lane == k) mine = best;
+    }
+    if (lane < 16) cand[warp * 16 + lane] = lane < a.U ? mine : 0ull;
+    __syncthreads();
+    if (warp == 0) {
+        unsigned long long c[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) c[j] = cand[lane + 32 * j];
+        float my_w = 0.f;
+        uint32_t my_id = 0;
+        for (int k = 0; k < a.U; ++k) {
+            unsigned long long b = c[0];
+#pragma unroll
+            for (int j = 1; j < 8; ++j) b = c[j] > b ? c[j] : b;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const unsigned long long other = __shfl_xor_sync(0xffffffffu, b, o);
+                b = other > b ? other : b;
             }
-            for (int t0 = 0; t0 < a.n_tok; t0 += 8) {
-                float acc[8];
 #pragma unroll
-                for (int t = 0; t < 8; ++t) acc[t] = 0.f;
+            for (int j = 0; j < 8; ++j)
+                if (c[j] == b) c[j] = 0ull;
+            if (lane == k) {
+                my_w = __uint_as_float((uint32_t)(b >> 32));
+                my_id = 0xffffffffu - (uint32_t)b;
+            }
+        }
+        float total = 0.f;
+        for (int k = 0; k < a.U; ++k) total += __shfl_sync(0xffffffffu, my_w, k);
+        total = fmaxf(total, 6.103515625e-5f);
+        if (lane < a.U) {
+            float w = my_w / total;
+            if (a.wscale != 0.f && a.wscale != 1.f) w *= a.wscale;
+            sel_ids[lane] = my_id;
+            sel_w[lane] = w;
+        }
+        if (lane == 0) *sel_scale = scale;
+    }
+    __syncthreads();
+}
+
+constexpr int kRouterTok = 4;       // tokens staged in shared memory per pass
+constexpr int kRouterWarps = 2;     // expert rows per CTA
+
+// W rows are loaded into registers before pdl_wait(), so they stream while the previous kernel
+// (the last layer's down GEMV) still runs. x is staged in shared memory as f32.
+template <int NJ>
+__global__ void __launch_bounds__(64) router_kernel(RouterArgs a) {
+    extern __shared__ __align__(16) float xsm[];          // [kRouterTok][E]
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int r = blockIdx.x * kRouterWarps + warp;
+    GX_TRACE_START(0);
+    pdl_launch_dependents();
+    const bool has_row = r < a.NE;
+    const float *w = a.W + (size_t)(has_row ? r : 0) * a.E;
+    float4 wv[NJ];                                       // E <= 128 * NJ
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int c = cbase + 128 * j + 4 * lane;
-                    if (c >= a.E) break;
+    for (int j = 0; j < NJ; ++j) {
+        const int c = 128 * j + 4 * lane;
+        wv[j] = (has_row && c < a.E) ? __ldg(reinterpret_cast<const float4 *>(w + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    GX_TRACE_POINT(0);
+    pdl_wait();
+    GX_TRACE_POINT(1);
+    for (int t0 = 0; t0 < a.n_tok; t0 += kRouterTok) {
+        const int nt = min(kRouterTok, a.n_tok - t0);
+        __syncthreads();
+        // 8 values per thread per iteration (E is a multiple of 128): independent 16-byte loads.
+#pragma unroll 4
+        for (int i = threadIdx.x * 8; i < nt * a.E; i += blockDim.x * 8) {
+            const size_t g = (size_t)t0 * a.E + i;
+            float v[8];
+            if (a.x_bf16) {
+                const uint4 q = *reinterpret_cast<const uint4 *>(reinterpret_cast<const __nv_bfloat16 *>(a.x) + g);
+                const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-                    for (int t = 0; t < 8; ++t) {
-                        if (t0 + t < a.n_tok) {
-                            const size_t base = (size_t)(t0 + t) * a.E + c;
-                            float x0, x1, x2, x3;
-                            if (a.x_bf16) {
-                                const __nv_bfloat162 *p = reinterpret_cast<const __nv_bfloat162 *>(
-                                    reinterpret_cast<const __nv_bfloat16 *>(a.x) + base);
-                                const float2 u0 = __bfloat1622float2(p[0]), u1 = __bfloat1622float2(p[1]);
-                                x0 = u0.x; x1 = u0.y; x2 = u1.x; x3 = u1.y;
-                            } else {
-                                const float4 xv = *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(a.x) + base);
-                                x0 = xv.x; x1 = xv.y; x2 = xv.z; x3 = xv.w;
-                            }
-                            acc[t] = fmaf(wv[j].x, x0, acc[t]);
-                            acc[t] = fmaf(wv[j].y, x1, acc[t]);
-                            acc[t] = fmaf(wv[j].z, x2, acc[t]);
-                            acc[t] = fmaf(wv[j].w, x3, acc[t]);
-                        }
-                    }
+                for (int j = 0; j < 4; ++j) {
+                    v[2 * j] = __uint_as_float(w4[j] << 16);
+                    v[2 * j + 1] = __uint_as_float(w4[j] & 0xffff0000u);
+                }
+            } else {
+                const float4 p0 = *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(a.x) + g);
+                const float4 p1 = *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(a.x) + g + 4);
+                v[0] = p0.x; v[1] = p0.y; v[2] = p0.z; v[3] = p0.w;
+                v[4] = p1.x; v[5] = p1.y; v[6] = p1.z; v[7] = p1.w;
+            }
+            *reinterpret_cast<float4 *>(xsm + i) = make_float4(v[0], v[1], v[2], v[3]);
+            *reinterpret_cast<float4 *>(xsm + i + 4) = make_float4(v[4], v[5], v[6], v[7]);
+        }
+        __syncthreads();
+        GX_TRACE_POINT(5);
+        // CTA 0 publishes each token's sum of squares for the RMSNorm scale (read by top-k).
+        if (a.norm_eps > 0.f && blockIdx.x == 0 && warp == 0) {
+            for (int t = 0; t < nt; ++t) {
+                float ss = 0.f;
+                for (int i = lane * 4; i < a.E; i += 128) {
+                    const float4 v = *reinterpret_cast<const float4 *>(xsm + t * a.E + i);
+                    ss = fmaf(v.x, v.x, ss);
+                    ss = fmaf(v.y, v.y, ss);
+                    ss = fmaf(v.z, v.z, ss);
+                    ss = fmaf(v.w, v.w, ss);
                 }
 #pragma unroll
-                for (int t = 0; t < 8; ++t) {
+                for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+                if (lane == 0) a.ss[t0 + t] = ss;
+            }
+        }
+        float acc[kRouterTok];
 #pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) acc[t] += __shfl_xor_sync(0xffffffffu, acc[t], o);
-                }
-                if (lane == 0) {
-                    for (int t = 0; t < 8 && t0 + t < a.n_tok; ++t) {
-                        float *dst = a.logits + (size_t)(t0 + t) * a.NE + r;
-                        // Columns beyond the first 2048 accumulate onto the stored partial.
-                        *dst = (cbase == 0 ? bias : *dst) + acc[t];
+        for (int t = 0; t < kRouterTok; ++t) acc[t] = 0.f;
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) {
+            const int c = 128 * j + 4 * lane;
+            if (c < a.E) {
+#pragma unroll
+                for (int t = 0; t < kRouterTok; ++t) {
+                    if (t < nt) {
+                        const float4 xv = *reinterpret_cast<const float4 *>(xsm + t * a.E + c);
+                        acc[t] = fmaf(wv[j].x, xv.x, acc[t]);
+                        acc[t] = fmaf(wv[j].y, xv.y, acc[t]);
+                        acc[t] = fmaf(wv[j].z, xv.z, acc[t]);
+                        acc[t] = fmaf(wv[j].w, xv.w, acc[t]);
                     }
                 }
             }
         }
+#pragma unroll
+        for (int t = 0; t < kRouterTok; ++t)
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) acc[t] += __shfl_xor_sync(0xffffffffu, acc[t], o);
+        if (lane == 0 && has_row)
+            for (int t = 0; t < nt; ++t) a.logits[(size_t)(t0 + t) * a.NE + r] = acc[t];
     }
-    if (!fused_topk) return;
-    __shared__ int is_last;
-    __threadfence();  // every logits writer publishes before the CTA takes its ticket
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        const unsigned prev = atomicAdd(a.counter, 1u);
-        is_last = prev == gridDim.x - 1;
-    }
-    __syncthreads();
-    if (!is_last) return;
-    __threadfence();
-    for (int t = warp; t < a.n_tok; t += wpb)
-        topk_token(a.logits + (size_t)t * a.NE, a.NE, a.U, a.scale, a.ids + (size_t)t * a.U,
-                   a.weights + (size_t)t * a.U, lane);
-    if (threadIdx.x == 0) *a.counter = 0u;
+    GX_TRACE_POINT(2);
 }
 
 __global__ void __launch_bounds__(256) topk_kernel(RouterArgs a) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (t >= a.n_tok) return;
-    topk_token(a.logits + (size_t)t * a.NE, a.NE, a.U, a.scale, a.ids + (size_t)t * a.U,
-               a.weights + (size_t)t * a.U, lane);
+    topk_token(a, t, lane);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -266,8 +384,9 @@ __device__ __forceinline__ bool stage_wait(const StageCtl &c, int s, int *err) {
 }
 
 // ---- gate/up: unit = (slot, RG row-groups of both projections) ---------------------------
-template <uint32_t T, int KBW>
+template <uint32_t T, int KBW, int NC>
 __global__ void __launch_bounds__(512, 1) gate_up_kernel(GateUpArgs a, int P) {
+    using CB = Codebook<NC>;
     constexpr int TB = tile_bytes(T);
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -283,8 +402,15 @@ __global__ void __launch_bounds__(512, 1) gate_up_kernel(GateUpArgs a, int P) {
     uint8_t *stage = smem + CB::BYTES;
     float *part = reinterpret_cast<float *>(stage + 2 * stage_bytes);  // [P][2][16][8]
     float *xs = part + P * 2 * 16 * 8;                                  // [16][128]
-    uint64_t *bar = reinterpret_cast<uint64_t *>(xs + 16 * 128);
+    unsigned long long *cand = reinterpret_cast<unsigned long long *>(xs + 16 * 128);  // [256]
+    uint32_t *sel_ids = reinterpret_cast<uint32_t *>(cand + 256);      // [8][16]
+    float *sel_w = reinterpret_cast<float *>(sel_ids + 128);           // [8][16]
+    float *sel_scale = sel_w + 128;                                    // [8]
+    float *red = sel_scale + 8;                                        // [16]
+    uint64_t *bar = reinterpret_cast<uint64_t *>(red + 16);
 
+    GX_TRACE_START(1);
+    pdl_launch_dependents();
     const int n_units = a.n_slots * UPS;
     StageCtl ctl;
     ctl.bar = bar;
@@ -292,6 +418,8 @@ __global__ void __launch_bounds__(512, 1) gate_up_kernel(GateUpArgs a, int P) {
     ctl.u0 = (int)((long long)blockIdx.x * n_units / gridDim.x);
     ctl.u1 = (int)((long long)(blockIdx.x + 1) * n_units / gridDim.x);
     ctl.n_stages = (ctl.u1 - ctl.u0 + P - 1) / P;
+    const int tok_first = (ctl.u0 / UPS) / a.U;
+    const int n_tok_cta = ctl.n_stages > 0 ? ((ctl.u1 - 1) / UPS) / a.U - tok_first + 1 : 0;
 
     if (tid == 0) {
         mbar_init(&bar[0], 1);
@@ -300,60 +428,92 @@ __global__ void __launch_bounds__(512, 1) gate_up_kernel(GateUpArgs a, int P) {
     }
     __syncthreads();
 
+    // Warp 0 fills stage s: lane 0 posts the byte count, then every lane loads one slot's
+    // expert id and issues that copy, so the id loads and copies go out in parallel.
     auto issue = [&](int s) {
         uint8_t *buf = stage + (s & 1) * stage_bytes;
         const int ua = ctl.u0 + s * P, ub = min(ua + P, ctl.u1);
-        uint32_t total = 0;
-        for (int u = ua; u < ub; ++u) {
-            const int ui = u % UPS;
-            total += 2u * (uint32_t)(min(RG, NT - ui * RG) * NB * TB);
+        if (lane == 0) {
+            uint32_t total = 0;
+            for (int u = ua; u < ub; ++u) total += 2u * (uint32_t)(min(RG, NT - (u % UPS) * RG) * NB * TB);
+            mbar_expect_tx(&bar[s & 1], total);
         }
-        mbar_expect_tx(&bar[s & 1], total);
-        for (int u = ua; u < ub; ++u) {
+        __syncwarp();
+        for (int k = lane; k < (ub - ua) * 2; k += 32) {
+            const int u = ua + (k >> 1), proj = k & 1;
             const int slot = u / UPS, ui = u % UPS;
             const uint32_t bytes = (uint32_t)(min(RG, NT - ui * RG) * NB * TB);
-            uint32_t e = a.ids[slot];
+            uint32_t e = a.fused_topk ? sel_ids[(slot / a.U - tok_first) * 16 + slot % a.U] : a.ids[slot];
             if (e >= (uint32_t)a.n_expert) {
                 atomicExch(a.err, KERR_BOUNDS);
                 e = 0;
             }
             const uint64_t off = (uint64_t)e * a.expert_bytes + (uint64_t)ui * unit_proj;
-            uint8_t *dst = buf + (u - ua) * 2 * unit_proj;
-            bulk_g2s(dst, a.gate + off, bytes, &bar[s & 1]);
-            bulk_g2s(dst + unit_proj, a.up + off, bytes, &bar[s & 1]);
+            bulk_g2s(buf + (u - ua) * 2 * unit_proj + proj * unit_proj, (proj ? a.up : a.gate) + off, bytes,
+                     &bar[s & 1]);
         }
     };
-    if (tid == 0) {
+    CB::stage(cb, a.codebook, tid, blockDim.x);
+    GX_TRACE_POINT(0);
+    pdl_wait();
+    GX_TRACE_POINT(1);
+    if (a.fused_topk) {
+        // Expert selection for the tokens of this CTA's units; the CTA holding a token's first
+        // unit publishes it for the down kernel.
+        for (int tt = 0; tt < n_tok_cta; ++tt)
+            block_topk(a, tok_first + tt, sel_ids + tt * 16, sel_w + tt * 16, sel_scale + tt, cand, red);
+        if (tid < n_tok_cta * a.U) {
+            const int tt = tid / a.U, k = tid % a.U, t = tok_first + tt;
+            const int first_unit = t * a.U * UPS;
+            if (first_unit >= ctl.u0 && first_unit < ctl.u1) {
+                a.ids_out[t * a.U + k] = sel_ids[tt * 16 + k];
+                a.weights_out[t * a.U + k] = sel_w[tt * 16 + k];
+            }
+        }
+    }
+    if (warp == 0) {
         if (ctl.n_stages > 0) issue(0);
         if (ctl.n_stages > 1) issue(1);
     }
-    CB::stage(cb, a.codebook, tid, blockDim.x);
     __syncthreads();
 
+    GX_TRACE_POINT(2);
     const bool active = warp < WB * RG;
     const int kcol = warp % WB, rg = warp / WB;
     const uint32_t copy_off = CB::copy_off(lane);
     uint32_t A[KBW][1][8][4];
     int cur_tok = -1;
     float *xw = xs + warp * 128;
+    // The first unit's activations are prepared while its weights are still in flight.
+    auto build_a = [&](int tok) {
+#pragma unroll
+        for (int j = 0; j < KBW; ++j) {
+            const int b = kcol + WB * j;
+            if (b < NB) {
+                rotated_block_to_smem(a.x, a.x_bf16, (size_t)tok * a.E + b * 128,
+                                      a.fused_topk ? sel_scale[tok - tok_first] : (a.xscale ? a.xscale[tok] : 1.f),
+                                      a.signs, b * 128, xw, lane);
+                build_a_single(xw, lane, A[j][0]);
+                __syncwarp();
+            }
+        }
+    };
+    if (active && ctl.n_stages > 0) {
+        cur_tok = (ctl.u0 / UPS) / a.U;
+        build_a(cur_tok);
+    }
+    GX_TRACE_POINT(3);
 
     for (int s = 0; s < ctl.n_stages; ++s) {
         if (!stage_wait(ctl, s, a.err)) return;
+        if (s == 0) GX_TRACE_POINT(4);
         const int ua = ctl.u0 + s * P, ub = min(ua + P, ctl.u1);
         const uint8_t *buf = stage + (s & 1) * stage_bytes;
         for (int u = ua; u < ub; ++u) {
             const int slot = u / UPS, ui = u % UPS;
             const int tok = slot / a.U;
             if (active && tok != cur_tok) {
-#pragma unroll
-                for (int j = 0; j < KBW; ++j) {
-                    const int b = kcol + WB * j;
-                    if (b < NB) {
-                        rotated_block_to_smem(a.x, a.x_bf16, (size_t)tok * a.E + b * 128, a.signs, b * 128, xw, lane);
-                        build_a_single(xw, lane, A[j][0]);
-                        __syncwarp();
-                    }
-                }
+                build_a(tok);
                 cur_tok = tok;
             }
             const int nt = min(RG, NT - ui * RG);
@@ -366,7 +526,7 @@ __global__ void __launch_bounds__(512, 1) gate_up_kernel(GateUpArgs a, int P) {
                     for (int j = 0; j < KBW; ++j) {
                         const int b = kcol + WB * j;
                         if (b < NB)
-                            tile_mma<T, 1>(ubase + proj * unit_proj + (rg * NB + b) * TB, cb, copy_off, lane, A[j], acc);
+                            tile_mma<T, 1, NC>(ubase + proj * unit_proj + (rg * NB + b) * TB, cb, copy_off, lane, A[j], acc);
                     }
                     if (lane < 4) {
                         float *p = part + (((u - ua) * 2 + proj) * 16 + rg * WB + kcol) * 8 + 2 * lane;
@@ -376,8 +536,9 @@ __global__ void __launch_bounds__(512, 1) gate_up_kernel(GateUpArgs a, int P) {
                 }
             }
         }
+        if (s == 0) GX_TRACE_POINT(5);
         __syncthreads();
-        if (tid == 0 && s + 2 < ctl.n_stages) issue(s + 2);
+        if (warp == 0 && s + 2 < ctl.n_stages) issue(s + 2);
         for (int r = tid; r < (ub - ua) * RG * 8; r += blockDim.x) {
             const int j = r / (RG * 8), rgi = (r >> 3) % RG, n = r & 7;
             const int u = ua + j, slot = u / UPS, ui = u % UPS;
@@ -391,11 +552,13 @@ __global__ void __launch_bounds__(512, 1) gate_up_kernel(GateUpArgs a, int P) {
         }
         __syncthreads();
     }
+    GX_TRACE_POINT(6);
 }
 
 // ---- down: unit = (token, one row group); warps own (slot, block) pairs -------------------
-template <uint32_t T, int KBW>
+template <uint32_t T, int KBW, int NC>
 __global__ void __launch_bounds__(512, 1) down_kernel(DownArgs a, int P) {
+    using CB = Codebook<NC>;
     constexpr int TB = tile_bytes(T);
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -411,8 +574,11 @@ __global__ void __launch_bounds__(512, 1) down_kernel(DownArgs a, int P) {
     uint8_t *stage = smem + CB::BYTES;
     float *part = reinterpret_cast<float *>(stage + 2 * stage_bytes);  // [P][PMAX][8]
     float *xs = part + P * PMAX * 8;                                    // [16][128]
-    uint64_t *bar = reinterpret_cast<uint64_t *>(xs + 16 * 128);
+    float *wsm = xs + 16 * 128;                                         // [P][16] routing weights
+    uint64_t *bar = reinterpret_cast<uint64_t *>(wsm + 4 * 16);
 
+    GX_TRACE_START(2);
+    pdl_launch_dependents();
     const int n_units = a.n_tok * NT;
     StageCtl ctl;
     ctl.bar = bar;
@@ -428,63 +594,98 @@ __global__ void __launch_bounds__(512, 1) down_kernel(DownArgs a, int P) {
     }
     __syncthreads();
 
+    // Warp 0 fills stage s, one (unit, slot) copy per lane (see gate_up_kernel).
     auto issue = [&](int s) {
         uint8_t *buf = stage + (s & 1) * stage_bytes;
         const int ua = ctl.u0 + s * P, ub = min(ua + P, ctl.u1);
-        mbar_expect_tx(&bar[s & 1], (uint32_t)((ub - ua) * unit_bytes));
-        for (int u = ua; u < ub; ++u) {
+        if (lane == 0) mbar_expect_tx(&bar[s & 1], (uint32_t)((ub - ua) * unit_bytes));
+        __syncwarp();
+        for (int q = lane; q < (ub - ua) * a.U; q += 32) {
+            const int u = ua + q / a.U, k = q % a.U;
             const int t = u / NT, i = u % NT;
-            for (int k = 0; k < a.U; ++k) {
-                uint32_t e = a.ids[t * a.U + k];
-                if (e >= (uint32_t)a.n_expert) {
-                    atomicExch(a.err, KERR_BOUNDS);
-                    e = 0;
-                }
-                bulk_g2s(buf + (u - ua) * unit_bytes + k * slot_bytes,
-                         a.down + (uint64_t)e * a.expert_bytes + (uint64_t)i * slot_bytes, (uint32_t)slot_bytes,
-                         &bar[s & 1]);
+            uint32_t e = a.ids[t * a.U + k];
+            if (e >= (uint32_t)a.n_expert) {
+                atomicExch(a.err, KERR_BOUNDS);
+                e = 0;
             }
+            bulk_g2s(buf + (u - ua) * unit_bytes + k * slot_bytes,
+                     a.down + (uint64_t)e * a.expert_bytes + (uint64_t)i * slot_bytes, (uint32_t)slot_bytes, &bar[s & 1]);
         }
     };
-    if (tid == 0) {
+    CB::stage(cb, a.codebook, tid, blockDim.x);
+    GX_TRACE_POINT(0);
+    pdl_wait();
+    GX_TRACE_POINT(1);
+    if (warp == 0) {
         if (ctl.n_stages > 0) issue(0);
         if (ctl.n_stages > 1) issue(1);
     }
-    CB::stage(cb, a.codebook, tid, blockDim.x);
     __syncthreads();
 
+    GX_TRACE_POINT(2);
     const uint32_t copy_off = CB::copy_off(lane);
     uint32_t A[KBW][1][8][4];
     int cur_tok = -1;
     float *xw = xs + warp * 128;
+    // Down input of token t: signs + FWHT of silu(g)*u per (slot, block) pair of this warp. All
+    // pairs' loads go out before the first transform.
+    auto build_a = [&](int t) {
+        float v[KBW][4], sg[KBW][4];
+#pragma unroll
+        for (int j = 0; j < KBW; ++j) {
+            const int p = warp + 16 * j;
+            if (p < NPAIR) {
+                const int k = p / NBF, b = p % NBF;
+                const float4 q = *reinterpret_cast<const float4 *>(a.act + (size_t)(t * a.U + k) * a.F + b * 128 + 4 * lane);
+                v[j][0] = q.x; v[j][1] = q.y; v[j][2] = q.z; v[j][3] = q.w;
+                if (a.signs) {
+                    const float4 g = *reinterpret_cast<const float4 *>(a.signs + b * 128 + 4 * lane);
+                    sg[j][0] = g.x; sg[j][1] = g.y; sg[j][2] = g.z; sg[j][3] = g.w;
+                }
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < KBW; ++j) {
+            const int p = warp + 16 * j;
+            if (p < NPAIR) {
+                if (a.signs) {
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) v[j][q] *= sg[j][q];
+                    fwht128_warp(v[j], lane);
+                }
+#pragma unroll
+                for (int q = 0; q < 4; ++q) xw[4 * lane + q] = v[j][q];
+                __syncwarp();
+                build_a_single(xw, lane, A[j][0]);
+                __syncwarp();
+            }
+        }
+    };
+    if (ctl.n_stages > 0) {
+        cur_tok = ctl.u0 / NT;
+        build_a(cur_tok);
+    }
+    GX_TRACE_POINT(3);
 
     for (int s = 0; s < ctl.n_stages; ++s) {
         if (!stage_wait(ctl, s, a.err)) return;
+        if (s == 0) GX_TRACE_POINT(4);
         const int ua = ctl.u0 + s * P, ub = min(ua + P, ctl.u1);
         const uint8_t *buf = stage + (s & 1) * stage_bytes;
         for (int u = ua; u < ub; ++u) {
             const int t = u / NT;
             if (t != cur_tok) {
-#pragma unroll
-                for (int j = 0; j < KBW; ++j) {
-                    const int p = warp + 16 * j;
-                    if (p < NPAIR) {
-                        const int k = p / NBF, b = p % NBF;
-                        rotated_block_to_smem(a.act, 0, (size_t)(t * a.U + k) * a.F + b * 128, a.signs, b * 128, xw,
-                                              lane);
-                        build_a_single(xw, lane, A[j][0]);
-                        __syncwarp();
-                    }
-                }
+                build_a(t);
                 cur_tok = t;
             }
+            if (warp == 0 && lane < a.U) wsm[(u - ua) * 16 + lane] = a.weights[t * a.U + lane];
 #pragma unroll
             for (int j = 0; j < KBW; ++j) {
                 const int p = warp + 16 * j;
                 if (p < NPAIR) {
                     const int k = p / NBF, b = p % NBF;
                     float acc[1][2] = {{0.f, 0.f}};
-                    tile_mma<T, 1>(buf + (u - ua) * unit_bytes + k * slot_bytes + b * TB, cb, copy_off, lane, A[j],
+                    tile_mma<T, 1, NC>(buf + (u - ua) * unit_bytes + k * slot_bytes + b * TB, cb, copy_off, lane, A[j],
                                    acc);
                     if (lane < 4) {
                         float *q = part + ((u - ua) * PMAX + p) * 8 + 2 * lane;
@@ -494,8 +695,9 @@ __global__ void __launch_bounds__(512, 1) down_kernel(DownArgs a, int P) {
                 }
             }
         }
+        if (s == 0) GX_TRACE_POINT(5);
         __syncthreads();
-        if (tid == 0 && s + 2 < ctl.n_stages) issue(s + 2);
+        if (warp == 0 && s + 2 < ctl.n_stages) issue(s + 2);
         for (int r = tid; r < (ub - ua) * 8; r += blockDim.x) {
             const int j = r >> 3, n = r & 7;
             const int u = ua + j, t = u / NT, i = u % NT;
@@ -504,7 +706,7 @@ __global__ void __launch_bounds__(512, 1) down_kernel(DownArgs a, int P) {
             for (int k = 0; k < a.U; ++k) {
                 float dk = 0.f;
                 for (int b = 0; b < NBF; ++b) dk += part[(j * PMAX + k * NBF + b) * 8 + n];
-                v += a.weights[t * a.U + k] * dk;
+                v += wsm[j * 16 + k] * dk;
             }
             const size_t o = (size_t)t * a.E + row;
             if (a.resid) v = load_act(a.resid, a.resid_bf16, o) + v;
@@ -515,11 +717,14 @@ __global__ void __launch_bounds__(512, 1) down_kernel(DownArgs a, int P) {
         }
         __syncthreads();
     }
+    GX_TRACE_POINT(6);
 }
 
 // ---- standalone matvec: unit = RG row groups; up to 16 tokens (2 groups of 8) -----------
-template <uint32_t T, int KBW, int NG>
+template <uint32_t T, int KBW, int NG, int NC>
 __global__ void __launch_bounds__(512, 1) matvec_kernel(MatvecArgs a, int t0, int P) {
+    using CB = Codebook<NC>;
+    GX_TRACE_START(3);
     constexpr int TB = tile_bytes(T);
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -552,14 +757,17 @@ __global__ void __launch_bounds__(512, 1) matvec_kernel(MatvecArgs a, int t0, in
     auto issue = [&](int s) {
         uint8_t *buf = stage + (s & 1) * stage_bytes;
         const int ua = ctl.u0 + s * P, ub = min(ua + P, ctl.u1);
-        uint32_t total = 0;
-        for (int u = ua; u < ub; ++u) total += (uint32_t)(min(RG, NT - u * RG) * NB * TB);
-        mbar_expect_tx(&bar[s & 1], total);
-        for (int u = ua; u < ub; ++u)
+        if (lane == 0) {
+            uint32_t total = 0;
+            for (int u = ua; u < ub; ++u) total += (uint32_t)(min(RG, NT - u * RG) * NB * TB);
+            mbar_expect_tx(&bar[s & 1], total);
+        }
+        __syncwarp();
+        for (int u = ua + lane; u < ub; u += 32)
             bulk_g2s(buf + (u - ua) * unit_bytes, a.tiles + (uint64_t)u * unit_bytes,
                      (uint32_t)(min(RG, NT - u * RG) * NB * TB), &bar[s & 1]);
     };
-    if (tid == 0) {
+    if (warp == 0) {
         if (ctl.n_stages > 0) issue(0);
         if (ctl.n_stages > 1) issue(1);
     }
@@ -610,7 +818,7 @@ __global__ void __launch_bounds__(512, 1) matvec_kernel(MatvecArgs a, int t0, in
 #pragma unroll
                 for (int j = 0; j < KBW; ++j) {
                     const int b = kcol + WB * j;
-                    if (b < NB) tile_mma<T, NG>(buf + (u - ua) * unit_bytes + (rg * NB + b) * TB, cb, copy_off, lane, A[j], acc);
+                    if (b < NB) tile_mma<T, NG, NC>(buf + (u - ua) * unit_bytes + (rg * NB + b) * TB, cb, copy_off, lane, A[j], acc);
                 }
 #pragma unroll
                 for (int grp = 0; grp < NG; ++grp) {
@@ -620,8 +828,9 @@ __global__ void __launch_bounds__(512, 1) matvec_kernel(MatvecArgs a, int t0, in
                 }
             }
         }
+        if (s == 0) GX_TRACE_POINT(5);
         __syncthreads();
-        if (tid == 0 && s + 2 < ctl.n_stages) issue(s + 2);
+        if (warp == 0 && s + 2 < ctl.n_stages) issue(s + 2);
         for (int r = tid; r < (ub - ua) * RG * 16 * 8; r += blockDim.x) {
             const int j = r / (RG * 128), rgi = (r / 128) % RG, tok = (r >> 3) & 15, n = r & 7;
             const int u = ua + j;
@@ -688,71 +897,91 @@ namespace {
 
 constexpr int kSmemLimit = 227 * 1024;
 
-// Raises a kernel's dynamic shared-memory limit once (never inside a stream capture: the
-// first launch of every instantiation happens in an eager call).
-template <typename K>
-cudaError_t set_smem(K kernel, int) {
-    static cudaError_t once = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+// Raises the dynamic shared-memory limit of kernel instantiation K once per process (never
+// inside a stream capture: the first launch of every instantiation happens in an eager call).
+template <auto K, int Bytes = kSmemLimit>
+cudaError_t set_smem() {
+    static const cudaError_t once = cudaFuncSetAttribute(K, cudaFuncAttributeMaxDynamicSharedMemorySize, Bytes);
     return once;
 }
 
-template <uint32_t T, int KBW>
-cudaError_t gate_up_t(const GateUpArgs &a, int sm_count, cudaStream_t s) {
+template <typename... KArgs, typename... Args>
+cudaError_t launch(void (*kernel)(KArgs...), int grid, int block, int smem, cudaStream_t s, bool pdl, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3((unsigned)block);
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+// Stage count P per buffer: as many units as fit under the budget (at most 4).
+int pick_stages(int fixed, int per_stage, int budget) {
+    int P = 4;
+    while (P > 1 && fixed + 2 * P * per_stage > budget) --P;
+    return fixed + 2 * P * per_stage <= budget ? P : 0;
+}
+
+template <uint32_t T, int KBW, int NC>
+cudaError_t gate_up_t(const GateUpArgs &a, int sm_count, cudaStream_t s, bool pdl) {
     const int NB = a.E / 128, WB = NB < 16 ? NB : 16, RG = 16 / WB;
     const int unit_proj = RG * NB * tile_bytes(T);
-    const int fixed = CB::BYTES + 16 * 128 * 4 + 64;
-    int P = 4;
-    while (P > 1 && fixed + 2 * P * 2 * unit_proj + P * 2 * 16 * 8 * 4 > kSmemLimit) --P;
+    // codebook + per-warp activation scratch + selection scratch + barriers
+    const int fixed = Codebook<NC>::BYTES + 16 * 128 * 4 + (256 * 8 + 128 * 4 * 2 + 8 * 4 + 16 * 4) + 64;
+    // per stage: P units x 2 projections, plus the partials of those units
+    const int per_unit = 2 * unit_proj + 2 * 16 * 8 * 4 / 2;
+    const int P = pick_stages(fixed, per_unit, kSmemLimit);
+    if (P == 0) return cudaErrorInvalidValue;
     const int smem = fixed + 2 * P * 2 * unit_proj + P * 2 * 16 * 8 * 4;
-    if (smem > kSmemLimit) return cudaErrorInvalidValue;
     const int NT = a.F / 8, UPS = (NT + RG - 1) / RG;
     const int n_units = a.n_slots * UPS;
     if (n_units == 0) return cudaSuccess;
+    // 512 threads at ~120 registers fill an SM's register file: one CTA per SM.
     const int grid = n_units < sm_count ? n_units : sm_count;
-    auto k = gate_up_kernel<T, KBW>;
-    cudaError_t e = set_smem(k, smem);
+    cudaError_t e = set_smem<gate_up_kernel<T, KBW, NC>>();
     if (e != cudaSuccess) return e;
-    k<<<grid, 512, smem, s>>>(a, P);
-    return cudaGetLastError();
+    return launch(gate_up_kernel<T, KBW, NC>, grid, 512, smem, s, pdl, a, P);
 }
 
-template <uint32_t T, int KBW>
-cudaError_t down_t(const DownArgs &a, int sm_count, cudaStream_t s) {
+template <uint32_t T, int KBW, int NC>
+cudaError_t down_t(const DownArgs &a, int sm_count, cudaStream_t s, bool pdl) {
     const int NBF = a.F / 128;
     const int unit_bytes = a.U * NBF * tile_bytes(T);
     const int PMAX = 16 * KBW;
-    const int fixed = CB::BYTES + 16 * 128 * 4 + 64;
-    int P = 4;
-    while (P > 1 && fixed + 2 * P * unit_bytes + P * PMAX * 8 * 4 > kSmemLimit) --P;
+    const int fixed = Codebook<NC>::BYTES + 16 * 128 * 4 + 4 * 16 * 4 + 64;
+    const int per_unit = unit_bytes + PMAX * 8 * 4 / 2;
+    const int P = pick_stages(fixed, per_unit, kSmemLimit);
+    if (P == 0) return cudaErrorInvalidValue;
     const int smem = fixed + 2 * P * unit_bytes + P * PMAX * 8 * 4;
-    if (smem > kSmemLimit) return cudaErrorInvalidValue;
     const int n_units = a.n_tok * (a.E / 8);
     if (n_units == 0) return cudaSuccess;
+    // 512 threads at ~120 registers fill an SM's register file: one CTA per SM.
     const int grid = n_units < sm_count ? n_units : sm_count;
-    auto k = down_kernel<T, KBW>;
-    cudaError_t e = set_smem(k, smem);
+    cudaError_t e = set_smem<down_kernel<T, KBW, NC>>();
     if (e != cudaSuccess) return e;
-    k<<<grid, 512, smem, s>>>(a, P);
-    return cudaGetLastError();
+    return launch(down_kernel<T, KBW, NC>, grid, 512, smem, s, pdl, a, P);
 }
 
 template <uint32_t T, int KBW, int NG>
 cudaError_t matvec_t(const MatvecArgs &a, int sm_count, cudaStream_t s) {
+    constexpr int NC = kCodebookCopies;
     const int NB = a.cols / 128, WB = NB < 16 ? NB : 16, RG = 16 / WB;
     const int unit_bytes = RG * NB * tile_bytes(T);
-    const int fixed = CB::BYTES + 64;
-    int P = 4;
-    while (P > 1 && fixed + 2 * P * unit_bytes + P * 16 * 16 * 8 * 4 > kSmemLimit) --P;
+    const int fixed = Codebook<NC>::BYTES + 64;
+    int P = pick_stages(fixed, unit_bytes + 16 * 16 * 8 * 4 / 2, kSmemLimit);
+    if (P == 0) return cudaErrorInvalidValue;
     const int smem = fixed + 2 * P * unit_bytes + P * 16 * 16 * 8 * 4;
-    if (smem > kSmemLimit) return cudaErrorInvalidValue;
     const int NT = a.rows / 8, n_units = (NT + RG - 1) / RG;
     const int grid = n_units < sm_count ? n_units : sm_count;
-    auto k = matvec_kernel<T, KBW, NG>;
-    cudaError_t e = set_smem(k, smem);
+    cudaError_t e = set_smem<matvec_kernel<T, KBW, NG, NC>>();
     if (e != cudaSuccess) return e;
     for (int t0 = 0; t0 < a.n_tok; t0 += 16) {
-        k<<<grid, 512, smem, s>>>(a, t0, P);
-        e = cudaGetLastError();
+        e = launch(matvec_kernel<T, KBW, NG, NC>, grid, 512, smem, s, false, a, t0, P);
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;
@@ -771,31 +1000,49 @@ cudaError_t matvec_t(const MatvecArgs &a, int sm_count, cudaStream_t s) {
         default: return cudaErrorInvalidValue;     \
     }
 
+
 }  // namespace
 
-cudaError_t launch_router(const RouterArgs &a, cudaStream_t s) {
-    const int wpb = 2;
-    const int grid = (a.NE + wpb - 1) / wpb;
-    const int fused = a.n_tok <= 32;
-    router_kernel<<<grid, 32 * wpb, 0, s>>>(a, fused);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess || fused) return e;
-    topk_kernel<<<(a.n_tok + 7) / 8, 256, 0, s>>>(a);
-    return cudaGetLastError();
+bool gate_up_fuses_topk(int E, int F, int U, int n_tok, int sm_count) {
+    const int NB = E / 128, WB = NB < 16 ? NB : 16, RG = 16 / WB;
+    const int UPS = (F / 8 + RG - 1) / RG;
+    const long long units = (long long)n_tok * U * UPS;
+    if (units == 0) return false;
+    const long long grid = units < sm_count ? units : sm_count;
+    const long long per_cta = (units + grid - 1) / grid;
+    const long long per_tok = (long long)U * UPS;
+    return (per_cta + per_tok - 1) / per_tok + 1 <= 8;
 }
 
-cudaError_t launch_gate_up(const GateUpArgs &a, int sm_count, cudaStream_t s) {
+cudaError_t launch_router(const RouterArgs &a, cudaStream_t s, bool pdl, bool with_topk) {
+    const int grid = (a.NE + kRouterWarps - 1) / kRouterWarps;
+    const int smem = kRouterTok * a.E * 4;
+    cudaError_t e;
+    if (a.E <= 2048) {
+        e = set_smem<router_kernel<16>, kRouterTok * 4096 * 4>();
+        if (e == cudaSuccess) e = launch(router_kernel<16>, grid, 32 * kRouterWarps, smem, s, pdl, a);
+    } else {
+        e = set_smem<router_kernel<32>, kRouterTok * 4096 * 4>();
+        if (e == cudaSuccess) e = launch(router_kernel<32>, grid, 32 * kRouterWarps, smem, s, pdl, a);
+    }
+    if (e != cudaSuccess || !with_topk) return e;
+    return launch(topk_kernel, (a.n_tok + 7) / 8, 256, 0, s, pdl, a);
+}
+
+cudaError_t launch_gate_up(const GateUpArgs &a, int sm_count, cudaStream_t s, bool pdl) {
+    constexpr int NC = kCodebookCopies;
     const int NB = a.E / 128;
-    if (NB <= 16) { GX_TYPE_SWITCH(a.type, return (gate_up_t<T, 1>(a, sm_count, s))) }
-    if (NB <= 32) { GX_TYPE_SWITCH(a.type, return (gate_up_t<T, 2>(a, sm_count, s))) }
+    if (NB <= 16) { GX_TYPE_SWITCH(a.type, return (gate_up_t<T, 1, NC>(a, sm_count, s, pdl))) }
+    if (NB <= 32) { GX_TYPE_SWITCH(a.type, return (gate_up_t<T, 2, NC>(a, sm_count, s, pdl))) }
     return cudaErrorInvalidValue;
 }
 
-cudaError_t launch_down(const DownArgs &a, int sm_count, cudaStream_t s) {
+cudaError_t launch_down(const DownArgs &a, int sm_count, cudaStream_t s, bool pdl) {
+    constexpr int NC = kCodebookCopies;
     const int npair = a.U * (a.F / 128);
-    if (npair <= 16) { GX_TYPE_SWITCH(a.type, return (down_t<T, 1>(a, sm_count, s))) }
-    if (npair <= 32) { GX_TYPE_SWITCH(a.type, return (down_t<T, 2>(a, sm_count, s))) }
-    if (npair <= 64) { GX_TYPE_SWITCH(a.type, return (down_t<T, 4>(a, sm_count, s))) }
+    if (npair <= 16) { GX_TYPE_SWITCH(a.type, return (down_t<T, 1, NC>(a, sm_count, s, pdl))) }
+    if (npair <= 32) { GX_TYPE_SWITCH(a.type, return (down_t<T, 2, NC>(a, sm_count, s, pdl))) }
+    if (npair <= 64) { GX_TYPE_SWITCH(a.type, return (down_t<T, 4, NC>(a, sm_count, s, pdl))) }
     return cudaErrorInvalidValue;
 }
 
@@ -830,3 +1077,15 @@ cudaError_t launch_residual_copy(const void *x, int x_bf16, float *out, size_t n
 }
 
 }  // namespace gx
+
+#ifdef GX_TRACE
+// Trace readout for instrumented builds only (not part of the C ABI of include/gyro_moe.h).
+extern "C" __attribute__((visibility("default"))) int gx_trace_read(long long *out, int clear) {
+    if (cudaMemcpyFromSymbol(out, gx::gx_trace, sizeof(gx::gx_trace)) != cudaSuccess) return -1;
+    if (clear) {
+        static long long zeros[gx::kTraceKernels][gx::kTraceCtas][gx::kTracePoints] = {};
+        if (cudaMemcpyToSymbol(gx::gx_trace, zeros, sizeof(zeros)) != cudaSuccess) return -1;
+    }
+    return 0;
+}
+#endif

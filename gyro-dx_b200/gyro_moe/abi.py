@@ -76,6 +76,7 @@ SIGNATURES = {
     "gx_upload_matrix": [_P, _U32, _U32, _U32, _P, _U64, ctypes.POINTER(_U32), _U32],
     "gx_matvec": [_P, _U32, _P, _U32, _P, ctypes.POINTER(_U64)],
     "gx_read_timings": [_P, ctypes.POINTER(Timings)],
+    "gx_set_flags": [_P, _U32],
     "gx_destroy": [_P, _U32],
 }
 
@@ -230,6 +231,9 @@ class Context:
         t = ctypes.c_uint64()
         _check(self.lib.gx_poll(self.handle, ctypes.byref(t)), "gx_poll")
         return t.value
+
+    def set_flags(self, flags: int) -> None:
+        _check(self.lib.gx_set_flags(self.handle, flags), "gx_set_flags")
 
     def timings(self) -> Timings:
         t = Timings()

@@ -155,10 +155,13 @@ GX_API gx_result gx_moe_forward_host(gx_context *context, uint32_t layer, const 
                                      uint32_t n_tok, void *y, uint32_t y_dtype, uint32_t *ids,
                                      float *weights, uint32_t timeout_ms);
 
-/* A stack of consecutive layers with a residual between them, x_{l+1} = x_l + MoE_l(x_l), for
- * n_tok tokens (the benchmark stand-in for the hyper-connection mixer between layers, which
- * lies outside this ABI). Device pointers; replayed from a CUDA graph after the first call
- * with the same (first_layer, n_layers, n_tok, dtypes). */
+/* A stack of consecutive layers with a pre-norm residual between them,
+ *   x_{l+1} = x_l + MoE_l(RMSNorm(x_l)),  RMSNorm(x) = x / sqrt(mean(x^2) + 1e-6) (unit weight,
+ *   src/kernels.zig:281-291),
+ * for n_tok tokens: the benchmark stand-in for the norm and hyper-connection mixer between the
+ * reference model's layers, which lie outside this ABI. Device pointers; the chain of kernels is
+ * captured into a CUDA graph on the first call and replayed on later calls with the same
+ * (first_layer, n_layers, n_tok, dtypes, flags). */
 GX_API gx_result gx_stack_forward(gx_context *context, uint32_t first_layer, uint32_t n_layers,
                                   const void *x, uint32_t x_dtype, uint32_t n_tok, void *y,
                                   uint32_t y_dtype, uint64_t *out_ticket);
@@ -197,6 +200,10 @@ GX_API gx_result gx_matvec(gx_context *context, uint32_t handle, const float *x,
                            float *y, uint64_t *out_ticket);
 
 GX_API gx_result gx_read_timings(gx_context *context, gx_timings *out_timings);
+
+/* Replaces the context's GX_FLAG_* set (e.g. to switch phase timing on for a profiled replay).
+ * Phase events serialise the kernels they separate, so timed calls should run without it. */
+GX_API gx_result gx_set_flags(gx_context *context, uint32_t flags);
 
 /* Closes the context (replaces gd_destroy, native/include/gyro_native.h:137). Waits up to
  * timeout_ms for queued work; on GX_E_TIMEOUT the context stays valid. */

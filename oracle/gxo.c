@@ -328,6 +328,14 @@ void gxo_decode_row_fast(uint32_t type_id, const uint8_t *row, float *out, size_
     for (size_t b = 0; b < cols / 128; ++b) decode_block(type_id, steps, bb, row + b * (size_t)bb, out + b * 128);
 }
 
+/* src/kernels.zig:281-291 (weight = 1) */
+void gxo_rms_norm(float *out, const float *x, size_t n, float eps) {
+    float ss = 0;
+    for (size_t i = 0; i < n; ++i) ss += x[i] * x[i];
+    const float scale = 1.0f / sqrtf(ss / (float)n + eps);
+    for (size_t i = 0; i < n; ++i) out[i] = x[i] * scale;
+}
+
 /* src/kernels.zig:340-349 */
 void gxo_softmax(float *x, size_t n) {
     float m = -INFINITY;

