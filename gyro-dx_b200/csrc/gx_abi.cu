@@ -6,6 +6,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <algorithm>
 #include <map>
 #include <thread>
 #include <tuple>
@@ -18,6 +19,9 @@
 namespace {
 
 constexpr int kEvents = 64;
+// Token count from which a forward call takes the tensor-core prefill path (grouped GEMM over
+// expert row tiles) instead of the per-slot decode GEMVs.
+constexpr uint32_t kPrefillMinTokens = 64;
 // RMSNorm epsilon of the stack's pre-norm residual x_{l+1} = x_l + MoE_l(RMSNorm(x_l)).
 constexpr float kStackNormEps = 1e-6f;
 
@@ -52,6 +56,16 @@ struct gx_context {
     // scratch sized for max_tokens
     float *logits = nullptr, *weights = nullptr, *act = nullptr, *xbuf[2] = {nullptr, nullptr};
     float *xscale = nullptr, *ss = nullptr;
+    // prefill buffers, sized on first use for the largest (E, F, U, NE) seen
+    struct Prefill {
+        size_t max_tiles = 0, E = 0, F = 0, slots = 0;
+        uint8_t *A = nullptr, *A2 = nullptr;
+        float *act = nullptr;
+        __half *Y = nullptr;
+        int *ints = nullptr;  // expert_count | tile_expert | tile_rows | n_mtiles | row_slot | slot_row
+        int *expert_count = nullptr, *tile_expert = nullptr, *tile_rows = nullptr, *n_mtiles = nullptr;
+        int *row_slot = nullptr, *slot_row = nullptr;
+    } pf;
     uint32_t *ids = nullptr;
     int *err = nullptr;
     void *x_stage = nullptr, *y_stage = nullptr;     // device staging (graphs, host calls)
@@ -169,6 +183,8 @@ void release_all(gx_context *c) {
     }
     c->graphs.clear();
     for (auto &l : c->layers) if (l.arena) cudaFree(l.arena);
+    void *pf[] = {c->pf.A, c->pf.A2, c->pf.act, c->pf.Y, c->pf.ints};
+    for (void *p : pf) if (p) cudaFree(p);
     for (auto &m : c->mats) if (m.tiles) cudaFree(m.tiles);
     void *dev[] = {c->codebook, c->logits, c->weights, c->xscale, c->ss, c->ids, c->act, c->xbuf[0], c->xbuf[1],
                    c->x_stage, c->y_stage, c->err};
@@ -183,7 +199,6 @@ void release_all(gx_context *c) {
 
 size_t dtype_size(uint32_t dt) { return dt == GX_BF16 ? 2 : 4; }
 
-// One routed layer: router + top-k, gate/up + SwiGLU, down + combine (+ residual).
 // Phase event: a plain record on the stream, or an event-record node (external record) while
 // the stream is being captured into a graph (a plain record there only orders graph nodes).
 cudaError_t record_phase(cudaEvent_t ev, cudaStream_t s) {
@@ -194,12 +209,166 @@ cudaError_t record_phase(cudaEvent_t ev, cudaStream_t s) {
                                                : cudaEventRecord(ev, s);
 }
 
+// Prefill buffers for max_tokens tokens of a layer shape. Rows are padded per expert to
+// 128-row tiles: at most slots/128 + min(NE, slots) tiles.
+gx_result ensure_prefill(gx_context *c, const Layer &L) {
+    const size_t slots = (size_t)c->max_tokens * L.U;
+    const size_t tiles = (slots + 127) / 128 + std::min<size_t>(L.local_experts, slots);
+    auto &p = c->pf;
+    if (p.max_tiles >= tiles && p.E >= L.E && p.F >= L.F && p.slots >= slots) return GX_OK;
+    void *old[] = {p.A, p.A2, p.act, p.Y, p.ints};
+    bool had = false;
+    for (void *q : old) if (q) { cudaFree(q); had = true; }
+    p = gx_context::Prefill{};
+    if (had) {  // captured stacks point at the old buffers
+        for (auto &kv : c->graphs) {
+            cudaGraphExecDestroy(kv.second.second);
+            cudaGraphDestroy(kv.second.first);
+        }
+        c->graphs.clear();
+    }
+    GX_CUDA(cudaMalloc(&p.A, tiles * (L.E / 64) * 16384));
+    GX_CUDA(cudaMalloc(&p.A2, tiles * (L.F / 64) * 16384));
+    GX_CUDA(cudaMalloc(&p.act, tiles * 128 * L.F * sizeof(float)));
+    GX_CUDA(cudaMalloc(&p.Y, tiles * 128 * L.E * sizeof(__half)));
+    const size_t n_ints = 512 + 2 * tiles + 1 + tiles * 128 + slots;
+    GX_CUDA(cudaMalloc(&p.ints, n_ints * sizeof(int)));
+    p.expert_count = p.ints;
+    p.tile_expert = p.expert_count + 512;
+    p.tile_rows = p.tile_expert + tiles;
+    p.n_mtiles = p.tile_rows + tiles;
+    p.row_slot = p.n_mtiles + 1;
+    p.slot_row = p.row_slot + tiles * 128;
+    p.max_tiles = tiles;
+    p.E = L.E;
+    p.F = L.F;
+    p.slots = slots;
+    return GX_OK;
+}
+
+// Many-token layer on tensor cores: router GEMM, per-token selection, grouping, packed f16
+// operand tiles, two grouped tcgen05 GEMMs with trellis decoding, combine.
+// ev (GX_FLAG_PROFILE): start, after selection/grouping/packing, after the gate/up GEMM, end.
+gx_result enqueue_layer_prefill(gx_context *c, const Layer &L, const void *x, uint32_t x_dtype, uint32_t n_tok,
+                                const void *resid, uint32_t resid_dtype, void *out, uint32_t out_dtype,
+                                float norm_eps, cudaEvent_t *ev) {
+    gx_result r = ensure_prefill(c, L);
+    if (r != GX_OK) return r;
+    auto &p = c->pf;
+    const int xb = x_dtype == GX_BF16;
+    if (ev) GX_CUDA(record_phase(ev[0], c->stream));
+    GX_CUDA(gx::launch_router_gemm(L.router, x, xb, (int)n_tok, (int)L.n_expert, (int)L.E, c->logits, c->stream));
+    gx::RouterArgs ra{};
+    ra.W = L.router;
+    ra.bias = L.bias;
+    ra.x = x;
+    ra.x_bf16 = xb;
+    ra.n_tok = (int)n_tok;
+    ra.NE = (int)L.n_expert;
+    ra.E = (int)L.E;
+    ra.U = (int)L.U;
+    ra.scale = L.scale;
+    ra.norm_eps = norm_eps;
+    ra.ss = c->ss;
+    ra.ss_from_x = 1;
+    ra.xscale = c->xscale;
+    ra.logits = c->logits;
+    ra.ids = c->ids;
+    ra.weights = c->weights;
+    ra.err = c->err;
+    GX_CUDA(gx::launch_topk(ra, c->stream));
+    gx::GroupArgs ga{};
+    ga.ids = c->ids;
+    ga.n_slots = (int)(n_tok * L.U);
+    ga.NE = (int)L.local_experts;
+    ga.expert_count = p.expert_count;
+    ga.tile_expert = p.tile_expert;
+    ga.tile_rows = p.tile_rows;
+    ga.n_mtiles = p.n_mtiles;
+    ga.row_slot = p.row_slot;
+    ga.slot_row = p.slot_row;
+    ga.err = c->err;
+    GX_CUDA(gx::launch_group(ga, c->stream));
+    gx::PackArgs pa{};
+    pa.src = x;
+    pa.src_bf16 = xb;
+    pa.by_token = 1;
+    pa.U = (int)L.U;
+    pa.K = (int)L.E;
+    pa.xscale = norm_eps > 0.f ? c->xscale : nullptr;
+    pa.signs = L.gate_signs;
+    pa.row_slot = p.row_slot;
+    pa.tile_rows = p.tile_rows;
+    pa.n_mtiles = p.n_mtiles;
+    pa.dst = p.A;
+    GX_CUDA(gx::launch_pack_rows(pa, (int)p.max_tiles, c->stream));
+    if (ev) GX_CUDA(record_phase(ev[1], c->stream));
+    gx::GemmArgs gm{};
+    gm.type = L.type;
+    gm.w0 = L.gate;
+    gm.w1 = L.up;
+    gm.expert_bytes = L.gate_expert_bytes;
+    gm.K = (int)L.E;
+    gm.n_ntiles = (int)(L.F / 128);
+    gm.n_expert = (int)L.local_experts;
+    gm.A = p.A;
+    gm.tile_expert = p.tile_expert;
+    gm.tile_rows = p.tile_rows;
+    gm.n_mtiles = p.n_mtiles;
+    gm.act = p.act;
+    gm.F = (int)L.F;
+    gm.Y = p.Y;
+    gm.E = (int)L.E;
+    gm.codebook = c->codebook;
+    gm.err = c->err;
+    GX_CUDA(gx::launch_moe_gemm(gm, 0, c->sm_count, c->stream));
+    if (ev) GX_CUDA(record_phase(ev[2], c->stream));
+    gx::PackArgs pd{};
+    pd.src = p.act;
+    pd.src_bf16 = 0;
+    pd.by_token = 0;
+    pd.U = (int)L.U;
+    pd.K = (int)L.F;
+    pd.signs = L.down_signs;
+    pd.row_slot = p.row_slot;
+    pd.tile_rows = p.tile_rows;
+    pd.n_mtiles = p.n_mtiles;
+    pd.dst = p.A2;
+    GX_CUDA(gx::launch_pack_rows(pd, (int)p.max_tiles, c->stream));
+    gm.w0 = L.down;
+    gm.w1 = nullptr;
+    gm.expert_bytes = L.down_expert_bytes;
+    gm.K = (int)L.F;
+    gm.n_ntiles = (int)(L.E / 256);
+    gm.A = p.A2;
+    GX_CUDA(gx::launch_moe_gemm(gm, 1, c->sm_count, c->stream));
+    gx::CombineArgs ca{};
+    ca.Y = p.Y;
+    ca.slot_row = p.slot_row;
+    ca.weights = c->weights;
+    ca.resid = resid;
+    ca.resid_bf16 = resid_dtype == GX_BF16;
+    ca.out = out;
+    ca.out_bf16 = out_dtype == GX_BF16;
+    ca.n_tok = (int)n_tok;
+    ca.U = (int)L.U;
+    ca.E = (int)L.E;
+    GX_CUDA(gx::launch_combine(ca, c->stream));
+    if (ev) GX_CUDA(record_phase(ev[3], c->stream));
+    return GX_OK;
+}
+
+// One routed layer: router + top-k, gate/up + SwiGLU, down + combine (+ residual).
 // prof_slot >= 0 records the phase events of layer slot prof_slot (GX_FLAG_PROFILE).
 // norm_eps > 0 routes and feeds the experts RMSNorm(x) (unit weight); the residual stays x.
 // chained: the previous operation on the stream is this library's down kernel.
 gx_result enqueue_layer(gx_context *c, const Layer &L, const void *x, uint32_t x_dtype, uint32_t n_tok,
                         const void *resid, uint32_t resid_dtype, void *out, uint32_t out_dtype, int prof_slot,
                         float norm_eps, bool chained) {
+    if (n_tok >= kPrefillMinTokens && L.n_expert <= 512 && L.E % 256 == 0) {
+        cudaEvent_t *pev = prof_slot >= 0 ? &c->prof[4 * (size_t)prof_slot] : nullptr;
+        return enqueue_layer_prefill(c, L, x, x_dtype, n_tok, resid, resid_dtype, out, out_dtype, norm_eps, pev);
+    }
     cudaEvent_t *ev = prof_slot >= 0 ? &c->prof[4 * (size_t)prof_slot] : nullptr;
     if (ev) GX_CUDA(record_phase(ev[0], c->stream));
     gx::RouterArgs ra{};

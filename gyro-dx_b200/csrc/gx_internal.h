@@ -1,6 +1,7 @@
 // gx_internal.h — launchers shared between the kernels (gx_kernels.cu) and the C ABI
 // (gx_abi.cu). Host-only declarations.
 #pragma once
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -19,6 +20,7 @@ struct RouterArgs {
     float scale;             // expert_weights_scale
     float norm_eps;          // > 0: route RMSNorm(x) (unit weight)
     float *ss;               // [n_tok] sum of squares of x (written when norm_eps > 0)
+    int ss_from_x;           // selection computes the sum of squares from x itself (prefill)
     float *xscale;           // [n_tok] per-token input scale (written by topk_kernel)
     float *logits;           // [n_tok][NE] scratch (raw W x, before scale and bias)
     uint32_t *ids;           // [n_tok][U]
@@ -72,6 +74,62 @@ struct DownArgs {
     int *err;
 };
 
+// ---- prefill (many tokens): grouping, row packing, tcgen05 grouped GEMM, combine ----------
+struct GroupArgs {
+    const uint32_t *ids;     // [n_slots] expert of each slot (local numbering)
+    int n_slots, NE;
+    int *expert_count;       // [NE]
+    int *tile_expert;        // [max_tiles] expert of each 128-row tile
+    int *tile_rows;          // [max_tiles] valid rows in the tile
+    int *n_mtiles;           // [1]
+    int *row_slot;           // [max_tiles * 128] slot of each valid padded row
+    int *slot_row;           // [n_slots] padded row of each slot
+    int *err;
+};
+
+struct PackArgs {
+    const void *src;         // by_token: x [n_tok][K]; else act [padded rows][K]
+    int src_bf16;
+    int by_token, U, K;
+    const float *xscale;     // [n_tok] or nullptr (by_token only)
+    const float *signs;      // [K] or nullptr (then no Hadamard transform)
+    const int *row_slot, *tile_rows, *n_mtiles;
+    uint8_t *dst;            // [tiles][K/64][16384] f16 swizzled
+};
+
+struct GemmArgs {
+    uint32_t type;
+    const uint8_t *w0, *w1;  // gate + up (mode 0) or down (mode 1) tiles of local expert 0
+    uint64_t expert_bytes;   // tiles of one projection of one expert
+    int K, n_ntiles, n_expert;
+    const uint8_t *A;        // packed operand tiles [tile][K/64][16384]
+    const int *tile_expert, *tile_rows, *n_mtiles;
+    float *act;              // mode 0 output [tiles*128][F]
+    int F;
+    __half *Y;               // mode 1 output [tiles*128][E]
+    int E;
+    const uint32_t *codebook;
+    int *err;
+};
+
+struct CombineArgs {
+    const __half *Y;
+    const int *slot_row;
+    const float *weights;
+    const void *resid;
+    int resid_bf16;
+    void *out;
+    int out_bf16;
+    int n_tok, U, E;
+};
+
+cudaError_t launch_router_gemm(const float *W, const void *x, int x_bf16, int n_tok, int NE, int E, float *C,
+                               cudaStream_t s);
+cudaError_t launch_group(const GroupArgs &a, cudaStream_t s);
+cudaError_t launch_pack_rows(const PackArgs &a, int max_tiles, cudaStream_t s);
+cudaError_t launch_moe_gemm(const GemmArgs &a, int mode, int sm_count, cudaStream_t s);
+cudaError_t launch_combine(const CombineArgs &a, cudaStream_t s);
+
 struct MatvecArgs {
     uint32_t type;
     const uint8_t *tiles;
@@ -85,6 +143,8 @@ struct MatvecArgs {
 // pdl: launch with programmatic stream serialization (overlap with the previous kernel).
 // with_topk: also launch the per-token selection kernel (when gate_up does not fuse it).
 cudaError_t launch_router(const RouterArgs &a, cudaStream_t s, bool pdl, bool with_topk);
+// Per-token selection (one warp per token) from raw logits.
+cudaError_t launch_topk(const RouterArgs &a, cudaStream_t s);
 cudaError_t launch_gate_up(const GateUpArgs &a, int sm_count, cudaStream_t s, bool pdl);
 cudaError_t launch_down(const DownArgs &a, int sm_count, cudaStream_t s, bool pdl);
 cudaError_t launch_matvec(const MatvecArgs &a, int sm_count, cudaStream_t s);

@@ -112,7 +112,23 @@ __device__ __forceinline__ void rotated_block_to_smem(const void *src, int bf16,
 // expert_weights_scale (src/engine.zig:533-539).
 __device__ void topk_token(const RouterArgs &a, int t, int lane) {
     const float *row = a.logits + (size_t)t * a.NE;
-    const float scale = a.norm_eps > 0.f ? 1.0f / sqrtf(__ldcg(a.ss + t) / (float)a.E + a.norm_eps) : 1.f;
+    float ss = 0.f;
+    if (a.norm_eps > 0.f) {
+        if (a.ss_from_x) {
+            for (int i = 4 * lane; i < a.E; i += 128) {
+                float v[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) v[j] = load_act(a.x, a.x_bf16, (size_t)t * a.E + i + j);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) ss = fmaf(v[j], v[j], ss);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        } else {
+            ss = __ldcg(a.ss + t);
+        }
+    }
+    const float scale = a.norm_eps > 0.f ? 1.0f / sqrtf(ss / (float)a.E + a.norm_eps) : 1.f;
     float v[16];
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
@@ -1027,6 +1043,11 @@ cudaError_t launch_router(const RouterArgs &a, cudaStream_t s, bool pdl, bool wi
     }
     if (e != cudaSuccess || !with_topk) return e;
     return launch(topk_kernel, (a.n_tok + 7) / 8, 256, 0, s, pdl, a);
+}
+
+cudaError_t launch_topk(const RouterArgs &a, cudaStream_t s) {
+    if (a.n_tok == 0) return cudaSuccess;
+    return launch(topk_kernel, (a.n_tok + 7) / 8, 256, 0, s, false, a);
 }
 
 cudaError_t launch_gate_up(const GateUpArgs &a, int sm_count, cudaStream_t s, bool pdl) {

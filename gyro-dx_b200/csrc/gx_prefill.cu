@@ -1,0 +1,524 @@
+// gx_prefill.cu — the many-token (prefill) path of the routed layer on sm_100a tensor cores.
+//
+//   router_gemm_kernel   logits = X W_r^T in fp32 on CUDA cores (tiled SGEMM), raw (before the
+//                        RMSNorm scale and bias, which the selection applies)
+//   group_kernel         count / prefix / stable fill of slots by expert (src/engine.zig:553-564),
+//                        expert segments padded to 128-row tiles
+//   pack_rows_kernel     gathers token rows per tile, applies scale, signs and the 128-point
+//                        Hadamard transform, writes f16 operand tiles in the 128-byte-swizzled
+//                        K-major layout the tensor core reads
+//   moe_gemm_kernel      grouped GEMM per (expert row tile, weight column tile): decoder warps
+//                        expand Gyro trellis codes into f16 B tiles in shared memory, one thread
+//                        issues tcgen05.mma into a TMEM accumulator, epilogue warps read TMEM:
+//                        gate/up -> SwiGLU, down -> f16 rows
+//   combine_kernel       weighted un-permute of the down rows (src/engine.zig:634-641) + residual
+//
+// f16 is used for both operands: every codebook value is exact in f16, d * CB is rounded once
+// (2^-11 relative), activations keep 11 mantissa bits; accumulation is f32 in TMEM.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "gx_device.cuh"
+#include "gx_internal.h"
+#include "gx_umma.cuh"
+
+namespace gx {
+
+// ------------------------------------------------------------------------------------------
+// Router GEMM: C[t][e] = sum_c X[t][c] W[e][c]. CTA tile 64 tokens x 32 experts, 256 threads,
+// each 4 tokens x 2 experts, K chunks of 32 staged in shared memory.
+// ------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) router_gemm_kernel(const float *__restrict__ W, const void *__restrict__ x,
+                                                          int x_bf16, int n_tok, int NE, int E, float *__restrict__ C) {
+    __shared__ __align__(16) float xs[32][64 + 4];
+    __shared__ __align__(16) float ws[32][32 + 4];
+    const int t0 = blockIdx.y * 64, e0 = blockIdx.x * 32;
+    const int tid = threadIdx.x;
+    const int tt = (tid & 15) * 4, ee = (tid >> 4) * 2;
+    float acc[4][2] = {};
+    for (int k0 = 0; k0 < E; k0 += 32) {
+        // x tile: 64 tokens x 32 columns (8 per thread)
+        for (int i = tid; i < 64 * 32; i += 256) {
+            const int r = i >> 5, c = i & 31;
+            const int t = t0 + r;
+            xs[c][r] = t < n_tok ? load_act(x, x_bf16, (size_t)t * E + k0 + c) : 0.f;
+        }
+        for (int i = tid; i < 32 * 32; i += 256) {
+            const int r = i >> 5, c = i & 31;
+            ws[c][r] = e0 + r < NE ? W[(size_t)(e0 + r) * E + k0 + c] : 0.f;
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int k = 0; k < 32; ++k) {
+            const float4 xv = *reinterpret_cast<const float4 *>(&xs[k][tt]);
+            const float2 wv = *reinterpret_cast<const float2 *>(&ws[k][ee]);
+            acc[0][0] = fmaf(xv.x, wv.x, acc[0][0]); acc[0][1] = fmaf(xv.x, wv.y, acc[0][1]);
+            acc[1][0] = fmaf(xv.y, wv.x, acc[1][0]); acc[1][1] = fmaf(xv.y, wv.y, acc[1][1]);
+            acc[2][0] = fmaf(xv.z, wv.x, acc[2][0]); acc[2][1] = fmaf(xv.z, wv.y, acc[2][1]);
+            acc[3][0] = fmaf(xv.w, wv.x, acc[3][0]); acc[3][1] = fmaf(xv.w, wv.y, acc[3][1]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int t = t0 + tt + i, e = e0 + ee + j;
+            if (t < n_tok && e < NE) C[(size_t)t * NE + e] = acc[i][j];
+        }
+}
+
+// ------------------------------------------------------------------------------------------
+// Grouping: one CTA of 1024 threads. Stable order of slots within each expert (the counting
+// sort of src/engine.zig:553-564), each expert's rows padded to whole 128-row tiles.
+// ------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024) group_kernel(GroupArgs a) {
+    extern __shared__ __align__(16) int gsm[];
+    int *count = gsm;                 // [NE]
+    int *tile_base = count + a.NE;    // [NE + 1]
+    int *run = tile_base + a.NE + 1;  // [NE] rows placed so far
+    int *wcount = run + a.NE;         // [32][NE] per-warp counts of the current chunk
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int e = tid; e < a.NE; e += 1024) { count[e] = 0; run[e] = 0; }
+    __syncthreads();
+    for (int s = tid; s < a.n_slots; s += 1024) {
+        const uint32_t e = a.ids[s];
+        if (e < (uint32_t)a.NE) atomicAdd(&count[e], 1);
+        else atomicExch(a.err, KERR_BOUNDS);
+    }
+    __syncthreads();
+    if (tid == 0) {
+        int acc = 0;
+        for (int e = 0; e < a.NE; ++e) {
+            tile_base[e] = acc;
+            a.expert_count[e] = count[e];
+            acc += (count[e] + 127) / 128;
+        }
+        tile_base[a.NE] = acc;
+        *a.n_mtiles = acc;
+    }
+    __syncthreads();
+    for (int e = tid; e < a.NE; e += 1024) {
+        const int n = (count[e] + 127) / 128;
+        for (int m = 0; m < n; ++m) {
+            a.tile_expert[tile_base[e] + m] = e;
+            a.tile_rows[tile_base[e] + m] = min(128, count[e] - m * 128);
+        }
+    }
+    for (int base = 0; base < a.n_slots; base += 1024) {
+        for (int i = tid; i < 32 * a.NE; i += 1024) wcount[i] = 0;
+        __syncthreads();
+        const int s = base + tid;
+        const bool live = s < a.n_slots;
+        const uint32_t e = live ? a.ids[s] : 0xffffffffu;
+        const bool ok = live && e < (uint32_t)a.NE;
+        const unsigned same = __match_any_sync(0xffffffffu, ok ? e : 0xffffffffu);
+        const int rank_w = __popc(same & ((1u << lane) - 1u));
+        if (ok && rank_w == 0) wcount[warp * a.NE + e] = __popc(same);
+        __syncthreads();
+        if (ok) {
+            int before = run[e] + rank_w;
+            for (int w = 0; w < warp; ++w) before += wcount[w * a.NE + e];
+            const int row = tile_base[e] * 128 + before;
+            a.row_slot[row] = s;
+            a.slot_row[s] = row;
+        }
+        __syncthreads();
+        for (int e2 = tid; e2 < a.NE; e2 += 1024) {
+            int add = 0;
+            for (int w = 0; w < 32; ++w) add += wcount[w * a.NE + e2];
+            run[e2] += add;
+        }
+        __syncthreads();
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// Row packing: one warp per (padded row, 128-column block). Source row = token of the slot
+// (gate/up input, x) or the padded row itself (down input, act). v = src * scale, * signs, then
+// H128 / sqrt(128) when signs are given; f16 into the swizzled K-major tile layout
+// [tile][K/64][128 rows x 64 cols].
+// ------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) pack_rows_kernel(PackArgs a) {
+    const int lane = threadIdx.x & 31;
+    const long long wid = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int nb = a.K / 128;
+    const long long row = wid / nb;
+    const int b = (int)(wid % nb);
+    const int n_rows = *a.n_mtiles * 128;
+    if (row >= n_rows) return;
+    const int t = (int)(row >> 7), i = (int)(row & 127);
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    if (i < a.tile_rows[t]) {
+        size_t src_row;
+        float sc = 1.f;
+        if (a.by_token) {
+            const int slot = a.row_slot[row];
+            const int tok = slot / a.U;
+            src_row = (size_t)tok;
+            if (a.xscale) sc = a.xscale[tok];
+        } else {
+            src_row = (size_t)row;
+        }
+        const size_t base = src_row * a.K + b * 128 + 4 * lane;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            v[j] = load_act(a.src, a.src_bf16, base + j) * sc;
+            if (a.signs) v[j] *= a.signs[b * 128 + 4 * lane + j];
+        }
+        if (a.signs) fwht128_warp(v, lane);
+    }
+    // lane holds columns 4*lane .. +3 of the block: k-step 2b + lane/16, columns 4*(lane%16)..
+    const int ks = 2 * b + (lane >> 4), col = 4 * (lane & 15);
+    uint8_t *tile = a.dst + ((size_t)t * (a.K / 64) + ks) * 16384u;
+    uint2 w;
+    w.x = pack_half2(v[0], v[1]);
+    w.y = pack_half2(v[2], v[3]);
+    *reinterpret_cast<uint2 *>(tile + sw128_offset((uint32_t)i, (uint32_t)col)) = w;
+}
+
+// ------------------------------------------------------------------------------------------
+// Grouped GEMM on tcgen05. 448 threads: warp 0 loads A tiles (bulk copies), warp 1 owns TMEM
+// and issues the MMAs, warps 2-9 decode B tiles (one weight row per thread per 64-column
+// step), warps 10-13 drain the accumulator. Work item = (row tile, column tile); the
+// accumulator is double-buffered in TMEM (2 x 256 columns).
+// MODE 0: B rows = 128 gate rows + 128 up rows of F-columns [nt*128, +128); epilogue writes
+//         act = silu(g) * u (f32) per padded row. MODE 1: B rows = 256 down rows
+//         [nt*256, +256); epilogue writes f16 rows of the expert output.
+// ------------------------------------------------------------------------------------------
+constexpr int kGemmStages = 3;
+constexpr int kGemmCopies = 8;
+constexpr int kStageBytes = 16384 + 32768;
+constexpr int kGemmThreads = 448;
+
+struct GemmSmem {
+    static constexpr int A = 0;                                   // per stage +kStageBytes
+    static constexpr int B = 16384;
+    static constexpr int CB = kGemmStages * kStageBytes;
+    static constexpr int BARS = CB + Codebook<kGemmCopies>::BYTES;
+    static constexpr int BYTES = BARS + 256;
+};
+
+template <uint32_t T, int MODE>
+__global__ void __launch_bounds__(kGemmThreads, 1) moe_gemm_kernel(GemmArgs a) {
+    using CBk = Codebook<kGemmCopies>;
+    extern __shared__ __align__(1024) uint8_t gsmem_raw[];
+    // 1024-byte alignment of the operand tiles (the swizzle pattern is address based)
+    uint8_t *sm = reinterpret_cast<uint8_t *>(((uintptr_t)gsmem_raw + 1023) & ~(uintptr_t)1023);
+    uint32_t *cb = reinterpret_cast<uint32_t *>(sm + GemmSmem::CB);
+    uint64_t *full_a = reinterpret_cast<uint64_t *>(sm + GemmSmem::BARS);
+    uint64_t *full_b = full_a + kGemmStages;
+    uint64_t *empty = full_b + kGemmStages;
+    uint64_t *acc_full = empty + kGemmStages;
+    uint64_t *acc_empty = acc_full + 2;
+    uint64_t *done = acc_empty + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int TB = tile_bytes(T);
+    const int NB = a.K / 128;
+    const int KS = a.K / 64;
+    if (tid == 0) {
+        for (int s = 0; s < kGemmStages; ++s) {
+            mbar_init(&full_a[s], 1);
+            mbar_init(&full_b[s], 8);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 4);
+        }
+        mbar_init(done, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, 512);
+    CBk::stage(cb, a.codebook, tid, kGemmThreads);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int n_items = *a.n_mtiles * a.n_ntiles;
+
+    auto wait = [&](uint64_t *bar, uint32_t parity) -> bool {
+        if (*abort_flag) return false;
+        if (mbar_wait(bar, parity, a.err)) return true;
+        *abort_flag = 1;
+        return false;
+    };
+
+    if (warp == 0) {
+        // ---- A producer ------------------------------------------------------------------
+        if (lane == 0) {
+            int n = 0;
+            for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
+                const int t = it / a.n_ntiles;
+                for (int ks = 0; ks < KS; ++ks, ++n) {
+                    const int s = n % kGemmStages, round = n / kGemmStages;
+                    if (!wait(&empty[s], (round & 1) ^ 1)) break;
+                    mbar_expect_tx(&full_a[s], 16384);
+                    bulk_g2s(sm + s * kStageBytes + GemmSmem::A, a.A + ((size_t)t * KS + ks) * 16384u, 16384, &full_a[s]);
+                }
+                if (*abort_flag) break;
+            }
+        }
+    } else if (warp == 1) {
+        // ---- MMA issuer --------------------------------------------------------------------
+        if (lane == 0) {
+            const uint32_t idesc = f16_idesc(128, 256);
+            int n = 0, cnt = 0;
+            for (int it = blockIdx.x; it < n_items; it += gridDim.x, ++cnt) {
+                const int ab = cnt & 1;
+                if (!wait(&acc_empty[ab], ((cnt >> 1) & 1) ^ 1)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + (uint32_t)(ab * 256);
+                bool ok = true;
+                for (int ks = 0; ks < KS; ++ks, ++n) {
+                    const int s = n % kGemmStages, round = n / kGemmStages;
+                    if (!wait(&full_a[s], round & 1) || !wait(&full_b[s], round & 1)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(sm + s * kStageBytes + GemmSmem::A);
+                    const uint32_t b_addr = smem_u32(sm + s * kStageBytes + GemmSmem::B);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)
+                        umma_f16(d_tmem, sw128_desc(a_addr + 32 * k), sw128_desc(b_addr + 32 * k), idesc,
+                                 (ks | k) != 0);
+                    umma_commit(&empty[s]);
+                }
+                if (!ok) break;
+                umma_commit(&acc_full[ab]);
+            }
+            // all issued MMAs complete before TMEM is released
+            umma_commit(done);
+            mbar_wait(done, 0, nullptr);
+        }
+    } else if (warp < 10) {
+        // ---- B decoders: thread d builds row d of the 256-row B tile -----------------------
+        const int d = tid - 64;
+        const uint32_t copy_off = CBk::copy_off(lane);
+        int n = 0;
+        for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
+            const int t = it / a.n_ntiles, nt = it % a.n_ntiles;
+            uint32_t e = (uint32_t)a.tile_expert[t];
+            if (e >= (uint32_t)a.n_expert) {
+                atomicExch(a.err, KERR_BOUNDS);
+                e = 0;
+            }
+            const uint8_t *mat;
+            int row;
+            if (MODE == 0) {
+                mat = (d < 128 ? a.w0 : a.w1) + (uint64_t)e * a.expert_bytes;
+                row = nt * 128 + (d & 127);
+            } else {
+                mat = a.w0 + (uint64_t)e * a.expert_bytes;
+                row = nt * 256 + d;
+            }
+            const uint8_t *rowtiles = mat + (size_t)(row >> 3) * NB * TB;
+            const int r8 = row & 7;
+            bool ok = true;
+            for (int ks = 0; ks < KS; ++ks, ++n) {
+                const int s = n % kGemmStages, round = n / kGemmStages;
+                const int b = ks >> 1, h = ks & 1;
+                const uint8_t *tile = rowtiles + (size_t)b * TB;
+                // two own quarters (2h, 2h+1) and the neighbour run of quarter (2h+3)%4
+                uint32_t own0[4], own1[4], nbr[4];
+                load_run<T>(tile, 4 * r8 + 2 * h, own0);
+                load_run<T>(tile, 4 * r8 + 2 * h + 1, own1);
+                load_run<T>(tile, 4 * r8 + ((2 * h + 3) & 3), nbr);
+                const uint16_t dh = *reinterpret_cast<const uint16_t *>(tile + tile_code_bytes(T) + 2 * r8);
+                const __half2 d2 = __halves2half2(__ushort_as_half(dh), __ushort_as_half(dh));
+                uint32_t i0[2][8], i1[2][8];
+                quarter_indices<T>(own0, neighbour_bits<T>(nbr), i0[0], i1[0]);
+                quarter_indices<T>(own1, neighbour_bits<T>(own0), i0[1], i1[1]);
+                if (!wait(&empty[s], (round & 1) ^ 1)) { ok = false; break; }
+                uint8_t *bt = sm + s * kStageBytes + GemmSmem::B;
+#pragma unroll
+                for (int qq = 0; qq < 2; ++qq)
+#pragma unroll
+                    for (int c = 0; c < 8; c += 2) {
+                        uint32_t w[4];
+                        const uint32_t p0 = cb[CBk::word(i0[qq][c], copy_off)];
+                        const uint32_t p1 = cb[CBk::word(i1[qq][c], copy_off)];
+                        const uint32_t p2 = cb[CBk::word(i0[qq][c + 1], copy_off)];
+                        const uint32_t p3 = cb[CBk::word(i1[qq][c + 1], copy_off)];
+                        const uint32_t pp[4] = {p0, p1, p2, p3};
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const __half2 v = __hmul2(*reinterpret_cast<const __half2 *>(&pp[j]), d2);
+                            w[j] = *reinterpret_cast<const uint32_t *>(&v);
+                        }
+                        const int col = 32 * qq + 4 * c;  // 8 consecutive weights: chunk col/8
+                        *reinterpret_cast<uint4 *>(bt + sw128_offset((uint32_t)d, (uint32_t)col)) =
+                            make_uint4(w[0], w[1], w[2], w[3]);
+                    }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&full_b[s]);
+            }
+            if (!ok) break;
+        }
+    } else {
+        // ---- epilogue: warp (10..13) reads TMEM lanes 32*(warp%4) .. +31 -------------------
+        const int lg = warp & 3;
+        const int r = 32 * lg + lane;
+        int cnt = 0;
+        for (int it = blockIdx.x; it < n_items; it += gridDim.x, ++cnt) {
+            const int t = it / a.n_ntiles, nt = it % a.n_ntiles;
+            const int ab = cnt & 1;
+            if (!wait(&acc_full[ab], (cnt >> 1) & 1)) break;
+            tc_fence_after();
+            const bool valid = r < a.tile_rows[t];
+            const uint32_t base = tmem_base + ((uint32_t)(32 * lg) << 16) + (uint32_t)(ab * 256);
+            const size_t prow = (size_t)t * 128 + r;
+            if (MODE == 0) {
+                float *dst = a.act + prow * a.F + nt * 128;
+#pragma unroll 1
+                for (int j = 0; j < 8; ++j) {
+                    uint32_t g[16], u[16];
+                    tmem_ld16(base + 16 * j, g);
+                    tmem_ld16(base + 128 + 16 * j, u);
+                    tmem_wait_ld();
+                    if (valid) {
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            float4 o;
+                            o.x = silu_ref(__uint_as_float(g[4 * q + 0])) * __uint_as_float(u[4 * q + 0]);
+                            o.y = silu_ref(__uint_as_float(g[4 * q + 1])) * __uint_as_float(u[4 * q + 1]);
+                            o.z = silu_ref(__uint_as_float(g[4 * q + 2])) * __uint_as_float(u[4 * q + 2]);
+                            o.w = silu_ref(__uint_as_float(g[4 * q + 3])) * __uint_as_float(u[4 * q + 3]);
+                            *reinterpret_cast<float4 *>(dst + 16 * j + 4 * q) = o;
+                        }
+                    }
+                }
+            } else {
+                __half *dst = a.Y + prow * a.E + nt * 256;
+#pragma unroll 1
+                for (int j = 0; j < 16; ++j) {
+                    uint32_t y[16];
+                    tmem_ld16(base + 16 * j, y);
+                    tmem_wait_ld();
+                    if (valid) {
+                        uint4 o0, o1;
+                        o0.x = pack_half2(__uint_as_float(y[0]), __uint_as_float(y[1]));
+                        o0.y = pack_half2(__uint_as_float(y[2]), __uint_as_float(y[3]));
+                        o0.z = pack_half2(__uint_as_float(y[4]), __uint_as_float(y[5]));
+                        o0.w = pack_half2(__uint_as_float(y[6]), __uint_as_float(y[7]));
+                        o1.x = pack_half2(__uint_as_float(y[8]), __uint_as_float(y[9]));
+                        o1.y = pack_half2(__uint_as_float(y[10]), __uint_as_float(y[11]));
+                        o1.z = pack_half2(__uint_as_float(y[12]), __uint_as_float(y[13]));
+                        o1.w = pack_half2(__uint_as_float(y[14]), __uint_as_float(y[15]));
+                        *reinterpret_cast<uint4 *>(dst + 16 * j) = o0;
+                        *reinterpret_cast<uint4 *>(dst + 16 * j + 8) = o1;
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[ab]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, 512);
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// Combine: out[t] = sum_k w[t][k] * Y[row(t, k)] (+ resid[t]); 4 columns per thread.
+// ------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) combine_kernel(CombineArgs a) {
+    const long long i = (long long)blockIdx.x * 256 + threadIdx.x;
+    const int per_row = a.E / 4;
+    if (i >= (long long)a.n_tok * per_row) return;
+    const int t = (int)(i / per_row), c = (int)(i % per_row) * 4;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int k = 0; k < a.U; ++k) {
+        const float w = a.weights[t * a.U + k];
+        const int row = a.slot_row[t * a.U + k];
+        const uint2 q = *reinterpret_cast<const uint2 *>(a.Y + (size_t)row * a.E + c);
+        const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&q.x));
+        const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(&q.y));
+        v[0] += w * f0.x;
+        v[1] += w * f0.y;
+        v[2] += w * f1.x;
+        v[3] += w * f1.y;
+    }
+    const size_t o = (size_t)t * a.E + c;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        if (a.resid) v[j] = load_act(a.resid, a.resid_bf16, o + j) + v[j];
+        if (a.out_bf16)
+            reinterpret_cast<__nv_bfloat16 *>(a.out)[o + j] = __float2bfloat16_rn(v[j]);
+        else
+            reinterpret_cast<float *>(a.out)[o + j] = v[j];
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// Host launchers
+// ------------------------------------------------------------------------------------------
+cudaError_t launch_router_gemm(const float *W, const void *x, int x_bf16, int n_tok, int NE, int E, float *C,
+                               cudaStream_t s) {
+    dim3 grid((NE + 31) / 32, (n_tok + 63) / 64);
+    router_gemm_kernel<<<grid, 256, 0, s>>>(W, x, x_bf16, n_tok, NE, E, C);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_group(const GroupArgs &a, cudaStream_t s) {
+    const int smem = (3 * a.NE + 1 + 32 * a.NE) * 4;
+    static const cudaError_t once = cudaFuncSetAttribute(group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                         (3 * 512 + 1 + 32 * 512) * 4);
+    if (once != cudaSuccess) return once;
+    group_kernel<<<1, 1024, smem, s>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_pack_rows(const PackArgs &a, int max_tiles, cudaStream_t s) {
+    const long long warps = (long long)max_tiles * 128 * (a.K / 128);
+    if (warps == 0) return cudaSuccess;
+    pack_rows_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(a);
+    return cudaGetLastError();
+}
+
+namespace {
+template <uint32_t T, int MODE>
+cudaError_t gemm_t(const GemmArgs &a, int sm_count, cudaStream_t s) {
+    const int smem = GemmSmem::BYTES + 1024;
+    static const cudaError_t once =
+        cudaFuncSetAttribute(moe_gemm_kernel<T, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (once != cudaSuccess) return once;
+    moe_gemm_kernel<T, MODE><<<sm_count, kGemmThreads, smem, s>>>(a);
+    return cudaGetLastError();
+}
+}  // namespace
+
+cudaError_t launch_moe_gemm(const GemmArgs &a, int mode, int sm_count, cudaStream_t s) {
+#define GX_GEMM_CASE(TT)                                                                 \
+    case TT:                                                                             \
+        return mode == 0 ? gemm_t<TT, 0>(a, sm_count, s) : gemm_t<TT, 1>(a, sm_count, s);
+    switch (a.type) {
+        GX_GEMM_CASE(144)
+        GX_GEMM_CASE(145)
+        GX_GEMM_CASE(146)
+        GX_GEMM_CASE(147)
+        GX_GEMM_CASE(148)
+        GX_GEMM_CASE(149)
+        GX_GEMM_CASE(150)
+        GX_GEMM_CASE(151)
+        default:
+            return cudaErrorInvalidValue;
+    }
+#undef GX_GEMM_CASE
+}
+
+cudaError_t launch_combine(const CombineArgs &a, cudaStream_t s) {
+    const long long n = (long long)a.n_tok * (a.E / 4);
+    if (n == 0) return cudaSuccess;
+    combine_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(a);
+    return cudaGetLastError();
+}
+
+}  // namespace gx

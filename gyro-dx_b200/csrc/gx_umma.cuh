@@ -1,0 +1,86 @@
+// gx_umma.cuh — tcgen05 (5th-generation tensor core) building blocks for sm_100a: shared-memory
+// matrix descriptors, the f16 instruction descriptor, TMEM allocation, MMA issue / commit and
+// TMEM loads, as inline PTX. Bit layouts follow the PTX ISA tcgen05 descriptor formats (the
+// same fields CUTLASS names in cute/arch/mma_sm100_desc.hpp).
+#pragma once
+#include <stdint.h>
+
+#include "gx_device.cuh"
+
+namespace gx {
+
+// ---- operand tiles in shared memory: K-major, 128-byte swizzle ----------------------------
+// A tile of R rows x 64 f16 (128 bytes per row): rows in groups of 8 (1024 bytes, the swizzle
+// atom), row r of a group at byte 128 r, its 16-byte chunk c stored at chunk position c ^ r.
+// Tiles start on 1024-byte boundaries so the hardware's address-bit swizzle lines up.
+GX_HD constexpr uint32_t sw128_offset(uint32_t row, uint32_t col /* f16 column 0..63 */) {
+    return (row >> 3) * 1024u + (row & 7u) * 128u + ((((col * 2u) >> 4) ^ (row & 7u)) << 4) + ((col * 2u) & 15u);
+}
+
+// Shared-memory matrix descriptor of such a tile at byte address addr (K offset folded into
+// addr: +32 bytes per 16-column MMA step inside the 128-byte swizzle row).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((addr >> 4) & 0x3FFFu);        // start address
+    d |= (uint64_t)1u << 16;                       // leading byte offset (unused with swizzle): 16 B
+    d |= (uint64_t)(1024u >> 4) << 32;             // stride byte offset: 8-row groups 1024 B apart
+    d |= (uint64_t)1u << 46;                       // descriptor version (sm_100)
+    d |= (uint64_t)2u << 61;                       // 128-byte swizzle
+    return d;
+}
+
+// Instruction descriptor: kind::f16, A and B f16, K-major, D f32, M x N.
+GX_HD constexpr uint32_t f16_idesc(uint32_t M, uint32_t N) {
+    return (1u << 4)             // D format f32
+         | (0u << 7)             // A f16
+         | (0u << 10)            // B f16
+         | ((N >> 3) << 17)      // N / 8
+         | ((M >> 4) << 24);     // M / 16
+}
+
+// ---- TMEM --------------------------------------------------------------------------------
+// Allocation by one full warp; the base address is written to shared memory at slot.
+__device__ __forceinline__ void tmem_alloc(uint32_t *slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t base, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// D[tmem] (+)= A[smem] x B[smem]^T, one thread issues.
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// mbarrier arrive once all previously issued tcgen05 ops of this thread have completed.
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+// 32 lanes x 16 consecutive 32-bit columns (warp w reads lanes 32*(w%4) .. +31).
+__device__ __forceinline__ void tmem_ld16(uint32_t addr, uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(addr)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Generic-proxy shared-memory writes become visible to the async proxy (tensor core reads).
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+}  // namespace gx

@@ -29,7 +29,7 @@ def check(ref, got, tight=TIGHT):
 
 @pytest.fixture(scope="module")
 def ctx():
-    with abi.Context(device=0, max_tokens=64, max_layers=4) as c:
+    with abi.Context(device=0, max_tokens=512, max_layers=4) as c:
         yield c
 
 
@@ -131,13 +131,13 @@ def test_stack_matches_oracle_chain(ctx):
 
 
 def test_forward_rejects_bad_calls(ctx):
-    import ctypes
     lib, h = ctx.lib, ctx.handle
+    ctx.upload_layer(0, small_layer()[0])
     x = np.zeros((1, 256), np.float32)
     y = np.zeros((1, 256), np.float32)
     assert lib.gx_moe_forward_host(h, 99, x.ctypes.data, 0, 1, y.ctypes.data, 0, None, None, 1000) == -6
     assert lib.gx_moe_forward_host(h, 0, x.ctypes.data, 7, 1, y.ctypes.data, 0, None, None, 1000) == -1
-    assert lib.gx_moe_forward_host(h, 0, x.ctypes.data, 0, 65, y.ctypes.data, 0, None, None, 1000) == -1
+    assert lib.gx_moe_forward_host(h, 0, x.ctypes.data, 0, 513, y.ctypes.data, 0, None, None, 1000) == -1
     assert lib.gx_wait(h, 10 ** 9, 0) == -1
 
 
@@ -205,3 +205,47 @@ def test_deep_stack_stays_finite_and_matches(ctx):
         ref = oracle.stack(layers, synth.bf16_round(x))
         assert np.isfinite(got).all()
         check(ref, got, tight=1e-4)
+
+
+# ---- prefill path (>= 64 tokens): tcgen05 grouped GEMM with f16 operands ------------------
+PREFILL_TIGHT = 5e-3   # f16 activations and d*CB rounded once: ~1e-3 relative expected
+
+
+@pytest.mark.parametrize("type_id", sorted(synth.BLOCK_BYTES))
+def test_prefill_small_all_types(ctx, type_id):
+    layer, x = small_layer(seed=200 + type_id, type_id=type_id, n_tok=100)
+    ctx.upload_layer(1, layer)
+    want, wids, ww = oracle.moe_ffn(layer, x)
+    got, ids, w = ctx.forward_host(1, x, want_routing=True)
+    assert metrics.topk_sets(wids, ids)["flips"] == 0
+    np.testing.assert_allclose(np.sort(w, 1), np.sort(ww, 1), rtol=1e-5, atol=1e-7)
+    check(want, got, tight=PREFILL_TIGHT)
+
+
+def test_prefill_config_shape_zipf_with_empty_experts(ctx):
+    """Config 2 in miniature: config-0 layer shape, 256 bf16 tokens, Zipf(1.1) popularity
+    (segments from 0 to several hundred rows, so several 128-row tiles for the head experts)
+    plus experts that receive no token at all."""
+    layer = synth.make_layer(31, zipf=1.1)
+    layer["router_bias"][[3, 50, 200]] = -np.inf
+    ctx.upload_layer(2, layer)
+    x = synth.tokens(32, 256, dtype="bf16")
+    want, wids, _ = oracle.moe_ffn(layer, x)
+    got, ids, _ = ctx.forward_host(2, synth.bf16_bits(x), want_routing=True)
+    counts = np.bincount(ids.reshape(-1), minlength=256)
+    assert counts.max() > 128 and (counts == 0).sum() >= 3
+    assert metrics.topk_sets(wids, ids)["flips"] == 0
+    check(want, got, tight=PREFILL_TIGHT)
+    gb = ctx.forward_host(2, synth.bf16_bits(x), out_dtype=np.uint16)
+    check(want, (gb.astype(np.uint32) << 16).view(np.float32), tight=PREFILL_TIGHT + 4e-3)
+
+
+def test_prefill_stack_matches_oracle(ctx):
+    layers = [synth.make_layer(70 + i, n_expert=16, E=256, F=128, U=4) for i in range(3)]
+    for i, l in enumerate(layers):
+        ctx.upload_layer(i, l)
+    x = synth.tokens(71, 80, E=256) * 2.0
+    ref = oracle.stack(layers, x)
+    for _ in range(2):
+        got = ctx.stack_forward_host(0, 3, x)
+        check(ref, got, tight=PREFILL_TIGHT)
