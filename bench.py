@@ -56,7 +56,8 @@ def parse():
     p.add_argument("--steps", type=int, default=128)
     p.add_argument("--warmup", type=int, default=8)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--workload", choices=["decode"], default="decode")
+    p.add_argument("--workload", choices=["decode", "prefill"], default="decode")
+    p.add_argument("--tokens", type=int, default=1024, help="prefill: tokens per step")
     p.add_argument("--layers", type=int, default=N_LAYERS)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=15.0)
@@ -327,10 +328,106 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_prefill(args):
+    """one sequence of --tokens bf16 tokens ~N(0,1) through the config-0
+    layer with Zipf(1.1) expert popularity (ragged segments, some experts empty), bf16 output.
+    Each step is one forward of the whole sequence; 4 distinct input batches rotate."""
+    import torch
+    from gyro_moe import abi, synth
+    from oracle import oracle
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    T, K, W = args.tokens, args.steps, args.warmup
+    layer = synth.make_layer(LAYER_SEED, zipf=1.1)
+    ctx = abi.Context(device=0, max_tokens=T, max_layers=1)
+    ctx.upload_layer(0, layer)
+    xs_host = step_tokens(4, T, 0)
+    xs = torch.from_numpy(xs_host.view(np.int16)).to(dev).view(torch.bfloat16)
+    y = torch.empty((T, E), dtype=torch.bfloat16, device=dev)
+    ids = torch.empty((T, U), dtype=torch.int32, device=dev)
+    for i in range(W):
+        ctx.forward(0, xs[i % 4], y, ids)
+    torch.cuda.synchronize(dev)
+    stream = torch.cuda.ExternalStream(ctx.stream(), device=dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clocks:
+        with torch.cuda.stream(stream):
+            start.record(stream)
+        for i in range(K):
+            ticket = ctx.forward(0, xs[i % 4], y)
+        with torch.cuda.stream(stream):
+            end.record(stream)
+        end.synchronize()
+    ctx.wait(ticket)
+    ms = start.elapsed_time(end)
+    ctx.set_flags(abi.GX_FLAG_PROFILE)
+    prof = []
+    for i in range(5):
+        ctx.wait(ctx.forward(0, xs[i % 4], y, ids))
+        prof.append(ctx.timings())
+    ctx.set_flags(0)
+    ids_np = ids.cpu().numpy().astype(np.int64)
+    counts = np.bincount(ids_np.reshape(-1), minlength=NE)
+    slots = T * U
+    gu_flops = slots * 2 * F * E * 2
+    dn_flops = slots * F * E * 2
+    gu_s = statistics.median(p.gate_up_ns for p in prof) * 1e-9
+    dn_s = statistics.median(p.down_ns for p in prof) * 1e-9
+    rt_s = statistics.median(p.router_ns for p in prof) * 1e-9
+    pk = peaks()
+    achieved = gu_flops / gu_s / 1e12
+    tiles = int(np.sum((counts + 127) // 128))
+    touched = int((counts > 0).sum()) * EXPERT_BYTES
+    # end to end: host bf16 in, host bf16 out
+    e2e_steps = min(K, 16)
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        ctx.forward_host(0, xs_host[i % 4], out_dtype=np.uint16)
+    e2e_s = time.perf_counter() - t0
+    line = {
+        "metric": METRIC, "value": K * T / (ms / 1e3), "unit": "tok/s", "n_gpus": 1, "steps": K, "warmup": W,
+        "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (seeded; shapes and distributions of BASELINE.json config 2)",
+        "config": {"workload": f"prefill: one {T}-token sequence through the config-0 routed layer, Zipf(1.1) routing",
+                   "tokens": T, "hidden": E, "experts": NE, "top_k": U, "ffn": F, "type": "TQ2_T",
+                   "experts_hit": int((counts > 0).sum()), "max_segment": int(counts.max()), "row_tiles": tiles,
+                   "l2": "inputs larger than L2: a step reads every touched expert (up to 214 MB)"},
+        "roofline": {
+            "kernel": "moe_gemm_kernel<gate/up> (tcgen05 grouped GEMM, in-smem trellis decode, SwiGLU epilogue)",
+            "bound": "tensor", "achieved": achieved, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+            "frac": achieved / pk["bf16_tflops"], "traffic": None,
+            "algorithmic_flops_per_launch": gu_flops, "launch_us": gu_s * 1e6,
+            "padded_flops_per_launch": tiles * 128 * 2 * F * E * 2,
+            "peak_source": f"{pk['source']} (MEASURED_PEAKS.json bf16_tflops, burst; f16 has the same dense rate)",
+            "phase_us": {"select_group_pack": rt_s * 1e6, "gate_up_gemm": gu_s * 1e6, "down_gemm_combine": dn_s * 1e6},
+            "down_tflops": dn_flops / dn_s / 1e12,
+            "hbm_gbs_experts": touched / (ms / K / 1e3) / 1e9,
+        },
+        "e2e": {"value": e2e_steps * T / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": T * E * 2,
+                "d2h_bytes_per_step": T * E * 2, "steps": e2e_steps,
+                "api": "gx_moe_forward_host (host bf16 in, host bf16 out)"},
+        "gpu_launches": K * 8,
+        "clocks": clocks.summary(),
+    }
+    if not args.no_cpu_baseline:
+        threads = oracle.max_threads()
+        xs32 = (xs_host[0][:64].astype(np.uint32) << 16).view(np.float32)
+        t0 = time.perf_counter()
+        oracle.moe_ffn(layer, xs32, threads=threads, fast=True)
+        el = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": 64 / el, "unit": "tok/s", "cores": threads, "kind": "port",
+                                "sample": f"64 of the {T} tokens through the layer, {el:.1f} s on {threads} threads"}
+    print(json.dumps(line), flush=True)
+    ctx.close()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "prefill":
+        run_prefill(args)
     else:
         run_ours(args)
 

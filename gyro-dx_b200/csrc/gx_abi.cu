@@ -60,6 +60,7 @@ struct gx_context {
     struct Prefill {
         size_t max_tiles = 0, E = 0, F = 0, slots = 0;
         uint8_t *A = nullptr, *A2 = nullptr;
+        __half *xh = nullptr;
         float *act = nullptr;
         __half *Y = nullptr;
         int *ints = nullptr;  // expert_count | tile_expert | tile_rows | n_mtiles | row_slot | slot_row
@@ -158,7 +159,7 @@ gx_result ensure_scratch(gx_context *c) {
     const size_t T = c->max_tokens ? c->max_tokens : 1;
     // Sized for the largest shapes the ABI accepts: E <= 4096, F <= 1024, NE <= 512, U <= 16.
     const size_t E = 4096, F = 1024, NE = 512, U = 16;
-    GX_CUDA(cudaMalloc(&c->logits, T * NE * sizeof(float)));
+    GX_CUDA(cudaMalloc(&c->logits, 4 * T * NE * sizeof(float)));  // up to 4 split-K partials
     GX_CUDA(cudaMalloc(&c->weights, T * U * sizeof(float)));
     GX_CUDA(cudaMalloc(&c->xscale, T * sizeof(float)));
     GX_CUDA(cudaMalloc(&c->ss, T * sizeof(float)));
@@ -183,7 +184,7 @@ void release_all(gx_context *c) {
     }
     c->graphs.clear();
     for (auto &l : c->layers) if (l.arena) cudaFree(l.arena);
-    void *pf[] = {c->pf.A, c->pf.A2, c->pf.act, c->pf.Y, c->pf.ints};
+    void *pf[] = {c->pf.A, c->pf.A2, c->pf.act, c->pf.Y, c->pf.ints, c->pf.xh};
     for (void *p : pf) if (p) cudaFree(p);
     for (auto &m : c->mats) if (m.tiles) cudaFree(m.tiles);
     void *dev[] = {c->codebook, c->logits, c->weights, c->xscale, c->ss, c->ids, c->act, c->xbuf[0], c->xbuf[1],
@@ -216,7 +217,7 @@ gx_result ensure_prefill(gx_context *c, const Layer &L) {
     const size_t tiles = (slots + 127) / 128 + std::min<size_t>(L.local_experts, slots);
     auto &p = c->pf;
     if (p.max_tiles >= tiles && p.E >= L.E && p.F >= L.F && p.slots >= slots) return GX_OK;
-    void *old[] = {p.A, p.A2, p.act, p.Y, p.ints};
+    void *old[] = {p.A, p.A2, p.act, p.Y, p.ints, p.xh};
     bool had = false;
     for (void *q : old) if (q) { cudaFree(q); had = true; }
     p = gx_context::Prefill{};
@@ -231,6 +232,7 @@ gx_result ensure_prefill(gx_context *c, const Layer &L) {
     GX_CUDA(cudaMalloc(&p.A2, tiles * (L.F / 64) * 16384));
     GX_CUDA(cudaMalloc(&p.act, tiles * 128 * L.F * sizeof(float)));
     GX_CUDA(cudaMalloc(&p.Y, tiles * 128 * L.E * sizeof(__half)));
+    GX_CUDA(cudaMalloc(&p.xh, (size_t)c->max_tokens * L.E * sizeof(__half)));
     const size_t n_ints = 512 + 2 * tiles + 1 + tiles * 128 + slots;
     GX_CUDA(cudaMalloc(&p.ints, n_ints * sizeof(int)));
     p.expert_count = p.ints;
@@ -257,7 +259,9 @@ gx_result enqueue_layer_prefill(gx_context *c, const Layer &L, const void *x, ui
     auto &p = c->pf;
     const int xb = x_dtype == GX_BF16;
     if (ev) GX_CUDA(record_phase(ev[0], c->stream));
-    GX_CUDA(gx::launch_router_gemm(L.router, x, xb, (int)n_tok, (int)L.n_expert, (int)L.E, c->logits, c->stream));
+    const int splits = (L.E % (4 * 32) == 0) ? 4 : 1;
+    GX_CUDA(gx::launch_router_gemm(L.router, x, xb, (int)n_tok, (int)L.n_expert, (int)L.E, c->logits, splits,
+                                   c->stream));
     gx::RouterArgs ra{};
     ra.W = L.router;
     ra.bias = L.bias;
@@ -271,6 +275,7 @@ gx_result enqueue_layer_prefill(gx_context *c, const Layer &L, const void *x, ui
     ra.norm_eps = norm_eps;
     ra.ss = c->ss;
     ra.ss_from_x = 1;
+    ra.logit_splits = splits;
     ra.xscale = c->xscale;
     ra.logits = c->logits;
     ra.ids = c->ids;
@@ -295,8 +300,9 @@ gx_result enqueue_layer_prefill(gx_context *c, const Layer &L, const void *x, ui
     pa.by_token = 1;
     pa.U = (int)L.U;
     pa.K = (int)L.E;
-    pa.xscale = norm_eps > 0.f ? c->xscale : nullptr;
-    pa.signs = L.gate_signs;
+    GX_CUDA(gx::launch_rotate_tokens(x, xb, norm_eps > 0.f ? c->xscale : nullptr, L.gate_signs, (int)n_tok,
+                                     (int)L.E, p.xh, c->stream));
+    pa.xh = p.xh;
     pa.row_slot = p.row_slot;
     pa.tile_rows = p.tile_rows;
     pa.n_mtiles = p.n_mtiles;
@@ -383,6 +389,7 @@ gx_result enqueue_layer(gx_context *c, const Layer &L, const void *x, uint32_t x
     ra.scale = L.scale;
     ra.norm_eps = norm_eps;
     ra.ss = c->ss;
+    ra.logit_splits = 1;
     ra.xscale = c->xscale;
     ra.logits = c->logits;
     ra.ids = c->ids;

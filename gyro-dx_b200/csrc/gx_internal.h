@@ -21,6 +21,7 @@ struct RouterArgs {
     float norm_eps;          // > 0: route RMSNorm(x) (unit weight)
     float *ss;               // [n_tok] sum of squares of x (written when norm_eps > 0)
     int ss_from_x;           // selection computes the sum of squares from x itself (prefill)
+    int logit_splits;        // > 1: logits holds that many split-K partials [split][n_tok][NE]
     float *xscale;           // [n_tok] per-token input scale (written by topk_kernel)
     float *logits;           // [n_tok][NE] scratch (raw W x, before scale and bias)
     uint32_t *ids;           // [n_tok][U]
@@ -91,7 +92,8 @@ struct PackArgs {
     const void *src;         // by_token: x [n_tok][K]; else act [padded rows][K]
     int src_bf16;
     int by_token, U, K;
-    const float *xscale;     // [n_tok] or nullptr (by_token only)
+    const float *xscale;     // [n_tok] or nullptr (transform mode only)
+    const __half *xh;        // by_token: rotated f16 token rows [n_tok][K] (rotate_tokens)
     const float *signs;      // [K] or nullptr (then no Hadamard transform)
     const int *row_slot, *tile_rows, *n_mtiles;
     uint8_t *dst;            // [tiles][K/64][16384] f16 swizzled
@@ -124,7 +126,9 @@ struct CombineArgs {
 };
 
 cudaError_t launch_router_gemm(const float *W, const void *x, int x_bf16, int n_tok, int NE, int E, float *C,
-                               cudaStream_t s);
+                               int splits, cudaStream_t s);
+cudaError_t launch_rotate_tokens(const void *x, int x_bf16, const float *xscale, const float *signs, int n_tok,
+                                int E, __half *xh, cudaStream_t s);
 cudaError_t launch_group(const GroupArgs &a, cudaStream_t s);
 cudaError_t launch_pack_rows(const PackArgs &a, int max_tiles, cudaStream_t s);
 cudaError_t launch_moe_gemm(const GemmArgs &a, int mode, int sm_count, cudaStream_t s);

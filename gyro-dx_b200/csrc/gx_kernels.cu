@@ -115,12 +115,27 @@ __device__ void topk_token(const RouterArgs &a, int t, int lane) {
     float ss = 0.f;
     if (a.norm_eps > 0.f) {
         if (a.ss_from_x) {
-            for (int i = 4 * lane; i < a.E; i += 128) {
-                float v[4];
+            // 8 values per lane per step (E is a multiple of 128): independent 16-byte loads
+#pragma unroll 4
+            for (int i = 8 * lane; i < a.E; i += 256) {
+                float v[8];
+                const size_t g = (size_t)t * a.E + i;
+                if (a.x_bf16) {
+                    const uint4 q = *reinterpret_cast<const uint4 *>(reinterpret_cast<const __nv_bfloat16 *>(a.x) + g);
+                    const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-                for (int j = 0; j < 4; ++j) v[j] = load_act(a.x, a.x_bf16, (size_t)t * a.E + i + j);
+                    for (int j = 0; j < 4; ++j) {
+                        v[2 * j] = __uint_as_float(w4[j] << 16);
+                        v[2 * j + 1] = __uint_as_float(w4[j] & 0xffff0000u);
+                    }
+                } else {
+                    const float4 p0 = *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(a.x) + g);
+                    const float4 p1 = *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(a.x) + g + 4);
+                    v[0] = p0.x; v[1] = p0.y; v[2] = p0.z; v[3] = p0.w;
+                    v[4] = p1.x; v[5] = p1.y; v[6] = p1.z; v[7] = p1.w;
+                }
 #pragma unroll
-                for (int j = 0; j < 4; ++j) ss = fmaf(v[j], v[j], ss);
+                for (int j = 0; j < 8; ++j) ss = fmaf(v[j], v[j], ss);
             }
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
@@ -133,7 +148,12 @@ __device__ void topk_token(const RouterArgs &a, int t, int lane) {
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
         const int i = lane + 32 * j;
-        v[j] = i < a.NE ? __ldcg(row + i) * scale + (a.bias ? __ldg(a.bias + i) : 0.f) : -INFINITY;
+        float raw = 0.f;
+        if (i < a.NE) {
+            raw = __ldcg(row + i);
+            for (int z = 1; z < a.logit_splits; ++z) raw += __ldcg(row + (size_t)z * a.n_tok * a.NE + i);
+        }
+        v[j] = i < a.NE ? raw * scale + (a.bias ? __ldg(a.bias + i) : 0.f) : -INFINITY;
     }
     float m = v[0];
 #pragma unroll

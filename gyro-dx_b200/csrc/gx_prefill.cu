@@ -25,29 +25,44 @@
 namespace gx {
 
 // ------------------------------------------------------------------------------------------
-// Router GEMM: C[t][e] = sum_c X[t][c] W[e][c]. CTA tile 64 tokens x 32 experts, 256 threads,
-// each 4 tokens x 2 experts, K chunks of 32 staged in shared memory.
+// Router GEMM: C[z][t][e] = sum over the z-th K slice of X[t][c] W[e][c] (split-K partials,
+// summed in a fixed order by the selection). CTA tile 64 tokens x 32 experts, 256 threads, each
+// 4 tokens x 2 experts, K chunks of 32 staged in shared memory with the next chunk prefetched.
 // ------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) router_gemm_kernel(const float *__restrict__ W, const void *__restrict__ x,
                                                           int x_bf16, int n_tok, int NE, int E, float *__restrict__ C) {
     __shared__ __align__(16) float xs[32][64 + 4];
     __shared__ __align__(16) float ws[32][32 + 4];
     const int t0 = blockIdx.y * 64, e0 = blockIdx.x * 32;
+    const int ksplit = E / gridDim.z, kbeg = blockIdx.z * ksplit, kend = kbeg + ksplit;
+    C += (size_t)blockIdx.z * n_tok * NE;
     const int tid = threadIdx.x;
     const int tt = (tid & 15) * 4, ee = (tid >> 4) * 2;
+    // loader mapping: x tile 64 x 32 -> 8 values per thread (rows lr + 8j, column lc);
+    // w tile 32 x 32 -> 4 values per thread (rows lr + 8j)
+    const int lc = tid & 31, lr = tid >> 5;
+    float xr[8], wr[4];
+    auto load = [&](int k0) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int t = t0 + lr + 8 * j;
+            xr[j] = t < n_tok ? load_act(x, x_bf16, (size_t)t * E + k0 + lc) : 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int e = e0 + lr + 8 * j;
+            wr[j] = e < NE ? __ldg(W + (size_t)e * E + k0 + lc) : 0.f;
+        }
+    };
     float acc[4][2] = {};
-    for (int k0 = 0; k0 < E; k0 += 32) {
-        // x tile: 64 tokens x 32 columns (8 per thread)
-        for (int i = tid; i < 64 * 32; i += 256) {
-            const int r = i >> 5, c = i & 31;
-            const int t = t0 + r;
-            xs[c][r] = t < n_tok ? load_act(x, x_bf16, (size_t)t * E + k0 + c) : 0.f;
-        }
-        for (int i = tid; i < 32 * 32; i += 256) {
-            const int r = i >> 5, c = i & 31;
-            ws[c][r] = e0 + r < NE ? W[(size_t)(e0 + r) * E + k0 + c] : 0.f;
-        }
+    load(kbeg);
+    for (int k0 = kbeg; k0 < kend; k0 += 32) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) xs[lc][lr + 8 * j] = xr[j];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) ws[lc][lr + 8 * j] = wr[j];
         __syncthreads();
+        if (k0 + 32 < kend) load(k0 + 32);   // next chunk in flight while this one is consumed
 #pragma unroll 8
         for (int k = 0; k < 32; ++k) {
             const float4 xv = *reinterpret_cast<const float4 *>(&xs[k][tt]);
@@ -134,47 +149,115 @@ __global__ void __launch_bounds__(1024) group_kernel(GroupArgs a) {
 }
 
 // ------------------------------------------------------------------------------------------
-// Row packing: one warp per (padded row, 128-column block). Source row = token of the slot
-// (gate/up input, x) or the padded row itself (down input, act). v = src * scale, * signs, then
-// H128 / sqrt(128) when signs are given; f16 into the swizzled K-major tile layout
-// [tile][K/64][128 rows x 64 cols].
+// Token rotation, once per token: xh[t] = f16(H128((x[t] * scale[t]) * signs) / sqrt(128)) per
+// 128-column block (src/engine.zig:547-551), one warp per (token, 4 blocks).
+// ------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) rotate_tokens_kernel(const void *x, int x_bf16, const float *xscale,
+                                                            const float *signs, int n_tok, int E, __half *xh) {
+    const int lane = threadIdx.x & 31;
+    const long long w = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int nb = E / 128, groups = (nb + 3) / 4;
+    if (w >= (long long)n_tok * groups) return;
+    const int t = (int)(w / groups), b0 = (int)(w % groups) * 4;
+    const float sc = xscale ? xscale[t] : 1.f;
+    float v[4][4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const int b = b0 + q;
+        if (b >= nb) break;
+        const size_t base = (size_t)t * E + b * 128 + 4 * lane;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[q][j] = load_act(x, x_bf16, base + j) * sc;
+        if (signs) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) v[q][j] *= signs[b * 128 + 4 * lane + j];
+        }
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const int b = b0 + q;
+        if (b >= nb) break;
+        if (signs) fwht128_warp(v[q], lane);
+        uint2 o;
+        o.x = pack_half2(v[q][0], v[q][1]);
+        o.y = pack_half2(v[q][2], v[q][3]);
+        *reinterpret_cast<uint2 *>(xh + (size_t)t * E + b * 128 + 4 * lane) = o;
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// Row packing: one warp per padded row. Source row = token of the slot (gate/up input, x) or
+// the padded row itself (down input, act). v = src * scale, * signs, then H128 / sqrt(128) per
+// 128-column block when signs are given; f16 into the swizzled K-major tile layout
+// [tile][K/64][128 rows x 64 cols]. Four blocks' loads are in flight at a time.
 // ------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) pack_rows_kernel(PackArgs a) {
     const int lane = threadIdx.x & 31;
-    const long long wid = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const long long row = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
     const int nb = a.K / 128;
-    const long long row = wid / nb;
-    const int b = (int)(wid % nb);
-    const int n_rows = *a.n_mtiles * 128;
-    if (row >= n_rows) return;
+    if (row >= (long long)*a.n_mtiles * 128) return;
     const int t = (int)(row >> 7), i = (int)(row & 127);
-    float v[4] = {0.f, 0.f, 0.f, 0.f};
-    if (i < a.tile_rows[t]) {
-        size_t src_row;
-        float sc = 1.f;
-        if (a.by_token) {
-            const int slot = a.row_slot[row];
-            const int tok = slot / a.U;
-            src_row = (size_t)tok;
-            if (a.xscale) sc = a.xscale[tok];
-        } else {
-            src_row = (size_t)row;
-        }
-        const size_t base = src_row * a.K + b * 128 + 4 * lane;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            v[j] = load_act(a.src, a.src_bf16, base + j) * sc;
-            if (a.signs) v[j] *= a.signs[b * 128 + 4 * lane + j];
-        }
-        if (a.signs) fwht128_warp(v, lane);
+    const bool valid = i < a.tile_rows[t];
+    size_t src_row = (size_t)row;
+    float sc = 1.f;
+    if (valid && a.by_token) {
+        const int tok = a.row_slot[row] / a.U;
+        src_row = (size_t)tok;
+        if (a.xscale) sc = a.xscale[tok];
     }
-    // lane holds columns 4*lane .. +3 of the block: k-step 2b + lane/16, columns 4*(lane%16)..
-    const int ks = 2 * b + (lane >> 4), col = 4 * (lane & 15);
-    uint8_t *tile = a.dst + ((size_t)t * (a.K / 64) + ks) * 16384u;
-    uint2 w;
-    w.x = pack_half2(v[0], v[1]);
-    w.y = pack_half2(v[2], v[3]);
-    *reinterpret_cast<uint2 *>(tile + sw128_offset((uint32_t)i, (uint32_t)col)) = w;
+    const int ks_lo = lane >> 4, col = 4 * (lane & 15);
+    if (a.by_token) {
+        // gate/up input: copy the token's rotated f16 row (rotate_tokens_kernel) into the tile
+        const __half *xr = a.xh + src_row * a.K;
+        for (int b = 0; b < nb; ++b) {
+            uint2 w = make_uint2(0u, 0u);
+            if (valid) w = *reinterpret_cast<const uint2 *>(xr + b * 128 + 4 * lane);
+            uint8_t *tile = a.dst + ((size_t)t * (a.K / 64) + 2 * b + ks_lo) * 16384u;
+            *reinterpret_cast<uint2 *>(tile + sw128_offset((uint32_t)i, (uint32_t)col)) = w;
+        }
+        return;
+    }
+    for (int b0 = 0; b0 < nb; b0 += 4) {
+        float v[4][4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int b = b0 + q;
+            if (valid && b < nb) {
+                const size_t base = src_row * a.K + b * 128 + 4 * lane;
+                if (a.src_bf16) {
+                    const uint2 w = *reinterpret_cast<const uint2 *>(reinterpret_cast<const __nv_bfloat16 *>(a.src) + base);
+                    v[q][0] = __uint_as_float(w.x << 16);
+                    v[q][1] = __uint_as_float(w.x & 0xffff0000u);
+                    v[q][2] = __uint_as_float(w.y << 16);
+                    v[q][3] = __uint_as_float(w.y & 0xffff0000u);
+                } else {
+                    const float4 w = *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(a.src) + base);
+                    v[q][0] = w.x; v[q][1] = w.y; v[q][2] = w.z; v[q][3] = w.w;
+                }
+                if (a.signs) {
+                    const float4 g = *reinterpret_cast<const float4 *>(a.signs + b * 128 + 4 * lane);
+                    v[q][0] *= g.x * sc; v[q][1] *= g.y * sc; v[q][2] *= g.z * sc; v[q][3] *= g.w * sc;
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) v[q][j] *= sc;
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) v[q][j] = 0.f;
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int b = b0 + q;
+            if (b >= nb) break;
+            if (a.signs) fwht128_warp(v[q], lane);
+            uint8_t *tile = a.dst + ((size_t)t * (a.K / 64) + 2 * b + ks_lo) * 16384u;
+            uint2 w;
+            w.x = pack_half2(v[q][0], v[q][1]);
+            w.y = pack_half2(v[q][2], v[q][3]);
+            *reinterpret_cast<uint2 *>(tile + sw128_offset((uint32_t)i, (uint32_t)col)) = w;
+        }
+    }
 }
 
 // ------------------------------------------------------------------------------------------
@@ -317,16 +400,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1) moe_gemm_kernel(GemmArgs a) {
             const uint8_t *rowtiles = mat + (size_t)(row >> 3) * NB * TB;
             const int r8 = row & 7;
             bool ok = true;
+            // codes of one k-step: the two own quarters (2h, 2h+1), the neighbour run of quarter
+            // (2h+3)%4 and the row's block scale; step ks+1 is fetched while ks is decoded
+            uint32_t nx0[4], nx1[4], nxn[4];
+            uint16_t nxd;
+            auto fetch = [&](int ks) {
+                const int h = ks & 1;
+                const uint8_t *tile = rowtiles + (size_t)(ks >> 1) * TB;
+                load_run<T>(tile, 4 * r8 + 2 * h, nx0);
+                load_run<T>(tile, 4 * r8 + 2 * h + 1, nx1);
+                load_run<T>(tile, 4 * r8 + ((2 * h + 3) & 3), nxn);
+                nxd = *reinterpret_cast<const uint16_t *>(tile + tile_code_bytes(T) + 2 * r8);
+            };
+            fetch(0);
             for (int ks = 0; ks < KS; ++ks, ++n) {
                 const int s = n % kGemmStages, round = n / kGemmStages;
-                const int b = ks >> 1, h = ks & 1;
-                const uint8_t *tile = rowtiles + (size_t)b * TB;
-                // two own quarters (2h, 2h+1) and the neighbour run of quarter (2h+3)%4
                 uint32_t own0[4], own1[4], nbr[4];
-                load_run<T>(tile, 4 * r8 + 2 * h, own0);
-                load_run<T>(tile, 4 * r8 + 2 * h + 1, own1);
-                load_run<T>(tile, 4 * r8 + ((2 * h + 3) & 3), nbr);
-                const uint16_t dh = *reinterpret_cast<const uint16_t *>(tile + tile_code_bytes(T) + 2 * r8);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) { own0[j] = nx0[j]; own1[j] = nx1[j]; nbr[j] = nxn[j]; }
+                const uint16_t dh = nxd;
+                if (ks + 1 < KS) fetch(ks + 1);
                 const __half2 d2 = __halves2half2(__ushort_as_half(dh), __ushort_as_half(dh));
                 uint32_t i0[2][8], i1[2][8];
                 quarter_indices<T>(own0, neighbour_bits<T>(nbr), i0[0], i1[0]);
@@ -461,8 +554,8 @@ __global__ void __launch_bounds__(256) combine_kernel(CombineArgs a) {
 // Host launchers
 // ------------------------------------------------------------------------------------------
 cudaError_t launch_router_gemm(const float *W, const void *x, int x_bf16, int n_tok, int NE, int E, float *C,
-                               cudaStream_t s) {
-    dim3 grid((NE + 31) / 32, (n_tok + 63) / 64);
+                               int splits, cudaStream_t s) {
+    dim3 grid((NE + 31) / 32, (n_tok + 63) / 64, splits);
     router_gemm_kernel<<<grid, 256, 0, s>>>(W, x, x_bf16, n_tok, NE, E, C);
     return cudaGetLastError();
 }
@@ -477,7 +570,7 @@ cudaError_t launch_group(const GroupArgs &a, cudaStream_t s) {
 }
 
 cudaError_t launch_pack_rows(const PackArgs &a, int max_tiles, cudaStream_t s) {
-    const long long warps = (long long)max_tiles * 128 * (a.K / 128);
+    const long long warps = (long long)max_tiles * 128;
     if (warps == 0) return cudaSuccess;
     pack_rows_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(a);
     return cudaGetLastError();
@@ -512,6 +605,14 @@ cudaError_t launch_moe_gemm(const GemmArgs &a, int mode, int sm_count, cudaStrea
             return cudaErrorInvalidValue;
     }
 #undef GX_GEMM_CASE
+}
+
+cudaError_t launch_rotate_tokens(const void *x, int x_bf16, const float *xscale, const float *signs, int n_tok,
+                                int E, __half *xh, cudaStream_t s) {
+    const long long warps = (long long)n_tok * ((E / 128 + 3) / 4);
+    if (warps == 0) return cudaSuccess;
+    rotate_tokens_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(x, x_bf16, xscale, signs, n_tok, E, xh);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_combine(const CombineArgs &a, cudaStream_t s) {
