@@ -8,6 +8,7 @@
 #include <cstring>
 #include <algorithm>
 #include <map>
+#include <mutex>
 #include <thread>
 #include <tuple>
 #include <vector>
@@ -945,6 +946,166 @@ GX_API gx_result gx_destroy(gx_context *c, uint32_t timeout_ms) {
     release_all(c);
     delete c;
     return GX_OK;
+}
+
+}  // extern "C"
+
+// ---- gx_moe_forward_noalloc: decode layer on library-owned static scratch -----------------
+// Some hosts may not allocate device memory once they start stepping: serving hosts that give
+// all free HBM to their own pools at start-up (so a later cudaMalloc fails), and step loops that
+// must not stall the device (cudaMalloc and cudaFree synchronise it). gx_moe_forward can
+// allocate on a call (the tensor-core path sizes its buffers on first use), so this entry point
+// runs the decode kernels on a fixed array that is part of the library image instead.
+namespace {
+
+constexpr uint32_t kNoAllocMaxTokens = GX_NOALLOC_MAX_TOKENS;
+constexpr uint64_t na_align(uint64_t v) { return (v + 255) & ~uint64_t(255); }
+// Per-token scratch at the ABI's largest accepted layer: 512 router logits, U*F <= 64*128
+// activations; selections for U <= 16; one norm and one input scale.
+constexpr size_t kNaLogits = 0;
+constexpr size_t kNaSs = kNaLogits + na_align((uint64_t)kNoAllocMaxTokens * 512 * 4);
+constexpr size_t kNaXscale = kNaSs + na_align((uint64_t)kNoAllocMaxTokens * 4);
+constexpr size_t kNaIds = kNaXscale + na_align((uint64_t)kNoAllocMaxTokens * 4);
+constexpr size_t kNaWeights = kNaIds + na_align((uint64_t)kNoAllocMaxTokens * 16 * 4);
+constexpr size_t kNaAct = kNaWeights + na_align((uint64_t)kNoAllocMaxTokens * 16 * 4);
+constexpr size_t kNaBytes = kNaAct + na_align((uint64_t)kNoAllocMaxTokens * 64 * 128 * 4);
+static_assert(kNaBytes == GX_NOALLOC_SCRATCH_BYTES, "header limit out of date");
+
+// The scratch: one array per device, shared by every context and every call on that device.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNaBytes];
+
+constexpr int kNaMaxDevices = 64;
+std::mutex g_noalloc_mu;
+uint8_t *g_noalloc_base[kNaMaxDevices] = {};
+
+// Device address of the array on the current device (c->device), looked up on the first call
+// for that device. The lookup loads the library's device code on that device if it is not
+// loaded yet, which is why the first call should come before any stream capture.
+gx_result noalloc_scratch(gx_context *c, uint8_t **out) {
+    if (c->device < 0 || c->device >= kNaMaxDevices) return GX_E_UNSUPPORTED;
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_base[c->device]) {
+        void *p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return fail_cuda_at(c, e, "cudaGetSymbolAddress(g_noalloc_scratch)", __LINE__);
+        g_noalloc_base[c->device] = static_cast<uint8_t *>(p);
+    }
+    *out = g_noalloc_base[c->device];
+    return GX_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+GX_API gx_result gx_moe_forward_noalloc(gx_context *c, uint32_t layer, const void *x, uint32_t x_dtype,
+                                        uint32_t n_tok, void *y, uint32_t y_dtype, uint32_t *ids, float *weights,
+                                        uint64_t *out_ticket) {
+    if (!c) return GX_E_INVALIDARG;
+    if (c->broken) return GX_E_DEVICE;
+    if (layer >= c->layers.size() || !c->layers[layer].ready) return GX_E_STATE;
+    if ((x_dtype != GX_F32 && x_dtype != GX_BF16) || (y_dtype != GX_F32 && y_dtype != GX_BF16)) return GX_E_INVALIDARG;
+    if (n_tok > kNoAllocMaxTokens) {
+        if (debug_enabled())
+            std::fprintf(stderr, "gyro_moe: gx_moe_forward_noalloc: n_tok %u exceeds the static scratch limit of %u\n",
+                         n_tok, kNoAllocMaxTokens);
+        return GX_E_INVALIDARG;
+    }
+    if (n_tok > 0 && (!x || !y)) return GX_E_INVALIDARG;
+    if (((uintptr_t)x & 15) || ((uintptr_t)y & 3) || ((uintptr_t)ids & 3) || ((uintptr_t)weights & 3))
+        return GX_E_INVALIDARG;
+    const Layer &L = c->layers[layer];
+    if (L.n_expert > 512 || L.U > 16 || (uint64_t)L.U * L.F > 64 * 128) return GX_E_INVALIDARG;
+    GX_CUDA(cudaSetDevice(c->device));
+    uint8_t *base = nullptr;
+    gx_result r = noalloc_scratch(c, &base);
+    if (r != GX_OK) return r;
+    if (n_tok == 0) return record_ticket(c, out_ticket);
+
+    // Every scratch word a kernel reads is written earlier in the same call (logits by the
+    // router, selections by the top-k step, activations by gate/up), so nothing is cleared.
+    float *logits = reinterpret_cast<float *>(base + kNaLogits);
+    float *ss = reinterpret_cast<float *>(base + kNaSs);
+    float *xscale = reinterpret_cast<float *>(base + kNaXscale);
+    uint32_t *sel_ids = reinterpret_cast<uint32_t *>(base + kNaIds);
+    float *sel_w = reinterpret_cast<float *>(base + kNaWeights);
+    float *act = reinterpret_cast<float *>(base + kNaAct);
+
+    gx::RouterArgs ra{};
+    ra.W = L.router;
+    ra.bias = L.bias;
+    ra.x = x;
+    ra.x_bf16 = x_dtype == GX_BF16;
+    ra.n_tok = (int)n_tok;
+    ra.NE = (int)L.n_expert;
+    ra.E = (int)L.E;
+    ra.U = (int)L.U;
+    ra.scale = L.scale;
+    ra.norm_eps = 0.f;
+    ra.ss = ss;
+    ra.logit_splits = 1;
+    ra.xscale = xscale;
+    ra.logits = logits;
+    ra.ids = sel_ids;
+    ra.weights = sel_w;
+    ra.err = c->err;
+    const bool fused = gx::gate_up_fuses_topk((int)L.E, (int)L.F, (int)L.U, (int)n_tok, c->sm_count);
+    GX_CUDA(gx::launch_router(ra, c->stream, false, !fused));
+
+    gx::GateUpArgs ga{};
+    ga.type = L.type;
+    ga.gate = L.gate;
+    ga.up = L.up;
+    ga.expert_bytes = L.gate_expert_bytes;
+    ga.x = x;
+    ga.x_bf16 = x_dtype == GX_BF16;
+    ga.signs = L.gate_signs;
+    ga.xscale = nullptr;
+    ga.ids = sel_ids;
+    ga.fused_topk = fused;
+    ga.logits = logits;
+    ga.bias = L.bias;
+    ga.ss = ss;
+    ga.NE = (int)L.n_expert;
+    ga.norm_eps = 0.f;
+    ga.wscale = L.scale;
+    ga.ids_out = sel_ids;
+    ga.weights_out = sel_w;
+    ga.act = act;
+    ga.codebook = c->codebook;
+    ga.E = (int)L.E;
+    ga.F = (int)L.F;
+    ga.U = (int)L.U;
+    ga.n_slots = (int)(n_tok * L.U);
+    ga.n_expert = (int)L.local_experts;
+    ga.err = c->err;
+    GX_CUDA(gx::launch_gate_up(ga, c->sm_count, c->stream, true));
+
+    gx::DownArgs da{};
+    da.type = L.type;
+    da.down = L.down;
+    da.expert_bytes = L.down_expert_bytes;
+    da.act = act;
+    da.signs = L.down_signs;
+    da.ids = sel_ids;
+    da.weights = sel_w;
+    da.resid = nullptr;
+    da.resid_bf16 = 0;
+    da.out = y;
+    da.out_bf16 = y_dtype == GX_BF16;
+    da.codebook = c->codebook;
+    da.E = (int)L.E;
+    da.F = (int)L.F;
+    da.U = (int)L.U;
+    da.n_tok = (int)n_tok;
+    da.n_expert = (int)L.local_experts;
+    da.err = c->err;
+    GX_CUDA(gx::launch_down(da, c->sm_count, c->stream, true));
+
+    const size_t sel_b = (size_t)n_tok * L.U * 4;
+    if (ids) GX_CUDA(cudaMemcpyAsync(ids, sel_ids, sel_b, cudaMemcpyDeviceToDevice, c->stream));
+    if (weights) GX_CUDA(cudaMemcpyAsync(weights, sel_w, sel_b, cudaMemcpyDeviceToDevice, c->stream));
+    return record_ticket(c, out_ticket);
 }
 
 }  // extern "C"

@@ -76,9 +76,12 @@ SIGNATURES = {
     "gx_upload_matrix": [_P, _U32, _U32, _U32, _P, _U64, ctypes.POINTER(_U32), _U32],
     "gx_matvec": [_P, _U32, _P, _U32, _P, ctypes.POINTER(_U64)],
     "gx_read_timings": [_P, ctypes.POINTER(Timings)],
+    "gx_moe_forward_noalloc": [_P, _U32, _P, _U32, _U32, _P, _U32, _P, _P, ctypes.POINTER(_U64)],
     "gx_set_flags": [_P, _U32],
     "gx_destroy": [_P, _U32],
 }
+
+NOALLOC_MAX_TOKENS = 16          # GX_NOALLOC_MAX_TOKENS
 
 _LIB = None
 
@@ -195,6 +198,15 @@ class Context:
         n_tok = x.shape[0]
         _check(self.lib.gx_moe_forward(self.handle, layer, _ptr(x), _dtype_code(x), n_tok, _ptr(y), _dtype_code(y),
                                        _ptr(ids), _ptr(weights), ctypes.byref(t)), "gx_moe_forward")
+        return t.value
+
+    def forward_noalloc(self, layer: int, x, y, ids=None, weights=None) -> int:
+        """gx_moe_forward_noalloc on device tensors: the decode layer on the library's static
+        scratch, for at most NOALLOC_MAX_TOKENS tokens. Returns the ticket."""
+        t = ctypes.c_uint64()
+        _check(self.lib.gx_moe_forward_noalloc(self.handle, layer, _ptr(x), _dtype_code(x), x.shape[0], _ptr(y),
+                                               _dtype_code(y), _ptr(ids), _ptr(weights), ctypes.byref(t)),
+               "gx_moe_forward_noalloc")
         return t.value
 
     def forward_host(self, layer: int, x: np.ndarray, out_dtype=np.float32, timeout_ms: int = 60000,

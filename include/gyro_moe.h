@@ -201,6 +201,33 @@ GX_API gx_result gx_matvec(gx_context *context, uint32_t handle, const float *x,
 
 GX_API gx_result gx_read_timings(gx_context *context, gx_timings *out_timings);
 
+/* No counterpart in the reference. The routed-expert layer for decode batches that allocates no
+ * device or host memory on any call. It is meant for hosts that may not allocate once they are
+ * stepping: a serving host that hands all free HBM to its own pools (expert arena, caches) at
+ * start-up, where a later cudaMalloc would fail, and step loops that must not stall the device,
+ * which cudaMalloc and cudaFree do because they synchronise it. gx_moe_forward can allocate on a
+ * call (buffers of the many-token path are sized on first use); this call never does.
+ *
+ * Same arguments, outputs, ticket and error reporting as gx_moe_forward, for
+ * n_tok <= GX_NOALLOC_MAX_TOKENS; a larger n_tok returns GX_E_INVALIDARG (with GX_DEBUG=1 set,
+ * the reason is printed). It runs the same decode kernels, always, and records no phase times.
+ *
+ * Its scratch (router logits, selected experts and weights, gate/up activations) is one fixed
+ * array of GX_NOALLOC_SCRATCH_BYTES bytes in the library's device image, one per device, shared
+ * by every context and every call on that device. Nothing in it needs to start at zero: a call
+ * writes each word before it reads it. Calls that overlap on the GPU (on different streams or
+ * contexts of one device, not ordered by the host) race on the array and give wrong results;
+ * calls through one context are ordered on its stream and do not overlap.
+ *
+ * The first call on each device looks up the array's device address (cudaGetSymbolAddress),
+ * which loads the library's device code on that device if needed; make that first call before
+ * any stream capture and before the host's no-allocation phase begins. */
+#define GX_NOALLOC_MAX_TOKENS 16u
+#define GX_NOALLOC_SCRATCH_BYTES 559616u
+GX_API gx_result gx_moe_forward_noalloc(gx_context *context, uint32_t layer, const void *x, uint32_t x_dtype,
+                                        uint32_t n_tok, void *y, uint32_t y_dtype, uint32_t *ids, float *weights,
+                                        uint64_t *out_ticket);
+
 /* Replaces the context's GX_FLAG_* set (e.g. to switch phase timing on for a profiled replay).
  * Phase events serialise the kernels they separate, so timed calls should run without it. */
 GX_API gx_result gx_set_flags(gx_context *context, uint32_t flags);
