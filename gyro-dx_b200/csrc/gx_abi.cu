@@ -14,6 +14,7 @@
 #include <vector>
 
 #include "../../include/gyro_moe.h"
+#include "gx_comm.h"
 #include "gx_internal.h"
 #include "gx_tile.h"
 
@@ -79,6 +80,23 @@ struct gx_context {
     uint32_t prof_layers = 0;        // layers recorded by the most recent forward call
     std::map<GraphKey, std::pair<cudaGraph_t, cudaGraphExec_t>> graphs;
     bool broken = false;
+    // expert-parallel group (world > 1)
+    const gx::NcclApi *nccl = nullptr;
+    ncclComm_t comm = nullptr;
+    uint32_t comm_timeout_ms = 120000;
+    struct Ep {
+        size_t src_cap = 0, recv_cap = 0, E = 0, U = 0;   // rows the buffers hold
+        int *pos_of = nullptr;                          // [max_tokens][world]
+        uint32_t *send_ids = nullptr;                   // [world * max_tokens][U]
+        float *send_w = nullptr;
+        __half *send_rows = nullptr, *ret_rows = nullptr;   // [world * max_tokens][E]
+        __half *recv_rows = nullptr, *part_rows = nullptr;  // [recv_cap][E]
+        uint32_t *recv_ids = nullptr;                   // [recv_rows][U]
+        float *recv_w = nullptr;
+        int *counts = nullptr;                          // device: send counts [world], recv counts [world]
+        int *h_counts = nullptr;                        // pinned copy
+        cudaEvent_t counts_ready = nullptr;
+    } ep;
 };
 
 namespace {
@@ -193,6 +211,17 @@ void release_all(gx_context *c) {
     for (void *p : dev) if (p) cudaFree(p);
     if (c->h_in) cudaFreeHost(c->h_in);
     if (c->h_out) cudaFreeHost(c->h_out);
+    void *ep[] = {c->ep.pos_of, c->ep.send_ids, c->ep.send_w, c->ep.send_rows, c->ep.ret_rows, c->ep.recv_rows,
+                  c->ep.part_rows, c->ep.recv_ids, c->ep.recv_w, c->ep.counts};
+    for (void *p : ep) if (p) cudaFree(p);
+    if (c->ep.h_counts) cudaFreeHost(c->ep.h_counts);
+    if (c->ep.counts_ready) cudaEventDestroy(c->ep.counts_ready);
+    if (c->comm) {
+        // Abort is local (no peer takes part) and also ends an operation stuck on a lost peer;
+        // the stream has been drained before this point unless the context is broken.
+        c->nccl->CommAbort(c->comm);
+        c->comm = nullptr;
+    }
     for (auto &e : c->events) if (e) cudaEventDestroy(e);
     for (auto &e : c->prof) if (e) cudaEventDestroy(e);
     c->prof.clear();
@@ -213,8 +242,7 @@ cudaError_t record_phase(cudaEvent_t ev, cudaStream_t s) {
 
 // Prefill buffers for max_tokens tokens of a layer shape. Rows are padded per expert to
 // 128-row tiles: at most slots/128 + min(NE, slots) tiles.
-gx_result ensure_prefill(gx_context *c, const Layer &L) {
-    const size_t slots = (size_t)c->max_tokens * L.U;
+gx_result ensure_prefill(gx_context *c, const Layer &L, size_t slots) {
     const size_t tiles = (slots + 127) / 128 + std::min<size_t>(L.local_experts, slots);
     auto &p = c->pf;
     if (p.max_tiles >= tiles && p.E >= L.E && p.F >= L.F && p.slots >= slots) return GX_OK;
@@ -255,7 +283,7 @@ gx_result ensure_prefill(gx_context *c, const Layer &L) {
 gx_result enqueue_layer_prefill(gx_context *c, const Layer &L, const void *x, uint32_t x_dtype, uint32_t n_tok,
                                 const void *resid, uint32_t resid_dtype, void *out, uint32_t out_dtype,
                                 float norm_eps, cudaEvent_t *ev) {
-    gx_result r = ensure_prefill(c, L);
+    gx_result r = ensure_prefill(c, L, (size_t)c->max_tokens * L.U);
     if (r != GX_OK) return r;
     auto &p = c->pf;
     const int xb = x_dtype == GX_BF16;
@@ -365,6 +393,283 @@ gx_result enqueue_layer_prefill(gx_context *c, const Layer &L, const void *x, ui
     return GX_OK;
 }
 
+// ---- expert parallelism (world > 1) ------------------------------------------------------
+// Rank r serves experts [r*NE/W, (r+1)*NE/W). Per layer, every rank takes the same NCCL steps in
+// the same order, also with no tokens of its own: count exchange, dispatch of rotated token rows
+// (with their destination-local slots), the expert phase on what it received, and the return of
+// one weighted partial row per received row; the source adds the partial rows (+ residual).
+
+gx_result comm_result(gx_context *c, ncclResult_t r, const char *what) {
+    if (r == ncclSuccess) return GX_OK;
+    if (debug_enabled())
+        std::fprintf(stderr, "gyro_moe: %s: %s\n", what,
+                     r == ncclInProgress ? "no progress within the communication timeout" : c->nccl->GetErrorString(r));
+    c->broken = true;  // a lost peer leaves NCCL work queued; only gx_destroy (abort) is valid now
+    return GX_E_COMM;
+}
+
+gx_result comm_group_end(gx_context *c, const char *what) {
+    ncclResult_t r = c->nccl->GroupEnd();
+    if (r == ncclSuccess || r == ncclInProgress) r = gx::nccl_settle(c->nccl, c->comm, c->comm_timeout_ms);
+    return comm_result(c, r, what);
+}
+
+template <typename T>
+void free_dev(T *&p) {
+    if (p) cudaFree(p);
+    p = nullptr;
+}
+
+// Send-side buffers for world * max_tokens rows of the largest layer shape seen.
+gx_result ensure_ep_send(gx_context *c, const Layer &L) {
+    auto &e = c->ep;
+    const size_t W = c->world, T = c->max_tokens, rows = W * T;
+    if (!e.counts) {
+        GX_CUDA(cudaMalloc(&e.counts, 2 * W * sizeof(int)));
+        GX_CUDA(cudaMallocHost(&e.h_counts, 2 * W * sizeof(int)));
+        GX_CUDA(cudaEventCreateWithFlags(&e.counts_ready, cudaEventDisableTiming));
+    }
+    if (e.src_cap >= rows && e.E >= L.E && e.U >= L.U) return GX_OK;
+    free_dev(e.pos_of);
+    free_dev(e.send_ids);
+    free_dev(e.send_w);
+    free_dev(e.send_rows);
+    free_dev(e.ret_rows);
+    e.src_cap = 0;
+    const size_t E = std::max<size_t>(e.E, L.E), U = std::max<size_t>(e.U, L.U);
+    GX_CUDA(cudaMalloc(&e.pos_of, T * W * sizeof(int)));
+    GX_CUDA(cudaMalloc(&e.send_ids, rows * U * sizeof(uint32_t)));
+    GX_CUDA(cudaMalloc(&e.send_w, rows * U * sizeof(float)));
+    GX_CUDA(cudaMalloc(&e.send_rows, rows * E * sizeof(__half)));
+    GX_CUDA(cudaMalloc(&e.ret_rows, rows * E * sizeof(__half)));
+    e.src_cap = rows;
+    e.E = E;
+    e.U = U;
+    // receive buffers are sized for E and U too
+    free_dev(e.recv_rows);
+    free_dev(e.part_rows);
+    free_dev(e.recv_ids);
+    free_dev(e.recv_w);
+    e.recv_cap = 0;
+    return GX_OK;
+}
+
+// Receive-side buffers for R rows (grown geometrically, at most world * max_tokens).
+gx_result ensure_ep_recv(gx_context *c, size_t R) {
+    auto &e = c->ep;
+    if (e.recv_cap >= R) return GX_OK;
+    const size_t cap = std::min<size_t>(std::max<size_t>(R, 2 * e.recv_cap), e.src_cap);
+    free_dev(e.recv_rows);
+    free_dev(e.part_rows);
+    free_dev(e.recv_ids);
+    free_dev(e.recv_w);
+    e.recv_cap = 0;
+    GX_CUDA(cudaMalloc(&e.recv_rows, cap * e.E * sizeof(__half)));
+    GX_CUDA(cudaMalloc(&e.part_rows, cap * e.E * sizeof(__half)));
+    GX_CUDA(cudaMalloc(&e.recv_ids, cap * e.U * sizeof(uint32_t)));
+    GX_CUDA(cudaMalloc(&e.recv_w, cap * e.U * sizeof(float)));
+    e.recv_cap = cap;
+    return GX_OK;
+}
+
+// One layer across the expert-parallel group. ev (GX_FLAG_PROFILE): start, after the dispatch
+// exchange (selection, rotation, plan, counts, rows), after the gate/up GEMM, end (down GEMM,
+// partial rows, return exchange, sum).
+gx_result enqueue_layer_ep(gx_context *c, const Layer &L, const void *x, uint32_t x_dtype, uint32_t n_tok,
+                           const void *resid, uint32_t resid_dtype, void *out, uint32_t out_dtype, float norm_eps,
+                           cudaEvent_t *ev) {
+    const int W = (int)c->world;
+    const size_t E = L.E, U = L.U;
+    gx_result r = ensure_ep_send(c, L);
+    if (r != GX_OK) return r;
+    auto &e = c->ep;
+    const int xb = x_dtype == GX_BF16;
+    const size_t stride = n_tok ? n_tok : 1;  // send rows reserved per destination
+    if (ev) GX_CUDA(record_phase(ev[0], c->stream));
+    if (n_tok > 0) {
+        const int splits = (L.E % (4 * 32) == 0) ? 4 : 1;
+        GX_CUDA(gx::launch_router_gemm(L.router, x, xb, (int)n_tok, (int)L.n_expert, (int)L.E, c->logits, splits,
+                                       c->stream));
+        gx::RouterArgs ra{};
+        ra.W = L.router;
+        ra.bias = L.bias;
+        ra.x = x;
+        ra.x_bf16 = xb;
+        ra.n_tok = (int)n_tok;
+        ra.NE = (int)L.n_expert;
+        ra.E = (int)L.E;
+        ra.U = (int)L.U;
+        ra.scale = L.scale;
+        ra.norm_eps = norm_eps;
+        ra.ss = c->ss;
+        ra.ss_from_x = 1;
+        ra.logit_splits = splits;
+        ra.xscale = c->xscale;
+        ra.logits = c->logits;
+        ra.ids = c->ids;
+        ra.weights = c->weights;
+        ra.err = c->err;
+        GX_CUDA(gx::launch_topk(ra, c->stream));
+    }
+    gx::EpPlanArgs pa{};
+    pa.ids = c->ids;
+    pa.weights = c->weights;
+    pa.n_tok = (int)n_tok;
+    pa.U = (int)U;
+    pa.NE = (int)L.n_expert;
+    pa.W = W;
+    pa.stride = (int)stride;
+    pa.pos_of = e.pos_of;
+    pa.send_ids = e.send_ids;
+    pa.send_w = e.send_w;
+    pa.send_count = e.counts;
+    pa.err = c->err;
+    GX_CUDA(gx::launch_ep_plan(pa, c->stream));
+    GX_CUDA(gx::launch_rotate_tokens(x, xb, norm_eps > 0.f ? c->xscale : nullptr, L.gate_signs, (int)n_tok, (int)E,
+                                     e.send_rows, c->stream, e.pos_of, W));
+    // counts: rank d learns how many rows each source sends it
+    c->nccl->GroupStart();
+    for (int d = 0; d < W; ++d) {
+        c->nccl->Send(e.counts + d, 1, ncclInt32, d, c->comm, c->stream);
+        c->nccl->Recv(e.counts + W + d, 1, ncclInt32, d, c->comm, c->stream);
+    }
+    r = comm_group_end(c, "count exchange");
+    if (r != GX_OK) return r;
+    GX_CUDA(cudaMemcpyAsync(e.h_counts, e.counts, 2 * W * sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+    GX_CUDA(cudaEventRecord(e.counts_ready, c->stream));
+    r = wait_event(c, e.counts_ready, c->comm_timeout_ms);
+    if (r == GX_E_TIMEOUT) return comm_result(c, ncclInProgress, "count exchange");
+    if (r != GX_OK) return r;
+    std::vector<size_t> scnt(W), rcnt(W), roff(W);
+    size_t R = 0;
+    for (int d = 0; d < W; ++d) {
+        scnt[d] = (size_t)e.h_counts[d];
+        rcnt[d] = (size_t)e.h_counts[W + d];
+        roff[d] = R;
+        R += rcnt[d];
+    }
+    if (R > e.src_cap) return comm_result(c, ncclInvalidUsage, "received more rows than the group can hold");
+    r = ensure_ep_recv(c, R);
+    if (r != GX_OK) return r;
+    if (R > 0) {
+        r = ensure_prefill(c, L, R * U);
+        if (r != GX_OK) return r;
+    }
+    c->nccl->GroupStart();
+    for (int d = 0; d < W; ++d) {
+        const size_t so = (size_t)d * stride;
+        if (scnt[d]) {
+            c->nccl->Send(e.send_rows + so * E, scnt[d] * E, ncclFloat16, d, c->comm, c->stream);
+            c->nccl->Send(e.send_ids + so * U, scnt[d] * U, ncclUint32, d, c->comm, c->stream);
+            c->nccl->Send(e.send_w + so * U, scnt[d] * U, ncclFloat32, d, c->comm, c->stream);
+        }
+        if (rcnt[d]) {
+            c->nccl->Recv(e.recv_rows + roff[d] * E, rcnt[d] * E, ncclFloat16, d, c->comm, c->stream);
+            c->nccl->Recv(e.recv_ids + roff[d] * U, rcnt[d] * U, ncclUint32, d, c->comm, c->stream);
+            c->nccl->Recv(e.recv_w + roff[d] * U, rcnt[d] * U, ncclFloat32, d, c->comm, c->stream);
+        }
+    }
+    r = comm_group_end(c, "dispatch");
+    if (r != GX_OK) return r;
+    if (ev) GX_CUDA(record_phase(ev[1], c->stream));
+    if (R > 0) {
+        auto &p = c->pf;
+        gx::GroupArgs ga{};
+        ga.ids = e.recv_ids;
+        ga.n_slots = (int)(R * U);
+        ga.NE = (int)L.local_experts;
+        ga.expert_count = p.expert_count;
+        ga.tile_expert = p.tile_expert;
+        ga.tile_rows = p.tile_rows;
+        ga.n_mtiles = p.n_mtiles;
+        ga.row_slot = p.row_slot;
+        ga.slot_row = p.slot_row;
+        ga.err = c->err;
+        GX_CUDA(gx::launch_group(ga, c->stream));
+        gx::PackArgs pk{};
+        pk.by_token = 1;
+        pk.U = (int)U;
+        pk.K = (int)E;
+        pk.xh = e.recv_rows;
+        pk.row_slot = p.row_slot;
+        pk.tile_rows = p.tile_rows;
+        pk.n_mtiles = p.n_mtiles;
+        pk.dst = p.A;
+        GX_CUDA(gx::launch_pack_rows(pk, (int)p.max_tiles, c->stream));
+        gx::GemmArgs gm{};
+        gm.type = L.type;
+        gm.w0 = L.gate;
+        gm.w1 = L.up;
+        gm.expert_bytes = L.gate_expert_bytes;
+        gm.K = (int)L.E;
+        gm.n_ntiles = (int)(L.F / 128);
+        gm.n_expert = (int)L.local_experts;
+        gm.A = p.A;
+        gm.tile_expert = p.tile_expert;
+        gm.tile_rows = p.tile_rows;
+        gm.n_mtiles = p.n_mtiles;
+        gm.act = p.act;
+        gm.F = (int)L.F;
+        gm.Y = p.Y;
+        gm.E = (int)L.E;
+        gm.codebook = c->codebook;
+        gm.err = c->err;
+        GX_CUDA(gx::launch_moe_gemm(gm, 0, c->sm_count, c->stream));
+        if (ev) GX_CUDA(record_phase(ev[2], c->stream));
+        gx::PackArgs pd{};
+        pd.src = p.act;
+        pd.by_token = 0;
+        pd.U = (int)U;
+        pd.K = (int)L.F;
+        pd.signs = L.down_signs;
+        pd.row_slot = p.row_slot;
+        pd.tile_rows = p.tile_rows;
+        pd.n_mtiles = p.n_mtiles;
+        pd.dst = p.A2;
+        GX_CUDA(gx::launch_pack_rows(pd, (int)p.max_tiles, c->stream));
+        gm.w0 = L.down;
+        gm.w1 = nullptr;
+        gm.expert_bytes = L.down_expert_bytes;
+        gm.K = (int)L.F;
+        gm.n_ntiles = (int)(L.E / 256);
+        gm.A = p.A2;
+        GX_CUDA(gx::launch_moe_gemm(gm, 1, c->sm_count, c->stream));
+        gx::CombineArgs ca{};
+        ca.Y = p.Y;
+        ca.slot_row = p.slot_row;
+        ca.weights = e.recv_w;
+        ca.out = e.part_rows;
+        ca.out_f16 = 1;
+        ca.n_tok = (int)R;
+        ca.U = (int)U;
+        ca.E = (int)E;
+        GX_CUDA(gx::launch_combine(ca, c->stream));
+    } else if (ev) {
+        GX_CUDA(record_phase(ev[2], c->stream));
+    }
+    c->nccl->GroupStart();
+    for (int d = 0; d < W; ++d) {
+        if (rcnt[d]) c->nccl->Send(e.part_rows + roff[d] * E, rcnt[d] * E, ncclFloat16, d, c->comm, c->stream);
+        if (scnt[d])
+            c->nccl->Recv(e.ret_rows + (size_t)d * stride * E, scnt[d] * E, ncclFloat16, d, c->comm, c->stream);
+    }
+    r = comm_group_end(c, "combine");
+    if (r != GX_OK) return r;
+    gx::EpCombineArgs ec{};
+    ec.ret = e.ret_rows;
+    ec.pos_of = e.pos_of;
+    ec.W = W;
+    ec.resid = resid;
+    ec.resid_bf16 = resid_dtype == GX_BF16;
+    ec.out = out;
+    ec.out_bf16 = out_dtype == GX_BF16;
+    ec.n_tok = (int)n_tok;
+    ec.E = (int)E;
+    GX_CUDA(gx::launch_ep_combine(ec, c->stream));
+    if (ev) GX_CUDA(record_phase(ev[3], c->stream));
+    return GX_OK;
+}
+
 // One routed layer: router + top-k, gate/up + SwiGLU, down + combine (+ residual).
 // prof_slot >= 0 records the phase events of layer slot prof_slot (GX_FLAG_PROFILE).
 // norm_eps > 0 routes and feeds the experts RMSNorm(x) (unit weight); the residual stays x.
@@ -372,6 +677,10 @@ gx_result enqueue_layer_prefill(gx_context *c, const Layer &L, const void *x, ui
 gx_result enqueue_layer(gx_context *c, const Layer &L, const void *x, uint32_t x_dtype, uint32_t n_tok,
                         const void *resid, uint32_t resid_dtype, void *out, uint32_t out_dtype, int prof_slot,
                         float norm_eps, bool chained) {
+    if (c->world > 1) {
+        cudaEvent_t *pev = prof_slot >= 0 ? &c->prof[4 * (size_t)prof_slot] : nullptr;
+        return enqueue_layer_ep(c, L, x, x_dtype, n_tok, resid, resid_dtype, out, out_dtype, norm_eps, pev);
+    }
     if (n_tok >= kPrefillMinTokens && L.n_expert <= 512 && L.E % 256 == 0) {
         cudaEvent_t *pev = prof_slot >= 0 ? &c->prof[4 * (size_t)prof_slot] : nullptr;
         return enqueue_layer_prefill(c, L, x, x_dtype, n_tok, resid, resid_dtype, out, out_dtype, norm_eps, pev);
@@ -486,15 +795,50 @@ gx_result stack_enqueue(gx_context *c, uint32_t first, uint32_t n_layers, const 
     return GX_OK;
 }
 
+// Joins the expert-parallel group: a non-blocking NCCL communicator over all ranks' contexts,
+// bounded by the communication timeout (GX_COMM_TIMEOUT_MS in the environment, default 120 s).
+gx_result open_group(gx_context *c, const gx_options *o) {
+    c->nccl = gx::nccl_api();
+    if (!c->nccl) return GX_E_UNSUPPORTED;
+    if (const char *v = std::getenv("GX_COMM_TIMEOUT_MS")) {
+        const long ms = std::strtol(v, nullptr, 10);
+        if (ms > 0) c->comm_timeout_ms = (uint32_t)ms;
+    }
+    ncclUniqueId id;
+    std::memcpy(id.internal, o->nccl_id, sizeof(id.internal));
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.blocking = 0;
+    ncclResult_t nr = c->nccl->CommInitRankConfig(&c->comm, (int)c->world, id, (int)c->rank, &cfg);
+    if (nr == ncclSuccess || nr == ncclInProgress) nr = gx::nccl_settle(c->nccl, c->comm, c->comm_timeout_ms);
+    if (nr != ncclSuccess) {
+        if (debug_enabled())
+            std::fprintf(stderr, "gyro_moe: joining the expert-parallel group failed: %s\n",
+                         nr == ncclInProgress ? "not all ranks joined within the timeout" : c->nccl->GetErrorString(nr));
+        if (c->comm) c->nccl->CommAbort(c->comm);
+        c->comm = nullptr;
+        return GX_E_COMM;
+    }
+    return GX_OK;
+}
+
 }  // namespace
 
 extern "C" {
 
+GX_API gx_result gx_comm_unique_id(uint8_t *out_id, uint64_t bytes) {
+    if (!out_id || bytes != sizeof(ncclUniqueId)) return GX_E_INVALIDARG;
+    const gx::NcclApi *api = gx::nccl_api();
+    if (!api) return GX_E_UNSUPPORTED;
+    ncclUniqueId id;
+    if (api->GetUniqueId(&id) != ncclSuccess) return GX_E_COMM;
+    std::memcpy(out_id, id.internal, sizeof(id.internal));
+    return GX_OK;
+}
+
 GX_API gx_result gx_create(const gx_options *o, gx_context **out) {
     if (!o || !out || !o->codebook || o->codebook_bytes != 8192 || o->world == 0 || o->rank >= o->world ||
-        o->max_tokens == 0 || o->max_layers == 0 || o->max_tokens > (1u << 20))
+        o->max_tokens == 0 || o->max_layers == 0 || o->max_tokens > (1u << 20) || o->world > 512)
         return GX_E_INVALIDARG;
-    if (o->world > 1) return GX_E_UNSUPPORTED;
     *out = nullptr;
     int n = 0;
     if (cudaGetDeviceCount(&n) != cudaSuccess || (int)o->device >= n) return GX_E_INVALIDARG;
@@ -523,6 +867,8 @@ GX_API gx_result gx_create(const gx_options *o, gx_context **out) {
         if (cudaMalloc(&c->codebook, 8192) != cudaSuccess) { r = GX_E_OUTOFMEMORY; break; }
         if (cudaMemcpy(c->codebook, o->codebook, 8192, cudaMemcpyHostToDevice) != cudaSuccess) { r = GX_E_DEVICE; break; }
         r = ensure_scratch(c);
+        if (r != GX_OK || c->world == 1) break;
+        r = open_group(c, o);
     } while (false);
     if (r != GX_OK) {
         release_all(c);
@@ -568,6 +914,7 @@ GX_API gx_result gx_upload_layer(gx_context *c, uint32_t layer, const gx_layer_d
         return GX_E_INVALIDARG;
     if (d->n_used * (d->n_ff / 128) > 64) return GX_E_UNSUPPORTED;
     if (d->n_expert % c->world) return GX_E_INVALIDARG;
+    if (c->world > 1 && d->n_embd % 256) return GX_E_UNSUPPORTED;  // expert-parallel rows use the GEMM path
     const uint64_t bb = (uint64_t)gx::type_block_bytes(d->type_id);
     const uint64_t E = d->n_embd, F = d->n_ff, NE = d->n_expert;
     const uint64_t gate_row = E / 128 * bb, down_row = F / 128 * bb;
@@ -675,11 +1022,13 @@ GX_API gx_result gx_moe_forward(gx_context *c, uint32_t layer, const void *x, ui
         return GX_E_INVALIDARG;
     GX_CUDA(cudaSetDevice(c->device));
     const Layer &L = c->layers[layer];
-    if (n_tok > 0) {
+    if (n_tok > 0 || c->world > 1) {  // with world > 1 every rank takes part in the exchange
         const bool prof = (c->flags & GX_FLAG_PROFILE) != 0;
         if (prof) c->prof_layers = 1;
         r = enqueue_layer(c, L, x, x_dtype, n_tok, nullptr, GX_F32, y, y_dtype, prof ? 0 : -1, 0.f, false);
         if (r != GX_OK) return r;
+    }
+    if (n_tok > 0) {
         if (ids) GX_CUDA(cudaMemcpyAsync(ids, c->ids, (size_t)n_tok * L.U * 4, cudaMemcpyDeviceToDevice, c->stream));
         if (weights)
             GX_CUDA(cudaMemcpyAsync(weights, c->weights, (size_t)n_tok * L.U * 4, cudaMemcpyDeviceToDevice, c->stream));
@@ -691,13 +1040,15 @@ GX_API gx_result gx_moe_forward_host(gx_context *c, uint32_t layer, const void *
                                      void *y, uint32_t y_dtype, uint32_t *ids, float *weights, uint32_t timeout_ms) {
     gx_result r = check_forward(c, layer, x_dtype, n_tok, y_dtype);
     if (r != GX_OK) return r;
-    if (n_tok == 0) return GX_OK;
-    if (!x || !y) return GX_E_INVALIDARG;
+    if (n_tok == 0 && c->world == 1) return GX_OK;
+    if (n_tok > 0 && (!x || !y)) return GX_E_INVALIDARG;
     GX_CUDA(cudaSetDevice(c->device));
     const Layer &L = c->layers[layer];
     const size_t in_b = (size_t)n_tok * L.E * dtype_size(x_dtype), out_b = (size_t)n_tok * L.E * dtype_size(y_dtype);
-    std::memcpy(c->h_in, x, in_b);
-    GX_CUDA(cudaMemcpyAsync(c->x_stage, c->h_in, in_b, cudaMemcpyHostToDevice, c->stream));
+    if (in_b) {
+        std::memcpy(c->h_in, x, in_b);
+        GX_CUDA(cudaMemcpyAsync(c->x_stage, c->h_in, in_b, cudaMemcpyHostToDevice, c->stream));
+    }
     const bool prof = (c->flags & GX_FLAG_PROFILE) != 0;
     if (prof) c->prof_layers = 1;
     r = enqueue_layer(c, L, c->x_stage, x_dtype, n_tok, nullptr, GX_F32, c->y_stage, y_dtype, prof ? 0 : -1, 0.f,
@@ -705,14 +1056,14 @@ GX_API gx_result gx_moe_forward_host(gx_context *c, uint32_t layer, const void *
     if (r != GX_OK) return r;
     uint8_t *ho = static_cast<uint8_t *>(c->h_out);
     const size_t sel_b = (size_t)n_tok * L.U * 4;
-    GX_CUDA(cudaMemcpyAsync(ho, c->y_stage, out_b, cudaMemcpyDeviceToHost, c->stream));
+    if (out_b) GX_CUDA(cudaMemcpyAsync(ho, c->y_stage, out_b, cudaMemcpyDeviceToHost, c->stream));
     if (ids) GX_CUDA(cudaMemcpyAsync(ho + c->stage_bytes, c->ids, sel_b, cudaMemcpyDeviceToHost, c->stream));
     if (weights) GX_CUDA(cudaMemcpyAsync(ho + c->stage_bytes + sel_b, c->weights, sel_b, cudaMemcpyDeviceToHost, c->stream));
     r = sync_all(c, timeout_ms);
     if (r != GX_OK) return r;
-    std::memcpy(y, ho, out_b);
-    if (ids) std::memcpy(ids, ho + c->stage_bytes, sel_b);
-    if (weights) std::memcpy(weights, ho + c->stage_bytes + sel_b, sel_b);
+    if (out_b) std::memcpy(y, ho, out_b);
+    if (ids && sel_b) std::memcpy(ids, ho + c->stage_bytes, sel_b);
+    if (weights && sel_b) std::memcpy(weights, ho + c->stage_bytes + sel_b, sel_b);
     return GX_OK;
 }
 
@@ -724,11 +1075,19 @@ GX_API gx_result gx_stack_forward(gx_context *c, uint32_t first, uint32_t n_laye
         if (r != GX_OK) return r;
         if (c->layers[first + i].E != c->layers[first].E) return GX_E_INVALIDARG;
     }
-    if (n_tok == 0) return record_ticket(c, out_ticket);
-    if (!x || !y || ((uintptr_t)y & 3)) return GX_E_INVALIDARG;
+    if (n_tok == 0 && c->world == 1) return record_ticket(c, out_ticket);
+    if (n_tok > 0 && (!x || !y || ((uintptr_t)y & 3))) return GX_E_INVALIDARG;
     GX_CUDA(cudaSetDevice(c->device));
     const size_t E = c->layers[first].E;
     const size_t in_b = n_tok * E * dtype_size(x_dtype), out_b = n_tok * E * dtype_size(y_dtype);
+    if (c->world > 1) {
+        // The exchange sizes are read back per layer, so the chain runs eagerly (no graph).
+        if (in_b) GX_CUDA(cudaMemcpyAsync(c->x_stage, x, in_b, cudaMemcpyDeviceToDevice, c->stream));
+        gx_result r = stack_enqueue(c, first, n_layers, c->x_stage, x_dtype, n_tok, c->y_stage, y_dtype);
+        if (r != GX_OK) return r;
+        if (out_b) GX_CUDA(cudaMemcpyAsync(y, c->y_stage, out_b, cudaMemcpyDeviceToDevice, c->stream));
+        return record_ticket(c, out_ticket);
+    }
     // The graph reads x_stage and writes y_stage; the caller's buffers are copied around it.
     GX_CUDA(cudaMemcpyAsync(c->x_stage, x, in_b, cudaMemcpyDeviceToDevice, c->stream));
     const GraphKey key{first, n_layers, n_tok, x_dtype, y_dtype, c->flags};
@@ -764,21 +1123,23 @@ GX_API gx_result gx_stack_forward_host(gx_context *c, uint32_t first, uint32_t n
                                        uint32_t x_dtype, uint32_t n_tok, void *y, uint32_t y_dtype,
                                        uint32_t timeout_ms) {
     if (!c || n_layers == 0 || (uint64_t)first + n_layers > c->layers.size()) return GX_E_INVALIDARG;
-    if (n_tok == 0) return GX_OK;
-    if (!x || !y || n_tok > c->max_tokens) return GX_E_INVALIDARG;
+    if (n_tok == 0 && c->world == 1) return GX_OK;
+    if ((n_tok > 0 && (!x || !y)) || n_tok > c->max_tokens) return GX_E_INVALIDARG;
     if (!c->layers[first].ready) return GX_E_STATE;
     const size_t E = c->layers[first].E;
     const size_t in_b = n_tok * E * dtype_size(x_dtype), out_b = n_tok * E * dtype_size(y_dtype);
-    std::memcpy(c->h_in, x, in_b);
     GX_CUDA(cudaSetDevice(c->device));
-    GX_CUDA(cudaMemcpyAsync(c->xbuf[0], c->h_in, in_b, cudaMemcpyHostToDevice, c->stream));
+    if (in_b) {
+        std::memcpy(c->h_in, x, in_b);
+        GX_CUDA(cudaMemcpyAsync(c->xbuf[0], c->h_in, in_b, cudaMemcpyHostToDevice, c->stream));
+    }
     // xbuf[0] holds the input only until the stack's staging copy has read it.
     gx_result r = gx_stack_forward(c, first, n_layers, c->xbuf[0], x_dtype, n_tok, c->y_stage, y_dtype, nullptr);
     if (r != GX_OK) return r;
-    GX_CUDA(cudaMemcpyAsync(c->h_out, c->y_stage, out_b, cudaMemcpyDeviceToHost, c->stream));
+    if (out_b) GX_CUDA(cudaMemcpyAsync(c->h_out, c->y_stage, out_b, cudaMemcpyDeviceToHost, c->stream));
     r = sync_all(c, timeout_ms);
     if (r != GX_OK) return r;
-    std::memcpy(y, c->h_out, out_b);
+    if (out_b) std::memcpy(y, c->h_out, out_b);
     return GX_OK;
 }
 
@@ -1003,6 +1364,7 @@ GX_API gx_result gx_moe_forward_noalloc(gx_context *c, uint32_t layer, const voi
                                         uint64_t *out_ticket) {
     if (!c) return GX_E_INVALIDARG;
     if (c->broken) return GX_E_DEVICE;
+    if (c->world > 1) return GX_E_UNSUPPORTED;  // the decode kernels need every expert on this device
     if (layer >= c->layers.size() || !c->layers[layer].ready) return GX_E_STATE;
     if ((x_dtype != GX_F32 && x_dtype != GX_BF16) || (y_dtype != GX_F32 && y_dtype != GX_BF16)) return GX_E_INVALIDARG;
     if (n_tok > kNoAllocMaxTokens) {

@@ -1,0 +1,53 @@
+// gx_comm.cu — run-time binding of NCCL (see gx_comm.h).
+#include <dlfcn.h>
+
+#include <chrono>
+#include <mutex>
+#include <thread>
+
+#include "gx_comm.h"
+
+namespace gx {
+
+namespace {
+
+template <typename F>
+bool bind(void *h, F &fn, const char *name) {
+    fn = reinterpret_cast<F>(dlsym(h, name));
+    return fn != nullptr;
+}
+
+}  // namespace
+
+const NcclApi *nccl_api() {
+    static NcclApi api{};
+    static bool ok = false;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) return;
+        ok = bind(h, api.GetUniqueId, "ncclGetUniqueId") && bind(h, api.CommInitRankConfig, "ncclCommInitRankConfig") &&
+             bind(h, api.CommGetAsyncError, "ncclCommGetAsyncError") && bind(h, api.CommAbort, "ncclCommAbort") &&
+             bind(h, api.CommDestroy, "ncclCommDestroy") && bind(h, api.GroupStart, "ncclGroupStart") &&
+             bind(h, api.GroupEnd, "ncclGroupEnd") && bind(h, api.Send, "ncclSend") && bind(h, api.Recv, "ncclRecv") &&
+             bind(h, api.GetErrorString, "ncclGetErrorString") && bind(h, api.GetVersion, "ncclGetVersion");
+    });
+    return ok ? &api : nullptr;
+}
+
+ncclResult_t nccl_settle(const NcclApi *api, ncclComm_t comm, uint32_t timeout_ms) {
+    const auto start = std::chrono::steady_clock::now();
+    for (;;) {
+        ncclResult_t st = ncclSuccess;
+        const ncclResult_t r = api->CommGetAsyncError(comm, &st);
+        if (r != ncclSuccess) return r;
+        if (st != ncclInProgress) return st;
+        const auto ms =
+            std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - start).count();
+        if ((uint64_t)ms >= timeout_ms) return ncclInProgress;
+        std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+}
+
+}  // namespace gx

@@ -122,13 +122,44 @@ struct CombineArgs {
     int resid_bf16;
     void *out;
     int out_bf16;
+    int out_f16;             // f16 output (expert-parallel partial rows); overrides out_bf16
     int n_tok, U, E;
 };
 
 cudaError_t launch_router_gemm(const float *W, const void *x, int x_bf16, int n_tok, int NE, int E, float *C,
                                int splits, cudaStream_t s);
 cudaError_t launch_rotate_tokens(const void *x, int x_bf16, const float *xscale, const float *signs, int n_tok,
-                                int E, __half *xh, cudaStream_t s);
+                                int E, __half *xh, cudaStream_t s, const int *scatter = nullptr, int n_dst = 0);
+
+// ---- expert parallelism: dispatch plan and the source-side sum of returned rows ----------
+// Slot id meaning "no expert of this rank" in expert-parallel rows.
+constexpr uint32_t kNoSlot = 0xffffffffu;
+
+struct EpPlanArgs {
+    const uint32_t *ids;     // [n_tok][U] global expert ids from the selection
+    const float *weights;    // [n_tok][U]
+    int n_tok, U, NE, W;     // rank d serves experts [d*NE/W, (d+1)*NE/W)
+    int stride;              // send-buffer rows reserved per destination (>= n_tok)
+    int *pos_of;             // [n_tok][W] send row of (token, destination), -1 if none
+    uint32_t *send_ids;      // [W*stride][U] destination-local expert id or kNoSlot
+    float *send_w;           // [W*stride][U] routing weight (0 for kNoSlot)
+    int *send_count;         // [W] rows per destination
+    int *err;
+};
+
+struct EpCombineArgs {
+    const __half *ret;       // returned partial rows, laid out as the send buffer
+    const int *pos_of;       // [n_tok][W]
+    int W;
+    const void *resid;       // [n_tok][E] or nullptr
+    int resid_bf16;
+    void *out;               // [n_tok][E]
+    int out_bf16;
+    int n_tok, E;
+};
+
+cudaError_t launch_ep_plan(const EpPlanArgs &a, cudaStream_t s);
+cudaError_t launch_ep_combine(const EpCombineArgs &a, cudaStream_t s);
 cudaError_t launch_group(const GroupArgs &a, cudaStream_t s);
 cudaError_t launch_pack_rows(const PackArgs &a, int max_tiles, cudaStream_t s);
 cudaError_t launch_moe_gemm(const GemmArgs &a, int mode, int sm_count, cudaStream_t s);

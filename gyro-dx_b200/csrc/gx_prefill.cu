@@ -85,7 +85,8 @@ __global__ void __launch_bounds__(256) router_gemm_kernel(const float *__restric
 
 // ------------------------------------------------------------------------------------------
 // Grouping: one CTA of 1024 threads. Stable order of slots within each expert (the counting
-// sort of src/engine.zig:553-564), each expert's rows padded to whole 128-row tiles.
+// sort of src/engine.zig:553-564), each expert's rows padded to whole 128-row tiles. Slots whose
+// id is kNoSlot (expert-parallel rows carry them for experts of other ranks) get no row.
 // ------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(1024) group_kernel(GroupArgs a) {
     extern __shared__ __align__(16) int gsm[];
@@ -99,7 +100,7 @@ __global__ void __launch_bounds__(1024) group_kernel(GroupArgs a) {
     for (int s = tid; s < a.n_slots; s += 1024) {
         const uint32_t e = a.ids[s];
         if (e < (uint32_t)a.NE) atomicAdd(&count[e], 1);
-        else atomicExch(a.err, KERR_BOUNDS);
+        else if (e != kNoSlot) atomicExch(a.err, KERR_BOUNDS);
     }
     __syncthreads();
     if (tid == 0) {
@@ -131,6 +132,7 @@ __global__ void __launch_bounds__(1024) group_kernel(GroupArgs a) {
         const int rank_w = __popc(same & ((1u << lane) - 1u));
         if (ok && rank_w == 0) wcount[warp * a.NE + e] = __popc(same);
         __syncthreads();
+        if (live && !ok) a.slot_row[s] = -1;
         if (ok) {
             int before = run[e] + rank_w;
             for (int w = 0; w < warp; ++w) before += wcount[w * a.NE + e];
@@ -150,10 +152,13 @@ __global__ void __launch_bounds__(1024) group_kernel(GroupArgs a) {
 
 // ------------------------------------------------------------------------------------------
 // Token rotation, once per token: xh[t] = f16(H128((x[t] * scale[t]) * signs) / sqrt(128)) per
-// 128-column block (src/engine.zig:547-551), one warp per (token, 4 blocks).
+// 128-column block (src/engine.zig:547-551), one warp per (token, 4 blocks). With scatter, the
+// row goes instead to rows scatter[t][0..n_dst) of xh that are >= 0 (the expert-parallel send
+// buffer: one copy per destination rank that serves one of the token's experts).
 // ------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) rotate_tokens_kernel(const void *x, int x_bf16, const float *xscale,
-                                                            const float *signs, int n_tok, int E, __half *xh) {
+                                                            const float *signs, int n_tok, int E, __half *xh,
+                                                            const int *scatter, int n_dst) {
     const int lane = threadIdx.x & 31;
     const long long w = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
     const int nb = E / 128, groups = (nb + 3) / 4;
@@ -181,7 +186,14 @@ __global__ void __launch_bounds__(256) rotate_tokens_kernel(const void *x, int x
         uint2 o;
         o.x = pack_half2(v[q][0], v[q][1]);
         o.y = pack_half2(v[q][2], v[q][3]);
-        *reinterpret_cast<uint2 *>(xh + (size_t)t * E + b * 128 + 4 * lane) = o;
+        if (!scatter) {
+            *reinterpret_cast<uint2 *>(xh + (size_t)t * E + b * 128 + 4 * lane) = o;
+            continue;
+        }
+        for (int d = 0; d < n_dst; ++d) {
+            const int row = scatter[(size_t)t * n_dst + d];
+            if (row >= 0) *reinterpret_cast<uint2 *>(xh + (size_t)row * E + b * 128 + 4 * lane) = o;
+        }
     }
 }
 
@@ -520,7 +532,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) moe_gemm_kernel(GemmArgs a) {
 }
 
 // ------------------------------------------------------------------------------------------
-// Combine: out[t] = sum_k w[t][k] * Y[row(t, k)] (+ resid[t]); 4 columns per thread.
+// Combine: out[t] = sum_k w[t][k] * Y[row(t, k)] (+ resid[t]); 4 columns per thread. Slots
+// without a row (row < 0: served by another rank) add nothing.
 // ------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) combine_kernel(CombineArgs a) {
     const long long i = (long long)blockIdx.x * 256 + threadIdx.x;
@@ -529,8 +542,9 @@ __global__ void __launch_bounds__(256) combine_kernel(CombineArgs a) {
     const int t = (int)(i / per_row), c = (int)(i % per_row) * 4;
     float v[4] = {0.f, 0.f, 0.f, 0.f};
     for (int k = 0; k < a.U; ++k) {
-        const float w = a.weights[t * a.U + k];
         const int row = a.slot_row[t * a.U + k];
+        if (row < 0) continue;
+        const float w = a.weights[t * a.U + k];
         const uint2 q = *reinterpret_cast<const uint2 *>(a.Y + (size_t)row * a.E + c);
         const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&q.x));
         const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(&q.y));
@@ -543,7 +557,9 @@ __global__ void __launch_bounds__(256) combine_kernel(CombineArgs a) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         if (a.resid) v[j] = load_act(a.resid, a.resid_bf16, o + j) + v[j];
-        if (a.out_bf16)
+        if (a.out_f16)
+            reinterpret_cast<__half *>(a.out)[o + j] = __float2half_rn(v[j]);
+        else if (a.out_bf16)
             reinterpret_cast<__nv_bfloat16 *>(a.out)[o + j] = __float2bfloat16_rn(v[j]);
         else
             reinterpret_cast<float *>(a.out)[o + j] = v[j];
@@ -608,10 +624,11 @@ cudaError_t launch_moe_gemm(const GemmArgs &a, int mode, int sm_count, cudaStrea
 }
 
 cudaError_t launch_rotate_tokens(const void *x, int x_bf16, const float *xscale, const float *signs, int n_tok,
-                                int E, __half *xh, cudaStream_t s) {
+                                int E, __half *xh, cudaStream_t s, const int *scatter, int n_dst) {
     const long long warps = (long long)n_tok * ((E / 128 + 3) / 4);
     if (warps == 0) return cudaSuccess;
-    rotate_tokens_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(x, x_bf16, xscale, signs, n_tok, E, xh);
+    rotate_tokens_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(x, x_bf16, xscale, signs, n_tok, E, xh,
+                                                                      scatter, n_dst);
     return cudaGetLastError();
 }
 

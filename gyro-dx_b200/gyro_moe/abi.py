@@ -63,6 +63,7 @@ assert ctypes.sizeof(Options) == 168 and ctypes.sizeof(Caps) == 192 and ctypes.s
 _P, _U32, _U64, _F = ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_float
 SIGNATURES = {
     "gx_create": [ctypes.POINTER(Options), ctypes.POINTER(_P)],
+    "gx_comm_unique_id": [ctypes.c_char_p, _U64],
     "gx_get_caps": [_P, ctypes.POINTER(Caps)],
     "gx_upload_layer": [_P, _U32, ctypes.POINTER(LayerDesc), _U32],
     "gx_moe_forward": [_P, _U32, _P, _U32, _U32, _P, _U32, _P, _P, ctypes.POINTER(_U64)],
@@ -127,6 +128,13 @@ def _dtype_code(a) -> int:
     if name == "uint16":  # numpy bf16 bit patterns
         return GX_BF16
     raise ValueError(f"unsupported activation dtype {name}")
+
+
+def unique_id() -> bytes:
+    """A fresh NCCL unique id for gx_options.nccl_id (rank 0 makes it, the others receive it)."""
+    buf = ctypes.create_string_buffer(128)
+    _check(load().gx_comm_unique_id(buf, 128), "gx_comm_unique_id")
+    return buf.raw
 
 
 class Context:

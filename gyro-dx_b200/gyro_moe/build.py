@@ -16,8 +16,8 @@ PKG = Path(__file__).resolve().parent
 CSRC = PKG.parent / "csrc"
 ROOT = PKG.parents[1]
 LIB = PKG / "libgyromoe.so"
-SOURCES = ["gx_kernels.cu", "gx_prefill.cu", "gx_abi.cu"]
-HEADERS = ["gx_tile.h", "gx_device.cuh", "gx_internal.h", "gx_umma.cuh"]
+SOURCES = ["gx_kernels.cu", "gx_prefill.cu", "gx_ep.cu", "gx_comm.cu", "gx_abi.cu"]
+HEADERS = ["gx_tile.h", "gx_device.cuh", "gx_internal.h", "gx_umma.cuh", "gx_comm.h"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-fvisibility=hidden", "--expt-relaxed-constexpr",
@@ -46,7 +46,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         subprocess.run(cmd, check=True)
         objs.append(str(obj))
     tmp = LIB.with_suffix(".so.tmp")
-    subprocess.run([NVCC, *ARCH, "-shared", "-cudart", "static", *objs, "-o", str(tmp)], check=True)
+    subprocess.run([NVCC, *ARCH, "-shared", "-cudart", "static", *objs, "-ldl", "-o", str(tmp)], check=True)
     os.replace(tmp, LIB)
     return LIB
 

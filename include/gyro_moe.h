@@ -123,9 +123,18 @@ typedef struct gx_timings {
 } gx_timings;
 
 /* Opens a context on one device (replaces gd_create, native/include/gyro_native.h:71).
- * With world > 1 every rank calls it with the same nccl_id; experts are then sharded:
- * rank r owns experts [r*n_expert/world, (r+1)*n_expert/world). */
+ * With world > 1 every rank (one process or thread per GPU) calls it with the same nccl_id, and
+ * the call returns once all ranks have joined (GX_E_COMM if they have not within the
+ * communication timeout: GX_COMM_TIMEOUT_MS in the environment, default 120000). Experts are
+ * then sharded: rank r holds experts [r*n_expert/world, (r+1)*n_expert/world) of every layer,
+ * and every forward call is a collective (see gx_moe_forward). NCCL (libnccl.so.2) is loaded
+ * only for world > 1; GX_E_UNSUPPORTED if it cannot be found. */
 GX_API gx_result gx_create(const gx_options *options, gx_context **out_context);
+
+/* No counterpart in the reference (its bridge drives one GPU). Writes a new NCCL unique id
+ * (bytes must be 128) for gx_options.nccl_id: rank 0 calls it and hands the bytes to the other
+ * ranks over the host's own channel. */
+GX_API gx_result gx_comm_unique_id(uint8_t *out_id, uint64_t bytes);
 
 /* Replaces gd_get_caps (native/include/gyro_native.h:72). */
 GX_API gx_result gx_get_caps(gx_context *context, gx_caps *out_caps);
@@ -144,7 +153,13 @@ GX_API gx_result gx_upload_layer(gx_context *context, uint32_t layer, const gx_l
  * x: [n_tok][E] device, x_dtype GX_F32/GX_BF16; y: [n_tok][E] device, y_dtype GX_F32/GX_BF16.
  * ids/weights: optional device outputs [n_tok][U] (the ffn_moe_topk observation), or NULL.
  * out_ticket: optional; completes when y is written. With world > 1 this is a collective:
- * every rank calls it for its own tokens (n_tok may differ, may be 0). */
+ * every rank calls it for its own tokens (n_tok may differ, may be 0) with the same layer, in the
+ * same order. Each token's rotated row goes once to every rank that holds one of its experts,
+ * each such rank returns one weighted partial row, and the source adds them. The call blocks
+ * until the per-rank row counts are known (one short host round trip per layer); a peer that
+ * stops answering for the communication timeout gives GX_E_COMM, after which only gx_destroy
+ * is valid. With world > 1 every token count takes the tensor-core path, and n_embd must be a
+ * multiple of 256 (gx_upload_layer returns GX_E_UNSUPPORTED otherwise). */
 GX_API gx_result gx_moe_forward(gx_context *context, uint32_t layer, const void *x, uint32_t x_dtype,
                                 uint32_t n_tok, void *y, uint32_t y_dtype, uint32_t *ids, float *weights,
                                 uint64_t *out_ticket);
@@ -161,7 +176,8 @@ GX_API gx_result gx_moe_forward_host(gx_context *context, uint32_t layer, const 
  * for n_tok tokens: the benchmark stand-in for the norm and hyper-connection mixer between the
  * reference model's layers, which lie outside this ABI. Device pointers; the chain of kernels is
  * captured into a CUDA graph on the first call and replayed on later calls with the same
- * (first_layer, n_layers, n_tok, dtypes, flags). */
+ * (first_layer, n_layers, n_tok, dtypes, flags). With world > 1 it is a collective like
+ * gx_moe_forward, and the layers run without a graph. */
 GX_API gx_result gx_stack_forward(gx_context *context, uint32_t first_layer, uint32_t n_layers,
                                   const void *x, uint32_t x_dtype, uint32_t n_tok, void *y,
                                   uint32_t y_dtype, uint64_t *out_ticket);

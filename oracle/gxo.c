@@ -440,26 +440,78 @@ static void down_range(void *p, size_t a, size_t b) {
     free(wbuf);
 }
 
-/* src/engine.zig:520-642 */
-int gxo_moe_ffn(const gxo_layer *l, const float *x, size_t n, float *out,
-                uint32_t *ids, float *weights, int threads) {
-    if (!l || !x || !out || !ids || !weights || !g_codebook_ready) return -1;
+/* Expert phase of src/engine.zig:547-641 for a given routing (ids/weights [n][U]): rotation,
+ * grouping, gate/up, SwiGLU, down rotation, down, weighted sum. Slots whose id is not below
+ * n_expert are skipped; the expert-parallel model of the tests uses them for slots served by
+ * another rank. */
+static int experts_phase(const gxo_layer *l, const float *x, size_t n, const uint32_t *ids,
+                         const float *weights, float *out, int threads) {
     const size_t E = l->n_embd, F = l->n_ff, U = l->n_used, NE = l->n_expert;
     size_t gate_row = gxo_row_bytes(l->type_id, E), down_row = gxo_row_bytes(l->type_id, F);
-    if (l->type_id == 0 || !gate_row || !down_row || U == 0 || U > NE || NE > 512 || n == 0)
-        return -1;
-    float *router = malloc(sizeof(float) * n * NE);
     float *xh = malloc(sizeof(float) * n * E);
     float *act = malloc(sizeof(float) * n * U * F);
     float *act_up = malloc(sizeof(float) * n * U * F);
     float *down = malloc(sizeof(float) * n * U * E);
     uint32_t *order = malloc(sizeof(uint32_t) * n * U);
-    if (!router || !xh || !act || !act_up || !down || !order) {
-        free(router); free(xh); free(act); free(act_up); free(down); free(order);
+    if (!xh || !act || !act_up || !down || !order) {
+        free(xh); free(act); free(act_up); free(down); free(order);
         return -1;
     }
     uint32_t start[513];
-    ffn_ctx c = {l, x, xh, n, E, F, U, NE, gate_row, down_row, router, act, act_up, down, start, order};
+    ffn_ctx c = {l, x, xh, n, E, F, U, NE, gate_row, down_row, NULL, act, act_up, down, start, order};
+    /* Rotated expert input shared by gate and up, src/engine.zig:547-551. */
+    memcpy(xh, x, sizeof(float) * n * E);
+    if (l->gate_signs) for (size_t t = 0; t < n; ++t) gxo_rotate_f32(xh + t * E, E, 128, l->gate_signs);
+    /* Counting sort of slots by expert, src/engine.zig:553-564. */
+    memset(out, 0, sizeof(float) * n * E);
+    memset(start, 0, sizeof(start));
+    for (size_t i = 0; i < n * U; ++i) if (ids[i] < NE) start[ids[i] + 1] += 1;
+    for (size_t e = 0; e < NE; ++e) start[e + 1] += start[e];
+    uint32_t fill[513];
+    memcpy(fill, start, sizeof(fill));
+    for (size_t i = 0; i < n * U; ++i) if (ids[i] < NE) order[fill[ids[i]]++] = (uint32_t)i;
+    /* Phase 1: gate/up, chunk 16, src/engine.zig:568. */
+    pool_run(threads, NE * F, 16, gate_up_range, &c);
+    /* SwiGLU and down-input rotation, src/engine.zig:603-607. */
+    for (size_t slot = 0; slot < n * U; ++slot) {
+        if (ids[slot] >= NE) continue;
+        float *a = act + slot * F;
+        const float *up = act_up + slot * F;
+        for (size_t i = 0; i < F; ++i) a[i] = silu(a[i]) * up[i];
+        if (l->down_signs) gxo_rotate_f32(a, F, 128, l->down_signs);
+    }
+    /* Phase 2: down, chunk 64, src/engine.zig:609. */
+    pool_run(threads, NE * E, 64, down_range, &c);
+    /* Weighted sum, src/engine.zig:634-641. */
+    for (size_t t = 0; t < n; ++t) {
+        float *o = out + t * E;
+        for (size_t k = 0; k < U; ++k) {
+            size_t slot = t * U + k;
+            if (ids[slot] >= NE) continue;
+            float wgt = weights[slot];
+            const float *v = down + slot * E;
+            for (size_t i = 0; i < E; ++i) o[i] += wgt * v[i];
+        }
+    }
+    free(xh); free(act); free(act_up); free(down); free(order);
+    return 0;
+}
+
+static int layer_ok(const gxo_layer *l) {
+    if (!l || !g_codebook_ready || l->type_id == 0) return 0;
+    const size_t E = l->n_embd, F = l->n_ff, U = l->n_used, NE = l->n_expert;
+    return gxo_row_bytes(l->type_id, E) && gxo_row_bytes(l->type_id, F) && U && NE <= 512 && E && F;
+}
+
+/* src/engine.zig:520-642 */
+int gxo_moe_ffn(const gxo_layer *l, const float *x, size_t n, float *out,
+                uint32_t *ids, float *weights, int threads) {
+    if (!layer_ok(l) || !x || !out || !ids || !weights || !l->router || n == 0 || l->n_used > l->n_expert)
+        return -1;
+    const size_t E = l->n_embd, U = l->n_used, NE = l->n_expert;
+    float *router = malloc(sizeof(float) * n * NE);
+    if (!router) return -1;
+    ffn_ctx c = {l, x, NULL, n, E, l->n_ff, U, NE, 0, 0, router, NULL, NULL, NULL, NULL, NULL};
     /* Router, chunk as kernels.matmul picks it (pool.chunkFor(rows, 8)). */
     size_t router_chunk = threads > 1 ? NE / ((size_t)threads * 4) : NE;
     pool_run(threads, NE, router_chunk > 8 ? router_chunk : 8, router_range, &c);
@@ -480,38 +532,13 @@ int gxo_moe_ffn(const gxo_layer *l, const float *x, size_t n, float *out,
             if (l->expert_weights_scale != 0 && l->expert_weights_scale != 1) w[j] *= l->expert_weights_scale;
         }
     }
-    /* Rotated expert input shared by gate and up, src/engine.zig:547-551. */
-    memcpy(xh, x, sizeof(float) * n * E);
-    if (l->gate_signs) for (size_t t = 0; t < n; ++t) gxo_rotate_f32(xh + t * E, E, 128, l->gate_signs);
-    /* Counting sort of slots by expert, src/engine.zig:553-564. */
-    memset(out, 0, sizeof(float) * n * E);
-    memset(start, 0, sizeof(start));
-    for (size_t i = 0; i < n * U; ++i) start[ids[i] + 1] += 1;
-    for (size_t e = 0; e < NE; ++e) start[e + 1] += start[e];
-    uint32_t fill[513];
-    memcpy(fill, start, sizeof(fill));
-    for (size_t i = 0; i < n * U; ++i) order[fill[ids[i]]++] = (uint32_t)i;
-    /* Phase 1: gate/up, chunk 16, src/engine.zig:568. */
-    pool_run(threads, NE * F, 16, gate_up_range, &c);
-    /* SwiGLU and down-input rotation, src/engine.zig:603-607. */
-    for (size_t slot = 0; slot < n * U; ++slot) {
-        float *a = act + slot * F;
-        const float *up = act_up + slot * F;
-        for (size_t i = 0; i < F; ++i) a[i] = silu(a[i]) * up[i];
-        if (l->down_signs) gxo_rotate_f32(a, F, 128, l->down_signs);
-    }
-    /* Phase 2: down, chunk 64, src/engine.zig:609. */
-    pool_run(threads, NE * E, 64, down_range, &c);
-    /* Weighted sum, src/engine.zig:634-641. */
-    for (size_t t = 0; t < n; ++t) {
-        float *o = out + t * E;
-        for (size_t k = 0; k < U; ++k) {
-            size_t slot = t * U + k;
-            float wgt = weights[slot];
-            const float *v = down + slot * E;
-            for (size_t i = 0; i < E; ++i) o[i] += wgt * v[i];
-        }
-    }
-    free(router); free(xh); free(act); free(act_up); free(down); free(order);
-    return 0;
+    free(router);
+    return experts_phase(l, x, n, ids, weights, out, threads);
+}
+
+int gxo_moe_experts(const gxo_layer *l, const float *x, size_t n, const uint32_t *ids,
+                    const float *weights, float *out, int threads) {
+    if (!layer_ok(l) || !x || !out || !ids || !weights) return -1;
+    if (n == 0) return 0;
+    return experts_phase(l, x, n, ids, weights, out, threads);
 }

@@ -91,6 +91,12 @@ typedef struct gxo_layer {
 int gxo_moe_ffn(const gxo_layer *layer, const float *x, size_t n, float *out,
                 uint32_t *ids, float *weights, int threads);
 
+/* The expert half of gxo_moe_ffn for a given routing: ids/weights [n][n_used] (ids local to
+ * this layer's experts). Slots with ids[slot] >= n_expert contribute nothing (the slots another
+ * rank serves in the expert-parallel model). The router fields of the layer are not used. */
+int gxo_moe_experts(const gxo_layer *layer, const float *x, size_t n, const uint32_t *ids,
+                    const float *weights, float *out, int threads);
+
 /* Threads the library can use (1 when built without GXO_THREADS). */
 int gxo_max_threads(void);
 

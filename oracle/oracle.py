@@ -80,6 +80,8 @@ def lib(fast: bool = False) -> ctypes.CDLL:
     L.gxo_topk.restype = None
     L.gxo_moe_ffn.argtypes = [ctypes.POINTER(_Layer), _F32P, ctypes.c_size_t, _F32P, _U32P, _F32P,
                               ctypes.c_int]
+    L.gxo_moe_experts.argtypes = [ctypes.POINTER(_Layer), _F32P, ctypes.c_size_t, _U32P, _F32P, _F32P,
+                                  ctypes.c_int]
     L.gxo_max_threads.restype = ctypes.c_int
     L.gxo_rms_norm.argtypes = [_F32P, _F32P, ctypes.c_size_t, ctypes.c_float]
     L.gxo_rms_norm.restype = None
@@ -148,6 +150,37 @@ def moe_ffn(layer: dict, x: np.ndarray, threads: int = 1, fast: bool = False):
     if rc != 0:
         raise RuntimeError(f"gxo_moe_ffn failed ({rc})")
     return out, ids, w
+
+
+def moe_experts(layer: dict, x: np.ndarray, ids: np.ndarray, weights: np.ndarray, threads: int = 1,
+                fast: bool = False) -> np.ndarray:
+    """Expert half of src/engine.zig:547-641 for a given routing (ids local to the layer's experts;
+    ids >= n_expert contribute nothing). Returns out [n, E]."""
+    L = lib(fast)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    n, E = x.shape
+    ids = np.ascontiguousarray(ids, dtype=np.uint32)
+    weights = np.ascontiguousarray(weights, dtype=np.float32)
+    keep = []
+
+    def ptr(a, dtype):
+        if a is None:
+            return None
+        a = np.ascontiguousarray(a, dtype=dtype)
+        keep.append(a)
+        return a.ctypes.data
+
+    desc = _Layer(layer["type_id"], layer["n_expert"], E, layer["n_ff"], layer["n_used"],
+                  layer.get("expert_weights_scale", 0.0),
+                  ptr(layer["gate"], np.uint8), ptr(layer["up"], np.uint8), ptr(layer["down"], np.uint8),
+                  ptr(layer.get("router"), np.float32), ptr(layer.get("gate_signs"), np.float32),
+                  ptr(layer.get("down_signs"), np.float32), None)
+    out = np.zeros((n, E), dtype=np.float32)
+    rc = L.gxo_moe_experts(ctypes.byref(desc), _f32p(x), n, ids.ctypes.data_as(_U32P), _f32p(weights), _f32p(out),
+                           threads)
+    if rc != 0:
+        raise RuntimeError(f"gxo_moe_experts failed ({rc})")
+    return out
 
 
 STACK_NORM_EPS = 1e-6

@@ -1,0 +1,90 @@
+"""One rank of the 2-GPU expert-parallel parity test (tests/test_gpu_ep.py).
+
+Every rank makes the same C-ABI calls, in the same order, for every case. All collective work
+is done before any comparison, so that a failed check on one rank cannot leave the other
+waiting in an exchange. Results go to <out>/rank<r>.npz for the parent to check against the
+oracle.
+"""
+from __future__ import annotations
+
+import os
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parents[1]
+for p in (ROOT, ROOT / "gyro-dx_b200", ROOT / "tests"):
+    if str(p) not in sys.path:
+        sys.path.insert(0, str(p))
+
+CASES = [
+    # name, layer kwargs, tokens per rank
+    ("small", dict(seed=31, n_expert=16, E=256, F=128, U=4), [37, 21]),
+    ("zipf_empty_rank", dict(seed=32, n_expert=32, E=256, F=256, U=4, zipf=1.1), [70, 0]),
+    ("config0_shape", dict(seed=33, zipf=1.1), [300, 180]),
+]
+
+
+def make(kw):
+    from gyro_moe import synth
+    kw = dict(kw)
+    seed = kw.pop("seed")
+    return synth.make_layer(seed, **kw)
+
+
+def tokens(case_i, rank, n, E):
+    from gyro_moe import synth
+    return synth.tokens(9000 + 10 * case_i + rank, max(n, 1), E=E)[:n]
+
+
+def worker(rank: int, world: int, out_dir: str) -> None:
+    os.environ.setdefault("GX_COMM_TIMEOUT_MS", "30000")
+    import torch
+    torch.cuda.set_device(rank)
+    from gyro_moe import abi
+    idf = Path(out_dir) / "nccl_id"
+    if rank == 0:
+        tmp = idf.with_suffix(".tmp")
+        tmp.write_bytes(abi.unique_id())
+        tmp.rename(idf)
+    t0 = time.time()
+    while not idf.exists():
+        if time.time() - t0 > 60:
+            raise RuntimeError("no NCCL id from rank 0")
+        time.sleep(0.05)
+    nccl_id = idf.read_bytes()
+    res = {}
+    max_tok = max(max(n) for _, _, n in CASES)
+    with abi.Context(device=rank, max_tokens=max_tok, max_layers=2, rank=rank, world=world, nccl_id=nccl_id) as ctx:
+        caps = ctx.caps()
+        res["caps_world"] = np.array([caps.rank, caps.world])
+        for i, (name, kw, n_tok) in enumerate(CASES):
+            layer = make(kw)
+            ctx.upload_layer(0, layer)
+            x = tokens(i, rank, n_tok[rank], layer["n_embd"])
+            y, ids, w = ctx.forward_host(0, x, want_routing=True)
+            res[f"{name}_x"], res[f"{name}_y"], res[f"{name}_ids"] = x, y, ids
+        # a two-layer pre-norm stack, bf16 tokens in
+        layers = [make(dict(seed=41 + l, n_expert=16, E=256, F=128, U=4)) for l in range(2)]
+        for l, layer in enumerate(layers):
+            ctx.upload_layer(l, layer)
+        xs = tokens(7, rank, [50, 30][rank], 256)
+        xb = (xs.view(np.uint32) >> 16).astype(np.uint16)
+        res["stack_x"] = xb
+        res["stack_y"] = ctx.stack_forward_host(0, 2, xb)
+        # device pointers, one rank without tokens, twice in a row (buffers reused)
+        dev = torch.device("cuda", rank)
+        for rep in range(2):
+            n = [12, 0][rank]
+            xt = torch.from_numpy(tokens(8 + rep, rank, n, 256)).to(dev)
+            yt = torch.empty_like(xt)
+            ctx.wait(ctx.forward(1, xt, yt))
+            res[f"dev{rep}_x"], res[f"dev{rep}_y"] = xt.cpu().numpy(), yt.cpu().numpy()
+        try:
+            ctx.forward_noalloc(1, xt, yt)
+            res["noalloc_rc"] = np.array(0)
+        except abi.GxError as e:
+            res["noalloc_rc"] = np.array(e.code)
+    np.savez(Path(out_dir) / f"rank{rank}.npz", **res)
