@@ -19,6 +19,14 @@ over its event-timed duration in the final timed step; cpu_baseline = the CPU or
 reference engine) on the host cores, on a bounded sample. With N > 1 GPUs each rank runs an
 independent replica on its own tokens ("replicas": decode does not exchange data).
 
+Workload "prefill": one 1,024-token bf16 sequence through the config-0
+layer with Zipf(1.1) routing; roofline = the tcgen05 gate/up grouped GEMM in useful TFLOP/s.
+
+Workload "ep-prefill": 32 packed sequences (log-uniform lengths in
+[1, 512]) through the 40-layer stack with Zipf(1.1) routing. With N ranks the experts are
+sharded 256/N per GPU and tokens travel by NCCL dispatch / combine inside the library; the batch
+is fixed, so scaling is strong.
+
 --impl reference times the reference's CPU engine (restated in oracle/, the reference's Zig code
 cannot be built here) on the same workload with all host threads; rank 0 only.
 """
@@ -56,7 +64,7 @@ def parse():
     p.add_argument("--steps", type=int, default=128)
     p.add_argument("--warmup", type=int, default=8)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--workload", choices=["decode", "prefill"], default="decode")
+    p.add_argument("--workload", choices=["decode", "prefill", "ep-prefill"], default="decode")
     p.add_argument("--tokens", type=int, default=1024, help="prefill: tokens per step")
     p.add_argument("--layers", type=int, default=N_LAYERS)
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -155,35 +163,66 @@ def cpu_baseline(layers, seconds: float) -> dict:
 
 def run_reference(args):
     """Reference arm: the CPU engine restated in oracle/ (the reference's own CPU engine is Zig,
-    which is absent), all host threads, each step one token through the 40-layer stack."""
+    which is absent), all host threads, rank 0 only. Each step is a bounded sample of the
+    workload: decode, one token through the 40-layer stack; prefill, 64 of the 1,024 tokens
+    through the layer; ep-prefill, 64 tokens of the packed batch through the 40-layer stack."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     from oracle import oracle
     from gyro_moe import synth
-    layers = list(make_layers(args.layers))
     threads = oracle.max_threads()
-    xs = step_tokens(args.warmup + args.steps, 1, 0)
-    times = []
-    for i in range(args.warmup + args.steps):
-        x = (xs[i].astype(np.uint32) << 16).view(np.float32)
+    steps = args.warmup + args.steps
+    if args.workload == "decode":
+        layers = list(make_layers(args.layers))
+        xs = [(t.astype(np.uint32) << 16).view(np.float32) for t in step_tokens(steps, 1, 0)]
+        run = lambda x: oracle.stack(layers, x, threads=threads, fast=True)
+        per_step, scaling = 1, "weak"
+        config = {"workload": "decode: 40-layer stack of the config-0 routed layer (BASELINE.json configs[1]), "
+                              "batch 1, fresh token per step",
+                  "layers": args.layers, "n_tok": 1}
+        sample = f"{args.steps} steps x 1 token x {args.layers} layers"
+    elif args.workload == "prefill":
+        layer = synth.make_layer(LAYER_SEED, zipf=1.1)
+        xb = step_tokens(1, args.tokens, 0)[0]
+        xf = (xb.astype(np.uint32) << 16).view(np.float32)
+        xs = [xf[(64 * i) % args.tokens:(64 * i) % args.tokens + 64] for i in range(steps)]
+        run = lambda x: oracle.moe_ffn(layer, x, threads=threads, fast=True)
+        per_step, scaling = 64, "weak"
+        config = {"workload": f"prefill: one {args.tokens}-token sequence through the config-0 routed layer, "
+                              "Zipf(1.1) routing", "tokens": args.tokens}
+        sample = f"{args.steps} steps x 64 of the {args.tokens} tokens through the layer"
+    else:
+        layers = [synth.make_layer(LAYER_SEED + l, zipf=1.1) for l in range(args.layers)]
+        lengths, offsets, xall = ep_batch()
+        T = int(offsets[-1])
+        xf = (xall.astype(np.uint32) << 16).view(np.float32)
+        xs = [xf[(64 * i) % T:(64 * i) % T + 64] for i in range(steps)]
+        run = lambda x: oracle.stack(layers, x, threads=threads, fast=True)
+        per_step, scaling = 64, "strong"
+        config = {"workload": f"expert-parallel prefill: {EP_SEQS} packed sequences (log-uniform lengths in "
+                              f"[1, 512], {T} tokens) through the {args.layers}-layer stack of the config-0 layer, "
+                              "Zipf(1.1)", "tokens": T, "layers": args.layers}
+        sample = f"{args.steps} steps x up to 64 tokens of the packed batch through {args.layers} layers"
+    times, done = [], 0
+    for i in range(steps):
         t0 = time.perf_counter()
-        oracle.stack(layers, x, threads=threads, fast=True)
+        run(xs[i])
         if i >= args.warmup:
             times.append(time.perf_counter() - t0)
+            done += xs[i].shape[0]
     total = sum(times)
-    value = args.steps / total
+    value = done / total
+    config.update({"hidden": E, "experts": NE, "top_k": U, "ffn": F, "type": "TQ2_T", "parallelism": "host threads"})
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded; shapes of BASELINE.json config 1)",
-        "config": {"workload": "decode: 40-layer stack of the config-0 routed layer, batch 1",
-                   "layers": args.layers, "n_tok": 1, "hidden": E, "experts": NE, "top_k": U, "ffn": F,
-                   "type": "TQ2_T", "parallelism": "host threads"},
+        "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded; shapes and distributions of the BASELINE.json config)",
+        "config": config,
         "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
-                         "sample": f"{args.steps} steps x 1 token x {args.layers} layers (oracle/ restatement of "
-                                   "src/engine.zig:520-642; the reference's Zig engine cannot be built here)"},
+                         "sample": sample + " (oracle/ restatement of src/engine.zig:520-642; the reference's "
+                                            "Zig engine cannot be built here)"},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -412,14 +451,183 @@ def run_prefill(args):
     }
     if not args.no_cpu_baseline:
         threads = oracle.max_threads()
-        xs32 = (xs_host[0][:64].astype(np.uint32) << 16).view(np.float32)
+        xs32 = (xs_host[0].astype(np.uint32) << 16).view(np.float32)
+        done, el = 0, 0.0
         t0 = time.perf_counter()
-        oracle.moe_ffn(layer, xs32, threads=threads, fast=True)
-        el = time.perf_counter() - t0
-        line["cpu_baseline"] = {"value": 64 / el, "unit": "tok/s", "cores": threads, "kind": "port",
-                                "sample": f"64 of the {T} tokens through the layer, {el:.1f} s on {threads} threads"}
+        while el < args.cpu_seconds and done < T:       # 64-token chunks of the sequence, bounded time
+            oracle.moe_ffn(layer, xs32[done:done + 64], threads=threads, fast=True)
+            done += 64
+            el = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": done / el, "unit": "tok/s", "cores": threads, "kind": "port",
+                                "sample": f"{done} of the {T} tokens through the layer in 64-token chunks, "
+                                          f"{el:.1f} s on {threads} threads"}
     print(json.dumps(line), flush=True)
     ctx.close()
+
+
+EP_SEQS, EP_SEED = 32, 4
+
+
+def ep_batch():
+    """32 sequences with log-uniform lengths in [1, 512] packed into one
+    ragged buffer (offsets), bf16 tokens ~N(0, 1)."""
+    from gyro_moe import synth
+    lengths = synth.loguniform_lengths(EP_SEED, EP_SEQS)
+    offsets = np.concatenate([[0], np.cumsum(lengths)])
+    x = synth.bf16_bits(np.random.default_rng(EP_SEED + 1).standard_normal((int(offsets[-1]), E)).astype(np.float32))
+    return lengths, offsets, x
+
+
+def rank_tokens(offsets, x, rank: int, world: int) -> np.ndarray:
+    """A rank's slice of the ragged batch: sequences rank, rank + world, ..."""
+    seqs = range(rank, len(offsets) - 1, world)
+    parts = [x[offsets[i]:offsets[i + 1]] for i in seqs]
+    return np.concatenate(parts) if parts else np.zeros((0, E), np.uint16)
+
+
+def run_ep(args):
+    """the packed batch through the 40-layer stack (Zipf(1.1) routing per
+    layer). With N ranks each rank holds 256/N experts of every layer and routes its own
+    sequences; dispatch and combine are NCCL exchanges inside the library. The total batch is
+    fixed, so scaling is strong: value = all tokens / max-over-ranks time per step."""
+    import datetime
+    import torch
+    from gyro_moe import abi, synth
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    nccl_id = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        idt = torch.zeros(128, dtype=torch.uint8, device=dev)
+        if rank == 0:
+            idt.copy_(torch.frombuffer(bytearray(abi.unique_id()), dtype=torch.uint8))
+        dist.broadcast(idt, 0)
+        nccl_id = bytes(idt.cpu().numpy())
+    lengths, offsets, xall = ep_batch()
+    T = int(offsets[-1])
+    mine = rank_tokens(offsets, xall, rank, world)
+    n_tok = mine.shape[0]
+    max_tok = max(rank_tokens(offsets, xall, r, world).shape[0] for r in range(world))
+    K, W = args.steps, args.warmup
+    ctx = abi.Context(device=local, max_tokens=max(max_tok, 1), max_layers=args.layers, rank=rank, world=world,
+                      nccl_id=nccl_id)
+    keep_host = rank == 0 and world == 1 and not args.no_cpu_baseline
+    host_layers = []
+    for l in range(args.layers):
+        layer = synth.make_layer(LAYER_SEED + l, zipf=1.1)
+        ctx.upload_layer(l, layer)
+        if keep_host:
+            host_layers.append(layer)
+    # two input batches alternate: the same tokens scaled by 1 and by -1 route differently
+    x0 = torch.from_numpy(mine.view(np.int16)).to(dev).view(torch.bfloat16)
+    xs = [x0, -x0]
+    y = torch.empty((n_tok, E), dtype=torch.bfloat16, device=dev)
+    for i in range(W):
+        ticket = ctx.stack_forward(0, args.layers, xs[i % 2], y)
+    ctx.wait(ticket)
+    torch.cuda.synchronize(dev)
+    stream = torch.cuda.ExternalStream(ctx.stream(), device=dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as clocks:
+        with torch.cuda.stream(stream):
+            start.record(stream)
+        for i in range(K):
+            ticket = ctx.stack_forward(0, args.layers, xs[i % 2], y)
+        with torch.cuda.stream(stream):
+            end.record(stream)
+        end.synchronize()
+    ctx.wait(ticket)
+    ms_t = torch.tensor([start.elapsed_time(end)], dtype=torch.float64, device=dev)
+    if dist:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms = float(ms_t.item())
+    # phase times of one profiled layer-0 call and this rank's received slots, for the roofline
+    ids = torch.empty((n_tok, U), dtype=torch.int32, device=dev)
+    ctx.set_flags(abi.GX_FLAG_PROFILE)
+    ctx.wait(ctx.forward(0, xs[0], y, ids))
+    ph = ctx.timings()
+    ctx.set_flags(0)
+    per = NE // world
+    own = np.bincount(ids.cpu().numpy().reshape(-1).astype(np.int64) // per, minlength=world).astype(np.float64)
+    sent = torch.from_numpy(own).to(dev)
+    if dist:
+        dist.all_reduce(sent)                     # slots every rank serves, summed over sources
+    slots_here = float(sent[rank].item())
+    gu_flops = slots_here * 2 * F * E * 2
+    agg = torch.tensor([gu_flops, ph.gate_up_ns * 1e-9, ph.router_ns * 1e-9, ph.down_ns * 1e-9, ph.total_ns * 1e-9],
+                       dtype=torch.float64, device=dev)
+    if dist:
+        dist.all_reduce(agg)
+    flops_sum, gu_sum, rt_sum, dn_sum, tot_sum = (float(v) for v in agg.cpu())
+    pk = peaks()
+    achieved = flops_sum / gu_sum / 1e12 if gu_sum > 0 else None
+    # end to end: host bf16 in, host bf16 out
+    e2e_steps = min(K, 8)
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        src = mine if i % 2 == 0 else (mine ^ np.uint16(0x8000))
+        ctx.stack_forward_host(0, args.layers, src, out_dtype=np.uint16)
+    e2e_t = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device=dev)
+    if dist:
+        dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
+    e2e_s = float(e2e_t.item())
+    launches_per_layer = 11 if world > 1 else 9
+    line = {
+        "metric": METRIC, "value": K * T / (ms / 1e3), "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (seeded; shapes and distributions of BASELINE.json config 4)",
+        "config": {"workload": f"expert-parallel prefill: {EP_SEQS} packed sequences (log-uniform lengths in [1, 512], "
+                               f"{T} tokens) through the {args.layers}-layer stack of the config-0 layer, Zipf(1.1)",
+                   "tokens": T, "sequences": EP_SEQS, "layers": args.layers, "hidden": E, "experts": NE,
+                   "experts_per_gpu": per, "top_k": U, "ffn": F, "type": "TQ2_T",
+                   "parallelism": f"expert parallel x{world} (NCCL dispatch/combine)" if world > 1 else "single GPU",
+                   "tokens_per_rank_max": max_tok,
+                   "l2": "inputs larger than L2: a step reads every touched expert of 40 layers"},
+        "roofline": {
+            "kernel": "moe_gemm_kernel<gate/up> on each rank's received slots (tcgen05 grouped GEMM)",
+            "bound": "tensor", "achieved": achieved, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+            "frac": achieved / pk["bf16_tflops"] if achieved else None, "traffic": None,
+            "how": "sum over ranks of (received slots x 2 x F x E x 2) / sum over ranks of the gate/up GEMM "
+                   "event time, one profiled layer-0 call",
+            "phase_ms_mean_per_rank": {"select_dispatch": rt_sum / world * 1e3, "gate_up": gu_sum / world * 1e3,
+                                       "down_combine": dn_sum / world * 1e3, "layer": tot_sum / world * 1e3},
+            "peak_source": f"{pk['source']} (MEASURED_PEAKS.json bf16_tflops, burst)",
+        },
+        "e2e": {"value": e2e_steps * T / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": n_tok * E * 2,
+                "d2h_bytes_per_step": n_tok * E * 2, "steps": e2e_steps,
+                "api": "gx_stack_forward_host (host bf16 in, host bf16 out), per rank"},
+        "gpu_launches": K * args.layers * launches_per_layer,
+        "clocks": clocks.summary(),
+    }
+    if keep_host:
+        from oracle import oracle
+        threads = oracle.max_threads()
+        xf = (mine.astype(np.uint32) << 16).view(np.float32)
+        done, el, t0 = 0, 0.0, time.perf_counter()
+        while el < args.cpu_seconds and done < T:
+            oracle.stack(host_layers, xf[done:done + 64], threads=threads, fast=True)
+            done += min(64, T - done)
+            el = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": done / el, "unit": "tok/s", "cores": threads, "kind": "port",
+                                "sample": f"{done} of the {T} tokens in 64-token chunks through the "
+                                          f"{args.layers}-layer stack, {el:.1f} s on {threads} threads"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def main():
@@ -428,6 +636,8 @@ def main():
         run_reference(args)
     elif args.workload == "prefill":
         run_prefill(args)
+    elif args.workload == "ep-prefill":
+        run_ep(args)
     else:
         run_ours(args)
 
