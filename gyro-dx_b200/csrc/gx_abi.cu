@@ -78,6 +78,9 @@ struct gx_context {
     uint64_t submitted = 0;
     std::vector<cudaEvent_t> prof;   // 4 per layer slot: start, router done, gate/up done, down done
     uint32_t prof_layers = 0;        // layers recorded by the most recent forward call
+    uint32_t prof_stack = 0;         // > 0: the last call was one stack kernel over this many layers
+    gx::StackLayer *stack_table = nullptr;  // device table of uploaded layers (decode-stack kernel)
+    unsigned *stack_sync = nullptr;  // grid-barrier counter of the decode-stack kernel
     std::map<GraphKey, std::pair<cudaGraph_t, cudaGraphExec_t>> graphs;
     bool broken = false;
     // expert-parallel group (world > 1)
@@ -193,6 +196,9 @@ gx_result ensure_scratch(gx_context *c) {
     GX_CUDA(cudaMallocHost(&c->h_out, c->stage_bytes + T * U * 8));
     GX_CUDA(cudaMalloc(&c->err, sizeof(int)));
     GX_CUDA(cudaMemset(c->err, 0, sizeof(int)));
+    GX_CUDA(cudaMalloc(&c->stack_table, c->max_layers * sizeof(gx::StackLayer)));
+    GX_CUDA(cudaMemset(c->stack_table, 0, c->max_layers * sizeof(gx::StackLayer)));
+    GX_CUDA(cudaMalloc(&c->stack_sync, 64));
     return GX_OK;
 }
 
@@ -207,7 +213,7 @@ void release_all(gx_context *c) {
     for (void *p : pf) if (p) cudaFree(p);
     for (auto &m : c->mats) if (m.tiles) cudaFree(m.tiles);
     void *dev[] = {c->codebook, c->logits, c->weights, c->xscale, c->ss, c->ids, c->act, c->xbuf[0], c->xbuf[1],
-                   c->x_stage, c->y_stage, c->err};
+                   c->x_stage, c->y_stage, c->err, c->stack_table, c->stack_sync};
     for (void *p : dev) if (p) cudaFree(p);
     if (c->h_in) cudaFreeHost(c->h_in);
     if (c->h_out) cudaFreeHost(c->h_out);
@@ -779,7 +785,10 @@ gx_result stack_enqueue(gx_context *c, uint32_t first, uint32_t n_layers, const 
                         uint32_t n_tok, void *y, uint32_t y_dtype) {
     const void *cur = x;
     uint32_t cur_dtype = x_dtype;
-    if (c->flags & GX_FLAG_PROFILE) c->prof_layers = n_layers;
+    if (c->flags & GX_FLAG_PROFILE) {
+        c->prof_layers = n_layers;
+        c->prof_stack = 0;
+    }
     for (uint32_t i = 0; i < n_layers; ++i) {
         const Layer &L = c->layers[first + i];
         const bool last = i + 1 == n_layers;
@@ -792,6 +801,59 @@ gx_result stack_enqueue(gx_context *c, uint32_t first, uint32_t n_layers, const 
         cur = out;
         cur_dtype = out_dtype;
     }
+    return GX_OK;
+}
+
+// Whether a stack call runs as one persistent decode-stack kernel instead of the PDL-chained
+// per-phase kernels: opt-in with GX_STACK_KERNEL=1 (at batch 1 on B200 the chained kernels are
+// faster: its phases are short serial sections separated by grid barriers), one GPU, few tokens,
+// and every layer of the same type and shape within the kernel's limits.
+bool stack_kernel_fits(gx_context *c, uint32_t first, uint32_t n_layers, uint32_t n_tok) {
+    const char *opt = std::getenv("GX_STACK_KERNEL");
+    if (!opt || opt[0] != '1') return false;
+    if (c->world != 1 || n_tok == 0 || n_tok >= kPrefillMinTokens) return false;
+    const Layer &L0 = c->layers[first];
+    for (uint32_t i = 0; i < n_layers; ++i) {
+        const Layer &L = c->layers[first + i];
+        if (L.type != L0.type || L.E != L0.E || L.F != L0.F || L.U != L0.U || L.n_expert != L0.n_expert) return false;
+    }
+    return L0.n_expert <= 4u * (uint32_t)c->sm_count &&
+           gx::decode_stack_supported(L0.type, (int)L0.E, (int)L0.F, (int)L0.U, (int)L0.n_expert, (int)n_tok);
+}
+
+// The whole stack (pre-norm residual chain) as one cooperative kernel launch.
+gx_result enqueue_stack_kernel(gx_context *c, uint32_t first, uint32_t n_layers, const void *x, uint32_t x_dtype,
+                               uint32_t n_tok, void *y, uint32_t y_dtype) {
+    const Layer &L0 = c->layers[first];
+    const bool prof = (c->flags & GX_FLAG_PROFILE) != 0;
+    if (prof) {
+        c->prof_layers = 0;
+        c->prof_stack = n_layers;
+        GX_CUDA(record_phase(c->prof[0], c->stream));
+    }
+    gx::StackArgs a{};
+    a.layers = c->stack_table + first;
+    a.n_layers = (int)n_layers;
+    a.x = x;
+    a.x_bf16 = x_dtype == GX_BF16;
+    a.out = y;
+    a.out_bf16 = y_dtype == GX_BF16;
+    a.xa = c->xbuf[0];
+    a.xb = c->xbuf[1];
+    a.logits = c->logits;
+    a.act = c->act;
+    a.codebook = c->codebook;
+    a.sync = c->stack_sync;
+    a.n_tok = (int)n_tok;
+    a.NE = (int)L0.n_expert;
+    a.E = (int)L0.E;
+    a.F = (int)L0.F;
+    a.U = (int)L0.U;
+    a.norm_eps = kStackNormEps;
+    a.residual = 1;
+    a.err = c->err;
+    GX_CUDA(gx::launch_decode_stack(a, L0.type, c->sm_count, c->stream));
+    if (prof) GX_CUDA(record_phase(c->prof[3], c->stream));
     return GX_OK;
 }
 
@@ -1003,6 +1065,20 @@ GX_API gx_result gx_upload_layer(gx_context *c, uint32_t layer, const gx_layer_d
     L.bias = reinterpret_cast<float *>(arena + o_bias);
     L.gate_signs = d->gate_signs ? reinterpret_cast<float *>(arena + o_gs) : nullptr;
     L.down_signs = d->down_signs ? reinterpret_cast<float *>(arena + o_ds) : nullptr;
+    {
+        gx::StackLayer sl{};
+        sl.router = L.router;
+        sl.bias = L.bias;
+        sl.gate_signs = L.gate_signs;
+        sl.down_signs = L.down_signs;
+        sl.gate = L.gate;
+        sl.up = L.up;
+        sl.down = L.down;
+        sl.gate_expert_bytes = L.gate_expert_bytes;
+        sl.down_expert_bytes = L.down_expert_bytes;
+        sl.scale = L.scale;
+        GX_CUDA(cudaMemcpy(c->stack_table + layer, &sl, sizeof(sl), cudaMemcpyHostToDevice));
+    }
     // A re-uploaded layer invalidates captured stacks.
     for (auto &kv : c->graphs) {
         cudaGraphExecDestroy(kv.second.second);
@@ -1024,7 +1100,10 @@ GX_API gx_result gx_moe_forward(gx_context *c, uint32_t layer, const void *x, ui
     const Layer &L = c->layers[layer];
     if (n_tok > 0 || c->world > 1) {  // with world > 1 every rank takes part in the exchange
         const bool prof = (c->flags & GX_FLAG_PROFILE) != 0;
-        if (prof) c->prof_layers = 1;
+        if (prof) {
+            c->prof_layers = 1;
+            c->prof_stack = 0;
+        }
         r = enqueue_layer(c, L, x, x_dtype, n_tok, nullptr, GX_F32, y, y_dtype, prof ? 0 : -1, 0.f, false);
         if (r != GX_OK) return r;
     }
@@ -1050,7 +1129,10 @@ GX_API gx_result gx_moe_forward_host(gx_context *c, uint32_t layer, const void *
         GX_CUDA(cudaMemcpyAsync(c->x_stage, c->h_in, in_b, cudaMemcpyHostToDevice, c->stream));
     }
     const bool prof = (c->flags & GX_FLAG_PROFILE) != 0;
-    if (prof) c->prof_layers = 1;
+    if (prof) {
+        c->prof_layers = 1;
+        c->prof_stack = 0;
+    }
     r = enqueue_layer(c, L, c->x_stage, x_dtype, n_tok, nullptr, GX_F32, c->y_stage, y_dtype, prof ? 0 : -1, 0.f,
                       false);
     if (r != GX_OK) return r;
@@ -1080,6 +1162,18 @@ GX_API gx_result gx_stack_forward(gx_context *c, uint32_t first, uint32_t n_laye
     GX_CUDA(cudaSetDevice(c->device));
     const size_t E = c->layers[first].E;
     const size_t in_b = n_tok * E * dtype_size(x_dtype), out_b = n_tok * E * dtype_size(y_dtype);
+    if (stack_kernel_fits(c, first, n_layers, n_tok)) {
+        // One launch for the whole stack; the input is staged if it aliases the output or the
+        // kernel's layer buffers, or is not 16-byte aligned (the kernel reads it with vector loads).
+        const void *src = x;
+        if (x == y || x == c->xbuf[0] || x == c->xbuf[1] || ((uintptr_t)x & 15)) {
+            GX_CUDA(cudaMemcpyAsync(c->x_stage, x, in_b, cudaMemcpyDeviceToDevice, c->stream));
+            src = c->x_stage;
+        }
+        gx_result r = enqueue_stack_kernel(c, first, n_layers, src, x_dtype, n_tok, y, y_dtype);
+        if (r != GX_OK) return r;
+        return record_ticket(c, out_ticket);
+    }
     if (c->world > 1) {
         // The exchange sizes are read back per layer, so the chain runs eagerly (no graph).
         if (in_b) GX_CUDA(cudaMemcpyAsync(c->x_stage, x, in_b, cudaMemcpyDeviceToDevice, c->stream));
@@ -1274,7 +1368,16 @@ GX_API gx_result gx_matvec(gx_context *c, uint32_t handle, const float *x, uint3
 GX_API gx_result gx_read_timings(gx_context *c, gx_timings *t) {
     if (!c || !t) return GX_E_INVALIDARG;
     std::memset(t, 0, sizeof(*t));
-    if (!(c->flags & GX_FLAG_PROFILE) || c->prof_layers == 0) return GX_OK;
+    if (!(c->flags & GX_FLAG_PROFILE)) return GX_OK;
+    if (c->prof_stack > 0) {  // one stack kernel: only its total is known
+        float ms = 0.f;
+        GX_CUDA(cudaEventSynchronize(c->prof[3]));
+        GX_CUDA(cudaEventElapsedTime(&ms, c->prof[0], c->prof[3]));
+        t->total_ns = (uint64_t)(ms * 1e6);
+        t->layers = c->prof_stack;
+        return GX_OK;
+    }
+    if (c->prof_layers == 0) return GX_OK;
     GX_CUDA(cudaEventSynchronize(c->prof[4 * (size_t)(c->prof_layers - 1) + 3]));
     for (uint32_t l = 0; l < c->prof_layers; ++l) {
         const cudaEvent_t *ev = &c->prof[4 * (size_t)l];
@@ -1294,6 +1397,7 @@ GX_API gx_result gx_set_flags(gx_context *c, uint32_t flags) {
     if (!c || (flags & ~(uint32_t)GX_FLAG_PROFILE)) return GX_E_INVALIDARG;
     c->flags = flags;
     c->prof_layers = 0;
+    c->prof_stack = 0;
     return GX_OK;
 }
 

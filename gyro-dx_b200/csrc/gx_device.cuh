@@ -25,14 +25,12 @@ __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
-// ---- shared-memory codebook with NCOPY bank-interleaved copies --------------------------
-// Copy c occupies W = 32/NCOPY banks; word i of copy c sits at
-//   ((i >> log2 W) << 5) | (c << log2 W) | (i & (W-1)).
-// A lane reads copy (lane % NCOPY), so only lanes sharing a copy can conflict.
+// ---- shared-memory codebook with NCOPY interleaved copies ---------------------------------
+// Word i of copy c sits at i * NCOPY + c, and a lane reads copy (lane % NCOPY): two lanes of a
+// warp can only meet in a bank when they share a copy (at most 32 / NCOPY lanes), and the
+// address of a lookup is one multiply-add of the index.
 template <int NCOPY>
 struct Codebook {
-    static constexpr int W = 32 / NCOPY;
-    static constexpr int LW = W == 32 ? 5 : W == 16 ? 4 : W == 8 ? 3 : W == 4 ? 2 : W == 2 ? 1 : 0;
     static constexpr int WORDS = 2048 * NCOPY;
     static constexpr int BYTES = WORDS * 4;
 
@@ -41,16 +39,11 @@ struct Codebook {
     // independent, so they overlap.
     __device__ static void stage(uint32_t *smem, const uint32_t *__restrict__ global_table, int tid, int nthreads) {
 #pragma unroll 16
-        for (int w = tid; w < WORDS; w += nthreads) {
-            const int idx = ((w >> 5) << LW) | (w & (W - 1));
-            smem[w] = __ldg(global_table + idx);
-        }
+        for (int w = tid; w < WORDS; w += nthreads) smem[w] = __ldg(global_table + w / NCOPY);
     }
-    // Word index of codebook entry idx in this lane's copy (copy_off = (lane%NCOPY) << LW).
-    __device__ static __forceinline__ uint32_t word(uint32_t idx, uint32_t copy_off) {
-        return ((idx >> LW) << 5) | copy_off | (idx & (W - 1));
-    }
-    __device__ static __forceinline__ uint32_t copy_off(int lane) { return (uint32_t)(lane % NCOPY) << LW; }
+    // Word index of codebook entry idx in this lane's copy (copy_off = lane % NCOPY).
+    __device__ static __forceinline__ uint32_t word(uint32_t idx, uint32_t copy_off) { return idx * NCOPY + copy_off; }
+    __device__ static __forceinline__ uint32_t copy_off(int lane) { return (uint32_t)(lane % NCOPY); }
 };
 
 // ---- tensor-core dot product: mma.sync m16n8k16, f16 x f16 -> f32 -------------------------
@@ -145,10 +138,11 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // Optional phase trace (build with -DGX_TRACE): thread 0 of each CTA stores clock64 deltas from
-// the CTA's start at numbered points into gx_trace[kernel][cta][point]. Off in normal builds.
-#ifdef GX_TRACE
+// the CTA's start at numbered points into gx_trace[kernel][cta][point]. Off in normal builds; the
+// array lives in the translation unit that defines GX_TRACE_OWNER (gx_kernels.cu).
+#if defined(GX_TRACE) && defined(GX_TRACE_OWNER)
 constexpr int kTraceKernels = 4, kTraceCtas = 160, kTracePoints = 8;
-__device__ long long gx_trace[kTraceKernels][kTraceCtas][kTracePoints];  // this header has one includer
+__device__ long long gx_trace[kTraceKernels][kTraceCtas][kTracePoints];
 #define GX_TRACE_START(k) const long long gx_t0_ = clock64(); const int gx_tk_ = (k)
 #define GX_TRACE_POINT(p)                                                                  \
     do {                                                                                   \

@@ -131,6 +131,38 @@ cudaError_t launch_router_gemm(const float *W, const void *x, int x_bf16, int n_
 cudaError_t launch_rotate_tokens(const void *x, int x_bf16, const float *xscale, const float *signs, int n_tok,
                                 int E, __half *xh, cudaStream_t s, const int *scatter = nullptr, int n_dst = 0);
 
+// ---- decode stack as one persistent cooperative kernel (gx_decode_stack.cu) ----------------
+struct StackLayer {
+    const float *router;     // [NE][E]
+    const float *bias;       // [NE]
+    const float *gate_signs; // [E] or nullptr
+    const float *down_signs; // [F] or nullptr
+    const uint8_t *gate, *up, *down;
+    uint64_t gate_expert_bytes, down_expert_bytes;
+    float scale;             // expert_weights_scale
+};
+
+struct StackArgs {
+    const StackLayer *layers;  // device table, n_layers entries
+    int n_layers;
+    const void *x;           // [n_tok][E] input
+    int x_bf16;
+    void *out;               // [n_tok][E] output of the last layer
+    int out_bf16;
+    float *xa, *xb;          // [n_tok][E] f32 inputs of the inner layers
+    float *logits;           // [n_tok][NE]
+    float *act;              // [n_tok * U][F]
+    const uint32_t *codebook;
+    unsigned *sync;          // grid-barrier counter, zeroed by the launcher
+    int n_tok, NE, E, F, U;
+    float norm_eps;          // > 0: experts and router see RMSNorm(x)
+    int residual;            // 1: x_{l+1} = x_l + MoE_l(.); 0: out = MoE(x)
+    int *err;
+};
+
+bool decode_stack_supported(uint32_t type, int E, int F, int U, int NE, int n_tok);
+cudaError_t launch_decode_stack(const StackArgs &a, uint32_t type, int sm_count, cudaStream_t s);
+
 // ---- expert parallelism: dispatch plan and the source-side sum of returned rows ----------
 // Slot id meaning "no expert of this rank" in expert-parallel rows.
 constexpr uint32_t kNoSlot = 0xffffffffu;

@@ -3,6 +3,7 @@
 cosine >= 0.9999 (tests/parity.py:28-44 metrics), top-k compared as per-token sets; the kernels
 actually land near 1e-6 relative, which the tighter checks below pin."""
 import json
+import os
 from pathlib import Path
 
 import numpy as np
@@ -175,7 +176,9 @@ def test_matvec_type_sweep(ctx, type_id, shape):
         check(x.astype(np.float64) @ dense.T, yt.cpu().numpy())
 
 
-def test_profiled_stack_reports_phase_times():
+def test_profiled_stack_reports_times():
+    """Per-phase kernels report router / gate-up / down times per layer; the persistent stack
+    kernel (GX_STACK_KERNEL=1) reports its total."""
     layers = [synth.make_layer(60 + i, n_expert=16, E=256, F=128, U=4) for i in range(3)]
     x = synth.tokens(61, 1, E=256)
     with abi.Context(device=0, max_tokens=4, max_layers=3, flags=abi.GX_FLAG_PROFILE) as c:
@@ -188,6 +191,15 @@ def test_profiled_stack_reports_phase_times():
             c.wait(c.stack_forward(0, 3, xt, yt))
         t = c.timings()
         assert t.layers == 3 and t.gate_up_ns > 0 and t.down_ns > 0 and t.router_ns > 0
+        check(oracle.stack(layers, x), yt.cpu().numpy(), tight=5e-5)
+        os.environ["GX_STACK_KERNEL"] = "1"
+        try:
+            for _ in range(3):
+                c.wait(c.stack_forward(0, 3, xt, yt))
+            t = c.timings()
+        finally:
+            del os.environ["GX_STACK_KERNEL"]
+        assert t.layers == 3 and t.total_ns > 0
         check(oracle.stack(layers, x), yt.cpu().numpy(), tight=5e-5)
 
 
