@@ -36,6 +36,7 @@ struct Layer {
     uint8_t *gate = nullptr, *up = nullptr, *down = nullptr;
     uint64_t gate_expert_bytes = 0, down_expert_bytes = 0;
     float *router = nullptr, *bias = nullptr, *gate_signs = nullptr, *down_signs = nullptr;
+    uint8_t *router_parts = nullptr;  // router as three bf16 parts, tcgen05 tiles (many-token path)
 };
 
 struct Matrix {
@@ -177,6 +178,44 @@ gx_result sync_all(gx_context *c, uint32_t timeout_ms) {
     return wait_event(c, c->events[t % kEvents], timeout_ms);
 }
 
+// The router as three bf16 parts W = W0 + W1 + W2 (each the bf16 rounding of what the parts before
+// it leave), laid out as the router tensor-core kernel reads them: tiles of 128 experts x 64
+// columns, [expert tile][column step][part], each 128-byte swizzled K-major (row r of a tile at
+// (r/8)*1024 + (r%8)*128, its 16-byte chunk c at position c ^ (r%8)). Experts past NE are zero.
+uint16_t bf16_bits_rn_host(float f) {
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+float bf16_value_host(uint16_t b) {
+    const uint32_t u = (uint32_t)b << 16;
+    float f;
+    std::memcpy(&f, &u, 4);
+    return f;
+}
+std::vector<uint16_t> router_parts(const float *W, uint64_t NE, uint64_t E) {
+    const uint64_t NT = (NE + 127) / 128, KS = E / 64;
+    std::vector<uint16_t> out(gx::router_parts_bytes((int)NE, (int)E) / 2, 0);
+    for (uint64_t nt = 0; nt < NT; ++nt)
+        for (uint64_t ks = 0; ks < KS; ++ks)
+            for (uint32_t r = 0; r < 128; ++r) {
+                const uint64_t e = nt * 128 + r;
+                if (e >= NE) continue;
+                for (uint32_t col = 0; col < 64; ++col) {
+                    float rest = W[e * E + ks * 64 + col];
+                    const uint32_t off = (r >> 3) * 1024u + (r & 7u) * 128u + ((((col * 2u) >> 4) ^ (r & 7u)) << 4) +
+                                         ((col * 2u) & 15u);
+                    for (int j = 0; j < 3; ++j) {
+                        const uint16_t b = bf16_bits_rn_host(rest);
+                        rest -= bf16_value_host(b);
+                        out[(((nt * KS + ks) * 3 + (uint64_t)j) * 16384u + off) / 2] = b;
+                    }
+                }
+            }
+    return out;
+}
+
 gx_result ensure_scratch(gx_context *c) {
     const size_t T = c->max_tokens ? c->max_tokens : 1;
     // Sized for the largest shapes the ABI accepts: E <= 4096, F <= 1024, NE <= 512, U <= 16.
@@ -283,6 +322,19 @@ gx_result ensure_prefill(gx_context *c, const Layer &L, size_t slots) {
     return GX_OK;
 }
 
+// Raw router logits of n_tok tokens into c->logits as *splits partial sums: on the tensor cores
+// when the layer carries its bf16 router parts, else the fp32 CUDA-core GEMM.
+cudaError_t launch_router_logits(gx_context *c, const Layer &L, const void *x, int xb, uint32_t n_tok, int *splits) {
+    if (L.router_parts && L.n_expert <= 512) {
+        *splits = gx::router_tc_splits((int)n_tok, (int)L.n_expert, (int)L.E, c->sm_count);
+        return gx::launch_router_tc(x, xb, (int)n_tok, (int)L.n_expert, (int)L.E, L.router_parts, c->logits, *splits,
+                                    c->err, c->stream);
+    }
+    *splits = (L.E % (4 * 32) == 0) ? 4 : 1;
+    return gx::launch_router_gemm(L.router, x, xb, (int)n_tok, (int)L.n_expert, (int)L.E, c->logits, *splits,
+                                  c->stream);
+}
+
 // Many-token layer on tensor cores: router GEMM, per-token selection, grouping, packed f16
 // operand tiles, two grouped tcgen05 GEMMs with trellis decoding, combine.
 // ev (GX_FLAG_PROFILE): start, after selection/grouping/packing, after the gate/up GEMM, end.
@@ -294,9 +346,8 @@ gx_result enqueue_layer_prefill(gx_context *c, const Layer &L, const void *x, ui
     auto &p = c->pf;
     const int xb = x_dtype == GX_BF16;
     if (ev) GX_CUDA(record_phase(ev[0], c->stream));
-    const int splits = (L.E % (4 * 32) == 0) ? 4 : 1;
-    GX_CUDA(gx::launch_router_gemm(L.router, x, xb, (int)n_tok, (int)L.n_expert, (int)L.E, c->logits, splits,
-                                   c->stream));
+    int splits;
+    GX_CUDA(launch_router_logits(c, L, x, xb, n_tok, &splits));
     gx::RouterArgs ra{};
     ra.W = L.router;
     ra.bias = L.bias;
@@ -493,9 +544,8 @@ gx_result enqueue_layer_ep(gx_context *c, const Layer &L, const void *x, uint32_
     const size_t stride = n_tok ? n_tok : 1;  // send rows reserved per destination
     if (ev) GX_CUDA(record_phase(ev[0], c->stream));
     if (n_tok > 0) {
-        const int splits = (L.E % (4 * 32) == 0) ? 4 : 1;
-        GX_CUDA(gx::launch_router_gemm(L.router, x, xb, (int)n_tok, (int)L.n_expert, (int)L.E, c->logits, splits,
-                                       c->stream));
+        int splits;
+        GX_CUDA(launch_router_logits(c, L, x, xb, n_tok, &splits));
         gx::RouterArgs ra{};
         ra.W = L.router;
         ra.bias = L.bias;
@@ -1010,6 +1060,8 @@ GX_API gx_result gx_upload_layer(gx_context *c, uint32_t layer, const gx_layer_d
     const uint64_t o_bias = off; off = align256(off + NE * 4);
     const uint64_t o_gs = off; off = align256(off + E * 4);
     const uint64_t o_ds = off; off = align256(off + F * 4);
+    const bool with_parts = E % 64 == 0;
+    const uint64_t o_rp = off; off = align256(off + (with_parts ? gx::router_parts_bytes((int)NE, (int)E) : 0));
     uint8_t *arena = nullptr;
     GX_CUDA(cudaMalloc(&arena, off));
     uint8_t *raw = nullptr;
@@ -1039,6 +1091,11 @@ GX_API gx_result gx_upload_layer(gx_context *c, uint32_t layer, const gx_layer_d
         e = cudaMemcpyAsync(arena + o_gs, d->gate_signs, E * 4, cudaMemcpyHostToDevice, c->stream);
     if (e == cudaSuccess && d->down_signs)
         e = cudaMemcpyAsync(arena + o_ds, d->down_signs, F * 4, cudaMemcpyHostToDevice, c->stream);
+    std::vector<uint16_t> rparts;
+    if (e == cudaSuccess && with_parts) {
+        rparts = router_parts(d->router, NE, E);
+        e = cudaMemcpyAsync(arena + o_rp, rparts.data(), rparts.size() * 2, cudaMemcpyHostToDevice, c->stream);
+    }
     if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
     cudaFree(raw);
     if (e != cudaSuccess) {
@@ -1065,6 +1122,7 @@ GX_API gx_result gx_upload_layer(gx_context *c, uint32_t layer, const gx_layer_d
     L.bias = reinterpret_cast<float *>(arena + o_bias);
     L.gate_signs = d->gate_signs ? reinterpret_cast<float *>(arena + o_gs) : nullptr;
     L.down_signs = d->down_signs ? reinterpret_cast<float *>(arena + o_ds) : nullptr;
+    L.router_parts = with_parts ? arena + o_rp : nullptr;
     {
         gx::StackLayer sl{};
         sl.router = L.router;

@@ -471,7 +471,7 @@ __device__ __forceinline__ bool phase_down(const StackArgs &a, const StackLayer 
     P = opaque(P);
     const StackGeo g = stack_geo<T>(a, P);
     const int tid = opaque((int)threadIdx.x), lane = tid & 31, warp = tid >> 5;
-    const int G = gridDim.x, cta = blockIdx.x, U = g.U;
+    const int U = g.U;
     int v0, v1;
     down_range(g, v0, v1);
     const int n_st = (v1 - v0 + P - 1) / P;

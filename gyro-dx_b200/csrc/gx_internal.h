@@ -128,6 +128,12 @@ struct CombineArgs {
 
 cudaError_t launch_router_gemm(const float *W, const void *x, int x_bf16, int n_tok, int NE, int E, float *C,
                                int splits, cudaStream_t s);
+// Router GEMM on tcgen05 (gx_router_tc.cu): wparts holds the router as three bf16 parts in
+// 128-expert x 64-column swizzled tiles (router_parts_bytes); logits are [splits][n_tok][NE].
+size_t router_parts_bytes(int NE, int E);
+int router_tc_splits(int n_tok, int NE, int E, int sm_count);
+cudaError_t launch_router_tc(const void *x, int x_bf16, int n_tok, int NE, int E, const uint8_t *wparts,
+                             float *logits, int splits, int *err, cudaStream_t s);
 cudaError_t launch_rotate_tokens(const void *x, int x_bf16, const float *xscale, const float *signs, int n_tok,
                                 int E, __half *xh, cudaStream_t s, const int *scatter = nullptr, int n_dst = 0);
 
