@@ -69,6 +69,7 @@ def parse():
     p.add_argument("--layers", type=int, default=N_LAYERS)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=15.0)
+    p.add_argument("--no-replicas", action="store_true", help="ep-prefill: plain expert sharding, no replicas")
     return p.parse_args()
 
 
@@ -551,6 +552,20 @@ def run_ep(args):
     for i in range(W):
         ticket = ctx.stack_forward(0, args.layers, xs[i % 2], y)
     ctx.wait(ticket)
+    replicas = []
+    if dist and not args.no_replicas:
+        # expert-parallel load balance: the warm-up's routed-slot counts, summed over ranks,
+        # choose per layer the popular experts every rank serves for its own tokens
+        from gyro_moe import balance
+        for l in range(args.layers):
+            cnt = torch.from_numpy(ctx.expert_counts(l, reset=True).astype(np.int64)).to(dev)
+            dist.all_reduce(cnt)
+            rep = balance.choose_replicas(cnt.cpu().numpy(), world)
+            ctx.replicate_experts(l, rep)
+            replicas.append(len(rep))
+        for i in range(W):
+            ticket = ctx.stack_forward(0, args.layers, xs[i % 2], y)
+        ctx.wait(ticket)
     torch.cuda.synchronize(dev)
     stream = torch.cuda.ExternalStream(ctx.stream(), device=dev)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -612,6 +627,7 @@ def run_ep(args):
                    "tokens": T, "sequences": EP_SEQS, "layers": args.layers, "hidden": E, "experts": NE,
                    "experts_per_gpu": per, "top_k": U, "ffn": F, "type": "TQ2_T",
                    "parallelism": f"expert parallel x{world} (NCCL dispatch/combine)" if world > 1 else "single GPU",
+                   "replicated_experts_per_layer": (sum(replicas) / len(replicas)) if replicas else 0,
                    "tokens_per_rank_max": max_tok,
                    "l2": "inputs larger than L2: a step reads every touched expert of 40 layers"},
         "roofline": {

@@ -37,7 +37,17 @@ struct Layer {
     uint64_t gate_expert_bytes = 0, down_expert_bytes = 0;
     float *router = nullptr, *bias = nullptr, *gate_signs = nullptr, *down_signs = nullptr;
     uint8_t *router_parts = nullptr;  // router as three bf16 parts, tcgen05 tiles (many-token path)
+    // expert parallelism: slots after the local shard that hold copies of hot experts, the
+    // route of every global expert (serving rank or -1 = the token's own rank, local index),
+    // and this rank's routed-slot count per global expert
+    uint32_t replica_slots = 0;
+    std::vector<uint32_t> replicas;
+    int2 *route = nullptr;
+    unsigned *expert_count = nullptr;
 };
+
+// Copies of hot experts one expert-parallel rank can hold per layer, beside its own shard.
+constexpr uint32_t kMaxReplicas = 32;
 
 struct Matrix {
     uint32_t type = 0, rows = 0, cols = 0;
@@ -66,8 +76,9 @@ struct gx_context {
         __half *xh = nullptr;
         float *act = nullptr;
         __half *Y = nullptr;
-        int *ints = nullptr;  // expert_count | tile_expert | tile_rows | n_mtiles | row_slot | slot_row
-        int *expert_count = nullptr, *tile_expert = nullptr, *tile_rows = nullptr, *n_mtiles = nullptr;
+        int *ints = nullptr;  // expert_count | cursor | tile_expert | tile_rows | n_mtiles | row_slot | slot_row
+        int *expert_count = nullptr, *cursor = nullptr, *tile_expert = nullptr, *tile_rows = nullptr,
+            *n_mtiles = nullptr;
         int *row_slot = nullptr, *slot_row = nullptr;
     } pf;
     uint32_t *ids = nullptr;
@@ -288,7 +299,7 @@ cudaError_t record_phase(cudaEvent_t ev, cudaStream_t s) {
 // Prefill buffers for max_tokens tokens of a layer shape. Rows are padded per expert to
 // 128-row tiles: at most slots/128 + min(NE, slots) tiles.
 gx_result ensure_prefill(gx_context *c, const Layer &L, size_t slots) {
-    const size_t tiles = (slots + 127) / 128 + std::min<size_t>(L.local_experts, slots);
+    const size_t tiles = (slots + 127) / 128 + std::min<size_t>(L.local_experts + L.replica_slots, slots);
     auto &p = c->pf;
     if (p.max_tiles >= tiles && p.E >= L.E && p.F >= L.F && p.slots >= slots) return GX_OK;
     void *old[] = {p.A, p.A2, p.act, p.Y, p.ints, p.xh};
@@ -307,10 +318,11 @@ gx_result ensure_prefill(gx_context *c, const Layer &L, size_t slots) {
     GX_CUDA(cudaMalloc(&p.act, tiles * 128 * L.F * sizeof(float)));
     GX_CUDA(cudaMalloc(&p.Y, tiles * 128 * L.E * sizeof(__half)));
     GX_CUDA(cudaMalloc(&p.xh, (size_t)c->max_tokens * L.E * sizeof(__half)));
-    const size_t n_ints = 512 + 2 * tiles + 1 + tiles * 128 + slots;
+    const size_t n_ints = 1024 + 2 * tiles + 1 + tiles * 128 + slots;
     GX_CUDA(cudaMalloc(&p.ints, n_ints * sizeof(int)));
     p.expert_count = p.ints;
-    p.tile_expert = p.expert_count + 512;
+    p.cursor = p.expert_count + 512;
+    p.tile_expert = p.cursor + 512;
     p.tile_rows = p.tile_expert + tiles;
     p.n_mtiles = p.tile_rows + tiles;
     p.row_slot = p.n_mtiles + 1;
@@ -373,6 +385,7 @@ gx_result enqueue_layer_prefill(gx_context *c, const Layer &L, const void *x, ui
     ga.n_slots = (int)(n_tok * L.U);
     ga.NE = (int)L.local_experts;
     ga.expert_count = p.expert_count;
+    ga.cursor = p.cursor;
     ga.tile_expert = p.tile_expert;
     ga.tile_rows = p.tile_rows;
     ga.n_mtiles = p.n_mtiles;
@@ -574,6 +587,9 @@ gx_result enqueue_layer_ep(gx_context *c, const Layer &L, const void *x, uint32_
     pa.U = (int)U;
     pa.NE = (int)L.n_expert;
     pa.W = W;
+    pa.rank = (int)c->rank;
+    pa.route = L.route;
+    pa.expert_count = L.expert_count;
     pa.stride = (int)stride;
     pa.pos_of = e.pos_of;
     pa.send_ids = e.send_ids;
@@ -633,8 +649,9 @@ gx_result enqueue_layer_ep(gx_context *c, const Layer &L, const void *x, uint32_
         gx::GroupArgs ga{};
         ga.ids = e.recv_ids;
         ga.n_slots = (int)(R * U);
-        ga.NE = (int)L.local_experts;
+        ga.NE = (int)(L.local_experts + L.replica_slots);
         ga.expert_count = p.expert_count;
+        ga.cursor = p.cursor;
         ga.tile_expert = p.tile_expert;
         ga.tile_rows = p.tile_rows;
         ga.n_mtiles = p.n_mtiles;
@@ -659,7 +676,7 @@ gx_result enqueue_layer_ep(gx_context *c, const Layer &L, const void *x, uint32_
         gm.expert_bytes = L.gate_expert_bytes;
         gm.K = (int)L.E;
         gm.n_ntiles = (int)(L.F / 128);
-        gm.n_expert = (int)L.local_experts;
+        gm.n_expert = (int)(L.local_experts + L.replica_slots);
         gm.A = p.A;
         gm.tile_expert = p.tile_expert;
         gm.tile_rows = p.tile_rows;
@@ -1052,10 +1069,13 @@ GX_API gx_result gx_upload_layer(gx_context *c, uint32_t layer, const gx_layer_d
     }
     const uint64_t NEl = NE / c->world, first = c->rank * NEl;
     const uint64_t gate_local = NEl * F * gate_row, down_local = NEl * E * down_row;
+    const uint64_t R = c->world > 1 ? std::min<uint64_t>(kMaxReplicas, NE - NEl) : 0;  // replica slots
     uint64_t off = 0;
-    const uint64_t o_gate = off; off = align256(off + gate_local);
-    const uint64_t o_up = off; off = align256(off + gate_local);
-    const uint64_t o_down = off; off = align256(off + down_local);
+    const uint64_t o_gate = off; off = align256(off + (NEl + R) * F * gate_row);
+    const uint64_t o_up = off; off = align256(off + (NEl + R) * F * gate_row);
+    const uint64_t o_down = off; off = align256(off + (NEl + R) * E * down_row);
+    const uint64_t o_route = off; off = align256(off + (c->world > 1 ? NE * sizeof(int2) : 0));
+    const uint64_t o_count = off; off = align256(off + (c->world > 1 ? NE * sizeof(unsigned) : 0));
     const uint64_t o_router = off; off = align256(off + NE * E * 4);
     const uint64_t o_bias = off; off = align256(off + NE * 4);
     const uint64_t o_gs = off; off = align256(off + E * 4);
@@ -1091,6 +1111,13 @@ GX_API gx_result gx_upload_layer(gx_context *c, uint32_t layer, const gx_layer_d
         e = cudaMemcpyAsync(arena + o_gs, d->gate_signs, E * 4, cudaMemcpyHostToDevice, c->stream);
     if (e == cudaSuccess && d->down_signs)
         e = cudaMemcpyAsync(arena + o_ds, d->down_signs, F * 4, cudaMemcpyHostToDevice, c->stream);
+    std::vector<int2> route;
+    if (e == cudaSuccess && c->world > 1) {
+        route.resize(NE);
+        for (uint64_t x = 0; x < NE; ++x) route[x] = make_int2((int)(x / NEl), (int)(x % NEl));
+        e = cudaMemcpyAsync(arena + o_route, route.data(), NE * sizeof(int2), cudaMemcpyHostToDevice, c->stream);
+        if (e == cudaSuccess) e = cudaMemsetAsync(arena + o_count, 0, NE * sizeof(unsigned), c->stream);
+    }
     std::vector<uint16_t> rparts;
     if (e == cudaSuccess && with_parts) {
         rparts = router_parts(d->router, NE, E);
@@ -1123,6 +1150,10 @@ GX_API gx_result gx_upload_layer(gx_context *c, uint32_t layer, const gx_layer_d
     L.gate_signs = d->gate_signs ? reinterpret_cast<float *>(arena + o_gs) : nullptr;
     L.down_signs = d->down_signs ? reinterpret_cast<float *>(arena + o_ds) : nullptr;
     L.router_parts = with_parts ? arena + o_rp : nullptr;
+    L.replica_slots = (uint32_t)R;
+    L.replicas.clear();
+    L.route = c->world > 1 ? reinterpret_cast<int2 *>(arena + o_route) : nullptr;
+    L.expert_count = c->world > 1 ? reinterpret_cast<unsigned *>(arena + o_count) : nullptr;
     {
         gx::StackLayer sl{};
         sl.router = L.router;
@@ -1633,3 +1664,69 @@ GX_API gx_result gx_moe_forward_noalloc(gx_context *c, uint32_t layer, const voi
 }
 
 }  // extern "C"
+
+// ---- expert parallelism: usage counts and replicas of hot experts -------------------------
+extern "C" {
+
+GX_API gx_result gx_read_expert_counts(gx_context *c, uint32_t layer, uint32_t *counts, uint32_t reset,
+                                       uint32_t timeout_ms) {
+    if (!c || !counts) return GX_E_INVALIDARG;
+    if (c->broken) return GX_E_DEVICE;
+    if (layer >= c->layers.size() || !c->layers[layer].ready) return GX_E_STATE;
+    const Layer &L = c->layers[layer];
+    if (!L.expert_count) return GX_E_UNSUPPORTED;
+    GX_CUDA(cudaSetDevice(c->device));
+    GX_CUDA(cudaMemcpyAsync(c->h_out, L.expert_count, L.n_expert * sizeof(unsigned), cudaMemcpyDeviceToHost,
+                            c->stream));
+    if (reset) GX_CUDA(cudaMemsetAsync(L.expert_count, 0, L.n_expert * sizeof(unsigned), c->stream));
+    gx_result r = sync_all(c, timeout_ms);
+    if (r != GX_OK) return r;
+    std::memcpy(counts, c->h_out, L.n_expert * sizeof(unsigned));
+    return GX_OK;
+}
+
+GX_API gx_result gx_replicate_experts(gx_context *c, uint32_t layer, const uint32_t *experts, uint32_t n,
+                                      uint32_t timeout_ms) {
+    if (!c || (n && !experts)) return GX_E_INVALIDARG;
+    if (c->broken) return GX_E_DEVICE;
+    if (layer >= c->layers.size() || !c->layers[layer].ready) return GX_E_STATE;
+    Layer &L = c->layers[layer];
+    if (!L.route) return GX_E_UNSUPPORTED;
+    if (n > L.replica_slots) return GX_E_INVALIDARG;
+    std::vector<char> seen(L.n_expert, 0);
+    for (uint32_t i = 0; i < n; ++i) {
+        if (experts[i] >= L.n_expert || seen[experts[i]]) return GX_E_INVALIDARG;
+        seen[experts[i]] = 1;
+    }
+    GX_CUDA(cudaSetDevice(c->device));
+    const uint32_t NEl = L.local_experts;
+    // every rank's replica slot i receives expert experts[i] from the rank whose shard holds it
+    const uint64_t dn_bytes = L.down_expert_bytes, gu_bytes = L.gate_expert_bytes;
+    c->nccl->GroupStart();
+    for (uint32_t i = 0; i < n; ++i) {
+        const uint32_t e = experts[i], owner = e / NEl, k = e % NEl;
+        uint8_t *bases[3] = {L.gate, L.up, L.down};
+        const uint64_t bytes[3] = {gu_bytes, gu_bytes, dn_bytes};
+        for (int p = 0; p < 3; ++p) {
+            const uint8_t *src = bases[p] + (uint64_t)k * bytes[p];
+            uint8_t *dst = bases[p] + (uint64_t)(NEl + i) * bytes[p];
+            c->nccl->Broadcast(src, dst, bytes[p], ncclUint8, (int)owner, c->comm, c->stream);
+        }
+    }
+    gx_result r = comm_group_end(c, "expert replication");
+    if (r != GX_OK) return r;
+    std::vector<int2> route(L.n_expert);
+    for (uint32_t x = 0; x < L.n_expert; ++x) route[x] = make_int2((int)(x / NEl), (int)(x % NEl));
+    for (uint32_t i = 0; i < n; ++i) {
+        const uint32_t e = experts[i], owner = e / NEl;
+        route[e] = make_int2(-1, owner == c->rank ? (int)(e % NEl) : (int)(NEl + i));
+    }
+    GX_CUDA(cudaMemcpyAsync(L.route, route.data(), route.size() * sizeof(int2), cudaMemcpyHostToDevice, c->stream));
+    r = sync_all(c, timeout_ms);
+    if (r != GX_OK) return r;
+    L.replicas.assign(experts, experts + n);
+    return GX_OK;
+}
+
+}  // extern "C"
+

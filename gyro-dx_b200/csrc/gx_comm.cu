@@ -31,6 +31,7 @@ const NcclApi *nccl_api() {
              bind(h, api.CommGetAsyncError, "ncclCommGetAsyncError") && bind(h, api.CommAbort, "ncclCommAbort") &&
              bind(h, api.CommDestroy, "ncclCommDestroy") && bind(h, api.GroupStart, "ncclGroupStart") &&
              bind(h, api.GroupEnd, "ncclGroupEnd") && bind(h, api.Send, "ncclSend") && bind(h, api.Recv, "ncclRecv") &&
+             bind(h, api.Broadcast, "ncclBroadcast") &&
              bind(h, api.GetErrorString, "ncclGetErrorString") && bind(h, api.GetVersion, "ncclGetVersion");
     });
     return ok ? &api : nullptr;

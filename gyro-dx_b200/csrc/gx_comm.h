@@ -22,6 +22,7 @@ struct NcclApi {
     ncclResult_t (*GroupEnd)();
     ncclResult_t (*Send)(const void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t);
     ncclResult_t (*Recv)(void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t);
+    ncclResult_t (*Broadcast)(const void *, void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t);
     const char *(*GetErrorString)(ncclResult_t);
     ncclResult_t (*GetVersion)(int *);
 };

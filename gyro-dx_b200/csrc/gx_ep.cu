@@ -1,7 +1,8 @@
 // gx_ep.cu — expert-parallel dispatch plan and the sum of returned partial rows.
 //
-// With W ranks, rank d serves experts [d*NE/W, (d+1)*NE/W). A token travels once to every rank
-// that serves at least one of its U selected experts, carrying its U slots as destination-local
+// With W ranks, rank d serves experts [d*NE/W, (d+1)*NE/W), except the experts a route table
+// marks as replicated, which every rank serves for its own tokens. A token travels once to every
+// rank that serves at least one of its U selected experts, carrying its U slots as destination-local
 // expert ids (kNoSlot for experts served elsewhere) and routing weights. The destination
 // computes sum_k w_k * Expert_k(x) over its own slots and returns one partial row, and the source
 // adds the partial rows of all destinations. This is the scatter / gather around the expert
@@ -15,6 +16,20 @@
 #include "gx_internal.h"
 
 namespace gx {
+
+// Rank that serves expert e (< NE) and the expert's index among that rank's local experts: the
+// route table when the layer has one (replicated experts are served where the token is), else
+// the contiguous shard of e.
+__device__ __forceinline__ int serving_rank(const EpPlanArgs &a, uint32_t e, uint32_t per) {
+    if (a.route) {
+        const int r = a.route[e].x;
+        return r < 0 ? a.rank : r;
+    }
+    return (int)(e / per);
+}
+__device__ __forceinline__ uint32_t local_expert(const EpPlanArgs &a, uint32_t e, uint32_t lo) {
+    return a.route ? (uint32_t)a.route[e].y : e - lo;
+}
 
 // One CTA of 1024 threads per destination rank d: send rows for d are the tokens with a slot on
 // d, in token order (so each destination sees a stable order), at rows [d*stride, d*stride+count).
@@ -31,8 +46,12 @@ __global__ void __launch_bounds__(1024) ep_plan_kernel(EpPlanArgs a) {
         if (t < a.n_tok) {
             for (int k = 0; k < a.U; ++k) {
                 const uint32_t e = a.ids[(size_t)t * a.U + k];
-                if (e >= (uint32_t)a.NE) atomicExch(a.err, KERR_BOUNDS);
-                else if (e - lo < per) mine = true;
+                if (e >= (uint32_t)a.NE) {
+                    atomicExch(a.err, KERR_BOUNDS);
+                    continue;
+                }
+                if (d == 0 && a.expert_count) atomicAdd(a.expert_count + e, 1u);
+                if (serving_rank(a, e, per) == d) mine = true;
             }
         }
         const unsigned vote = __ballot_sync(0xffffffffu, mine);
@@ -57,8 +76,8 @@ __global__ void __launch_bounds__(1024) ep_plan_kernel(EpPlanArgs a) {
                 a.pos_of[(size_t)t * a.W + d] = (int)row;
                 for (int k = 0; k < a.U; ++k) {
                     const uint32_t e = a.ids[(size_t)t * a.U + k];
-                    const bool here = e < (uint32_t)a.NE && e - lo < per;
-                    a.send_ids[row * a.U + k] = here ? e - lo : kNoSlot;
+                    const bool here = e < (uint32_t)a.NE && serving_rank(a, e, per) == d;
+                    a.send_ids[row * a.U + k] = here ? local_expert(a, e, lo) : kNoSlot;
                     a.send_w[row * a.U + k] = here ? a.weights[(size_t)t * a.U + k] : 0.f;
                 }
             } else {

@@ -80,6 +80,7 @@ struct GroupArgs {
     const uint32_t *ids;     // [n_slots] expert of each slot (local numbering)
     int n_slots, NE;
     int *expert_count;       // [NE]
+    int *cursor;             // [NE] scratch: next free padded row of each expert
     int *tile_expert;        // [max_tiles] expert of each 128-row tile
     int *tile_rows;          // [max_tiles] valid rows in the tile
     int *n_mtiles;           // [1]
@@ -176,7 +177,10 @@ constexpr uint32_t kNoSlot = 0xffffffffu;
 struct EpPlanArgs {
     const uint32_t *ids;     // [n_tok][U] global expert ids from the selection
     const float *weights;    // [n_tok][U]
-    int n_tok, U, NE, W;     // rank d serves experts [d*NE/W, (d+1)*NE/W)
+    int n_tok, U, NE, W;     // without a route table rank d serves experts [d*NE/W, (d+1)*NE/W)
+    int rank;                // this rank (route entries with rank -1 mean "here")
+    const int2 *route;       // [NE] (serving rank or -1, local expert id there), or nullptr
+    unsigned *expert_count;  // [NE] slots routed to each expert, accumulated, or nullptr
     int stride;              // send-buffer rows reserved per destination (>= n_tok)
     int *pos_of;             // [n_tok][W] send row of (token, destination), -1 if none
     uint32_t *send_ids;      // [W*stride][U] destination-local expert id or kNoSlot

@@ -84,69 +84,66 @@ __global__ void __launch_bounds__(256) router_gemm_kernel(const float *__restric
 }
 
 // ------------------------------------------------------------------------------------------
-// Grouping: one CTA of 1024 threads. Stable order of slots within each expert (the counting
-// sort of src/engine.zig:553-564), each expert's rows padded to whole 128-row tiles. Slots whose
-// id is kNoSlot (expert-parallel rows carry them for experts of other ranks) get no row.
+// Grouping (the counting sort of src/engine.zig:553-564 without its stable order, which no
+// result depends on: every output row is computed from its own input row). Three kernels:
+//   count  per-expert slot counts (warp-aggregated atomics)
+//   scan   one CTA: 128-row tiles per expert, tile list, each expert's first row
+//   place  each slot takes the next row of its expert (warp-aggregated atomics)
+// Slots whose id is kNoSlot (expert-parallel rows carry them for experts of other ranks) get no
+// row; any other id outside [0, NE) is reported as KERR_BOUNDS.
 // ------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(1024) group_kernel(GroupArgs a) {
-    extern __shared__ __align__(16) int gsm[];
-    int *count = gsm;                 // [NE]
-    int *tile_base = count + a.NE;    // [NE + 1]
-    int *run = tile_base + a.NE + 1;  // [NE] rows placed so far
-    int *wcount = run + a.NE;         // [32][NE] per-warp counts of the current chunk
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    for (int e = tid; e < a.NE; e += 1024) { count[e] = 0; run[e] = 0; }
-    __syncthreads();
-    for (int s = tid; s < a.n_slots; s += 1024) {
-        const uint32_t e = a.ids[s];
-        if (e < (uint32_t)a.NE) atomicAdd(&count[e], 1);
-        else if (e != kNoSlot) atomicExch(a.err, KERR_BOUNDS);
+__global__ void __launch_bounds__(1024) group_count_kernel(GroupArgs a) {
+    const int s = blockIdx.x * 1024 + threadIdx.x;
+    const bool live = s < a.n_slots;
+    const uint32_t e = live ? a.ids[s] : kNoSlot;
+    const bool ok = live && e < (uint32_t)a.NE;
+    if (live && !ok && e != kNoSlot) atomicExch(a.err, KERR_BOUNDS);
+    const unsigned peers = __match_any_sync(0xffffffffu, ok ? e : 0xffffffffu);
+    if (ok && __ffs(peers) - 1 == (int)(threadIdx.x & 31)) atomicAdd(&a.expert_count[e], __popc(peers));
+}
+
+__global__ void __launch_bounds__(512) group_scan_kernel(GroupArgs a) {
+    __shared__ int wsum[16];
+    const int e = threadIdx.x, lane = e & 31, warp = e >> 5;
+    const int cnt = e < a.NE ? a.expert_count[e] : 0;
+    const int nt = (cnt + 127) / 128;
+    int incl = nt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
     }
+    if (lane == 31) wsum[warp] = incl;
     __syncthreads();
-    if (tid == 0) {
-        int acc = 0;
-        for (int e = 0; e < a.NE; ++e) {
-            tile_base[e] = acc;
-            a.expert_count[e] = count[e];
-            acc += (count[e] + 127) / 128;
+    int before = 0;
+    for (int w = 0; w < warp; ++w) before += wsum[w];
+    const int base = before + incl - nt;  // exclusive prefix of tiles
+    if (e < a.NE) {
+        for (int m = 0; m < nt; ++m) {
+            a.tile_expert[base + m] = e;
+            a.tile_rows[base + m] = min(128, cnt - m * 128);
         }
-        tile_base[a.NE] = acc;
-        *a.n_mtiles = acc;
+        a.cursor[e] = base * 128;
     }
-    __syncthreads();
-    for (int e = tid; e < a.NE; e += 1024) {
-        const int n = (count[e] + 127) / 128;
-        for (int m = 0; m < n; ++m) {
-            a.tile_expert[tile_base[e] + m] = e;
-            a.tile_rows[tile_base[e] + m] = min(128, count[e] - m * 128);
-        }
-    }
-    for (int base = 0; base < a.n_slots; base += 1024) {
-        for (int i = tid; i < 32 * a.NE; i += 1024) wcount[i] = 0;
-        __syncthreads();
-        const int s = base + tid;
-        const bool live = s < a.n_slots;
-        const uint32_t e = live ? a.ids[s] : 0xffffffffu;
-        const bool ok = live && e < (uint32_t)a.NE;
-        const unsigned same = __match_any_sync(0xffffffffu, ok ? e : 0xffffffffu);
-        const int rank_w = __popc(same & ((1u << lane) - 1u));
-        if (ok && rank_w == 0) wcount[warp * a.NE + e] = __popc(same);
-        __syncthreads();
-        if (live && !ok) a.slot_row[s] = -1;
-        if (ok) {
-            int before = run[e] + rank_w;
-            for (int w = 0; w < warp; ++w) before += wcount[w * a.NE + e];
-            const int row = tile_base[e] * 128 + before;
-            a.row_slot[row] = s;
-            a.slot_row[s] = row;
-        }
-        __syncthreads();
-        for (int e2 = tid; e2 < a.NE; e2 += 1024) {
-            int add = 0;
-            for (int w = 0; w < 32; ++w) add += wcount[w * a.NE + e2];
-            run[e2] += add;
-        }
-        __syncthreads();
+    if (e == 511) *a.n_mtiles = before + incl;
+}
+
+__global__ void __launch_bounds__(1024) group_place_kernel(GroupArgs a) {
+    const int s = blockIdx.x * 1024 + threadIdx.x, lane = threadIdx.x & 31;
+    const bool live = s < a.n_slots;
+    const uint32_t e = live ? a.ids[s] : kNoSlot;
+    const bool ok = live && e < (uint32_t)a.NE;
+    const unsigned peers = __match_any_sync(0xffffffffu, ok ? e : 0xffffffffu);
+    const int leader = __ffs(peers) - 1;
+    int base = 0;
+    if (ok && lane == leader) base = atomicAdd(&a.cursor[e], __popc(peers));
+    base = __shfl_sync(0xffffffffu, base, leader);
+    if (ok) {
+        const int row = base + __popc(peers & ((1u << lane) - 1u));
+        a.row_slot[row] = s;
+        a.slot_row[s] = row;
+    } else if (live) {
+        a.slot_row[s] = -1;
     }
 }
 
@@ -577,11 +574,13 @@ cudaError_t launch_router_gemm(const float *W, const void *x, int x_bf16, int n_
 }
 
 cudaError_t launch_group(const GroupArgs &a, cudaStream_t s) {
-    const int smem = (3 * a.NE + 1 + 32 * a.NE) * 4;
-    static const cudaError_t once = cudaFuncSetAttribute(group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                         (3 * 512 + 1 + 32 * 512) * 4);
-    if (once != cudaSuccess) return once;
-    group_kernel<<<1, 1024, smem, s>>>(a);
+    if (a.NE > 512) return cudaErrorInvalidValue;
+    cudaError_t e = cudaMemsetAsync(a.expert_count, 0, (size_t)a.NE * sizeof(int), s);
+    if (e != cudaSuccess) return e;
+    const unsigned blocks = (unsigned)((a.n_slots + 1023) / 1024);
+    if (blocks) group_count_kernel<<<blocks, 1024, 0, s>>>(a);
+    group_scan_kernel<<<1, 512, 0, s>>>(a);
+    if (blocks) group_place_kernel<<<blocks, 1024, 0, s>>>(a);
     return cudaGetLastError();
 }
 

@@ -84,32 +84,40 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(RtArgs a) {
     };
 
     if (warp < 4) {
-        // ---- activation parts: thread r writes row r (token m0 + r) of each part ----------
+        // ---- activation parts: thread r writes row r (token m0 + r) of each part; the row's
+        // next 64 columns are loaded while this step waits for its stage ----------------------
         const int r = tid;
         const int tok = m0 + r;
         const bool live = tok < a.n_tok;
+        constexpr int NV = AP == 1 ? 8 : 16;  // 16-byte loads per row and step
+        uint4 nx[NV];
+        auto fetch = [&](int i) {
+            const uint4 *src = reinterpret_cast<const uint4 *>(reinterpret_cast<const uint8_t *>(a.x) +
+                                                               ((size_t)tok * a.E + (size_t)(ks0 + i) * 64) * (AP == 1 ? 2 : 4));
+#pragma unroll
+            for (int v = 0; v < NV; ++v) nx[v] = live ? src[v] : make_uint4(0u, 0u, 0u, 0u);
+        };
+        if (nks > 0) fetch(0);
         bool ok = true;
+        const uint32_t rowoff = (uint32_t)(r >> 3) * 1024u + (uint32_t)(r & 7) * 128u;
         for (int i = 0; i < nks; ++i) {
             const int s = i % ST, round = i / ST;
+            uint4 cur[NV];
+#pragma unroll
+            for (int v = 0; v < NV; ++v) cur[v] = nx[v];
+            if (i + 1 < nks) fetch(i + 1);
             if (!wait(&empty[s], (round & 1) ^ 1)) { ok = false; break; }
             uint8_t *at = sm + s * STAGE;
-            const int k0 = (ks0 + i) * 64;
-            const uint32_t rowoff = (uint32_t)(r >> 3) * 1024u + (uint32_t)(r & 7) * 128u;
 #pragma unroll
             for (int c = 0; c < 8; ++c) {  // 16-byte chunk c = columns 8c .. 8c+7
                 uint32_t p[AP][4];
-                if (!live) {
-#pragma unroll
-                    for (int q = 0; q < AP; ++q) p[q][0] = p[q][1] = p[q][2] = p[q][3] = 0u;
-                } else if (AP == 1) {
-                    const uint4 v = *reinterpret_cast<const uint4 *>(
-                        reinterpret_cast<const unsigned short *>(a.x) + (size_t)tok * a.E + k0 + 8 * c);
-                    p[0][0] = v.x; p[0][1] = v.y; p[0][2] = v.z; p[0][3] = v.w;
+                if (AP == 1) {
+                    p[0][0] = cur[c].x; p[0][1] = cur[c].y; p[0][2] = cur[c].z; p[0][3] = cur[c].w;
                 } else {
-                    const float *src = reinterpret_cast<const float *>(a.x) + (size_t)tok * a.E + k0 + 8 * c;
-                    const float4 v0 = *reinterpret_cast<const float4 *>(src);
-                    const float4 v1 = *reinterpret_cast<const float4 *>(src + 4);
-                    const float f[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+                    const uint4 u0 = cur[2 * c], u1 = cur[(2 * c + 1) % NV];
+                    const float f[8] = {__uint_as_float(u0.x), __uint_as_float(u0.y), __uint_as_float(u0.z),
+                                        __uint_as_float(u0.w), __uint_as_float(u1.x), __uint_as_float(u1.y),
+                                        __uint_as_float(u1.z), __uint_as_float(u1.w)};
 #pragma unroll
                     for (int h = 0; h < 4; ++h) {
                         uint32_t lo[AP], hi[AP];

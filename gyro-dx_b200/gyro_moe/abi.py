@@ -77,6 +77,8 @@ SIGNATURES = {
     "gx_upload_matrix": [_P, _U32, _U32, _U32, _P, _U64, ctypes.POINTER(_U32), _U32],
     "gx_matvec": [_P, _U32, _P, _U32, _P, ctypes.POINTER(_U64)],
     "gx_read_timings": [_P, ctypes.POINTER(Timings)],
+    "gx_read_expert_counts": [_P, _U32, _P, _U32, _U32],
+    "gx_replicate_experts": [_P, _U32, _P, _U32, _U32],
     "gx_moe_forward_noalloc": [_P, _U32, _P, _U32, _U32, _P, _U32, _P, _P, ctypes.POINTER(_U64)],
     "gx_set_flags": [_P, _U32],
     "gx_destroy": [_P, _U32],
@@ -207,6 +209,20 @@ class Context:
         _check(self.lib.gx_moe_forward(self.handle, layer, _ptr(x), _dtype_code(x), n_tok, _ptr(y), _dtype_code(y),
                                        _ptr(ids), _ptr(weights), ctypes.byref(t)), "gx_moe_forward")
         return t.value
+
+    def expert_counts(self, layer: int, reset: bool = False, timeout_ms: int = 60000) -> np.ndarray:
+        """This rank's routed slots per global expert of a layer (expert-parallel contexts)."""
+        n = self.layers[layer]["n_expert"]
+        out = np.zeros(n, np.uint32)
+        _check(self.lib.gx_read_expert_counts(self.handle, layer, out.ctypes.data, int(reset), timeout_ms),
+               "gx_read_expert_counts")
+        return out
+
+    def replicate_experts(self, layer: int, experts, timeout_ms: int = 120000) -> None:
+        """Collective: every rank serves the listed global experts of the layer for its own tokens."""
+        ids = np.ascontiguousarray(np.asarray(experts, dtype=np.uint32))
+        _check(self.lib.gx_replicate_experts(self.handle, layer, ids.ctypes.data if ids.size else None, ids.size,
+                                             timeout_ms), "gx_replicate_experts")
 
     def forward_noalloc(self, layer: int, x, y, ids=None, weights=None) -> int:
         """gx_moe_forward_noalloc on device tensors: the decode layer on the library's static

@@ -217,6 +217,23 @@ GX_API gx_result gx_matvec(gx_context *context, uint32_t handle, const float *x,
 
 GX_API gx_result gx_read_timings(gx_context *context, gx_timings *out_timings);
 
+/* No counterpart in the reference (its bridge drives one GPU). Expert-parallel contexts only
+ * (world > 1, else GX_E_UNSUPPORTED). Copies into counts[n_expert] the number of this rank's
+ * routed slots per global expert of the layer since the last reset (reset != 0 zeroes them after
+ * the copy). Blocking. The host sums them over ranks to find the experts worth replicating. */
+GX_API gx_result gx_read_expert_counts(gx_context *context, uint32_t layer, uint32_t *counts, uint32_t reset,
+                                       uint32_t timeout_ms);
+
+/* No counterpart in the reference. Collective over the expert-parallel group: every rank passes
+ * the same list of n distinct global experts of the layer (n <= 32 and below the number of experts
+ * outside one rank's shard). Each listed expert's rank broadcasts its packed tiles into a replica
+ * slot on every other rank, and from then on every rank serves the listed experts for its own
+ * tokens, so their rows cross no link and the load of popular experts spreads over the group.
+ * A later call replaces the list (n = 0 restores plain sharding). Blocking; GX_E_COMM if a peer
+ * does not take part within the communication timeout. */
+GX_API gx_result gx_replicate_experts(gx_context *context, uint32_t layer, const uint32_t *experts, uint32_t n,
+                                      uint32_t timeout_ms);
+
 /* No counterpart in the reference. The routed-expert layer for decode batches that allocates no
  * device or host memory on any call. It is meant for hosts that may not allocate once they are
  * stepping: a serving host that hands all free HBM to its own pools (expert arena, caches) at

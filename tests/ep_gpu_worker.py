@@ -27,6 +27,10 @@ CASES = [
 ]
 
 
+REPLICATION_LAYER = dict(seed=34, n_expert=32, E=256, F=256, U=4, zipf=1.1)
+REPLICAS = [3, 20, 9]
+
+
 def make(kw):
     from gyro_moe import synth
     kw = dict(kw)
@@ -87,4 +91,19 @@ def worker(rank: int, world: int, out_dir: str) -> None:
             res["noalloc_rc"] = np.array(0)
         except abi.GxError as e:
             res["noalloc_rc"] = np.array(e.code)
+        # hot experts served where the token is: one from each shard, and a list naming one twice
+        layer = make(REPLICATION_LAYER)
+        ctx.upload_layer(0, layer)
+        x = tokens(20, rank, [40, 24][rank], layer["n_embd"])
+        res["rep_x"] = x
+        res["rep_y0"] = ctx.forward_host(0, x)
+        res["rep_counts0"] = ctx.expert_counts(0, reset=True)
+        ctx.replicate_experts(0, REPLICAS)
+        res["rep_y1"], res["rep_ids1"], _ = ctx.forward_host(0, x, want_routing=True)
+        res["rep_counts1"] = ctx.expert_counts(0)
+        try:
+            ctx.replicate_experts(0, [3, 3])
+            res["rep_dup_rc"] = np.array(0)
+        except abi.GxError as e:
+            res["rep_dup_rc"] = np.array(e.code)
     np.savez(Path(out_dir) / f"rank{rank}.npz", **res)

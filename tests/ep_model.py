@@ -5,6 +5,7 @@ Test infrastructure: it restates the exchange the library performs over NCCL
 the kernels. It checks the decomposition itself on the CPU:
 
 - Each rank routes its own tokens with the replicated router.
+- Replicated experts are served by the token's own rank (route table of gx_replicate_experts).
 - A token goes once to every rank that serves one of its U experts. It carries its U slots
   there: destination-local expert id, or NO_SLOT for experts served elsewhere.
 - The serving rank returns sum_k w_k * Expert_k(x) over its own slots.
@@ -29,35 +30,49 @@ for p in (ROOT, ROOT / "gyro-dx_b200", ROOT / "tests"):
 NO_SLOT = 0xFFFFFFFF
 
 
-def plan(ids: np.ndarray, weights: np.ndarray, n_expert: int, world: int):
+def route_table(n_expert: int, world: int, rank: int, replicas=()) -> np.ndarray:
+    """[n_expert][2]: (serving rank or -1 = the token's own rank, local expert index there), as
+    gx_replicate_experts sets it on `rank`: shard experts at their shard index, replica i of a
+    listed expert at slot per + i (or the shard index on the expert's own rank)."""
+    per = n_expert // world
+    route = np.stack([np.arange(n_expert) // per, np.arange(n_expert) % per], axis=1)
+    for i, e in enumerate(replicas):
+        route[e] = (-1, e % per if e // per == rank else per + i)
+    return route
+
+
+def plan(ids: np.ndarray, weights: np.ndarray, n_expert: int, world: int, rank: int = 0, replicas=()):
     """Dispatch plan, as ep_plan_kernel lays it out.
 
-    For destination d, the send rows are the tokens with a slot on d, in token order. Returns
-    pos_of [n][world] (-1 if the token is not sent there) and, per destination, (tokens, local
-    ids [rows][U], weights [rows][U])."""
+    For destination d, the send rows are the tokens with a slot served by d, in token order.
+    Returns pos_of [n][world] (-1 if the token is not sent there) and, per destination, (tokens,
+    local ids [rows][U], weights [rows][U])."""
     n, U = ids.shape
-    per = n_expert // world
+    route = route_table(n_expert, world, rank, replicas)
+    dest = np.where(route[ids, 0] < 0, rank, route[ids, 0]) if n else np.zeros((0, U), np.int64)
     pos_of = -np.ones((n, world), np.int64)
     sends = []
     for d in range(world):
-        here = (ids // per) == d
+        here = dest == d
         toks = np.nonzero(here.any(axis=1))[0]
-        loc = np.where(here[toks], ids[toks] - d * per, NO_SLOT).astype(np.uint32)
+        loc = np.where(here[toks], route[ids[toks], 1], NO_SLOT).astype(np.uint32)
         w = np.where(here[toks], weights[toks], 0.0).astype(np.float32)
         pos_of[toks, d] = np.arange(len(toks))
         sends.append((toks, loc.reshape(-1, U), w.reshape(-1, U)))
     return pos_of, sends
 
 
-def local_slice(layer: dict, rank: int, world: int) -> dict:
-    """The experts rank `rank` holds: rows [r*NE/W*F, ...) of gate/up, [r*NE/W*E, ...) of down."""
+def local_slice(layer: dict, rank: int, world: int, replicas=()) -> dict:
+    """The experts rank `rank` holds: its shard (rows [r*NE/W*F, ...) of gate/up, [r*NE/W*E, ...)
+    of down), then a copy of every replicated expert in list order."""
     per = layer["n_expert"] // world
     F, E = layer["n_ff"], layer["n_embd"]
+    experts = list(range(rank * per, (rank + 1) * per)) + list(replicas)
     out = dict(layer)
-    out["n_expert"] = per
-    out["gate"] = layer["gate"][rank * per * F:(rank + 1) * per * F]
-    out["up"] = layer["up"][rank * per * F:(rank + 1) * per * F]
-    out["down"] = layer["down"][rank * per * E:(rank + 1) * per * E]
+    out["n_expert"] = len(experts)
+    out["gate"] = np.concatenate([layer["gate"][e * F:(e + 1) * F] for e in experts])
+    out["up"] = np.concatenate([layer["up"][e * F:(e + 1) * F] for e in experts])
+    out["down"] = np.concatenate([layer["down"][e * E:(e + 1) * E] for e in experts])
     return out
 
 
@@ -89,7 +104,7 @@ def _exchange(parts: list, rank: int, world: int, dtype, width):
     return got
 
 
-def ep_layer(layer: dict, x: np.ndarray, rank: int, world: int) -> np.ndarray:
+def ep_layer(layer: dict, x: np.ndarray, rank: int, world: int, replicas=()) -> np.ndarray:
     """One expert-parallel layer on this rank's tokens x [n][E]; returns out [n][E]."""
     from oracle import oracle
     E, U, NE = layer["n_embd"], layer["n_used"], layer["n_expert"]
@@ -98,11 +113,11 @@ def ep_layer(layer: dict, x: np.ndarray, rank: int, world: int) -> np.ndarray:
         _, ids, w = oracle.moe_ffn(layer, x)          # selection with the replicated router
     else:
         ids, w = np.zeros((0, U), np.uint32), np.zeros((0, U), np.float32)
-    pos_of, sends = plan(ids.astype(np.int64), w, NE, world)
+    pos_of, sends = plan(ids.astype(np.int64), w, NE, world, rank, replicas)
     rows = _exchange([x[t] for t, _, _ in sends], rank, world, np.float32, E)
     rids = _exchange([loc.astype(np.int64) for _, loc, _ in sends], rank, world, np.int64, U)
     rw = _exchange([wt for _, _, wt in sends], rank, world, np.float32, U)
-    mine = local_slice(layer, rank, world)
+    mine = local_slice(layer, rank, world, replicas)
     R = [len(r) for r in rows]
     allrows = np.concatenate(rows) if sum(R) else np.zeros((0, E), np.float32)
     if sum(R):
@@ -143,7 +158,7 @@ def worker(rank: int, world: int, store: str, case: dict, result_dir: str) -> No
         if case.get("leave_rank") == rank:
             return                               # never joins the exchange
         try:
-            out = ep_layer(layer, x, rank, world)
+            out = ep_layer(layer, x, rank, world, case.get("replicas", ()))
         except RuntimeError as e:                # a peer that left: the collective ends with an error
             np.savez(os.path.join(result_dir, f"rank{rank}.npz"), error=str(e))
             return

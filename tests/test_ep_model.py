@@ -54,6 +54,20 @@ def test_all_traffic_to_one_rank(tmp_path):
     check(run(tmp_path, dict(BASE, seed=9, n_tok=[4, 6], only_rank=1)))
 
 
+def test_replicated_hot_experts_are_served_where_the_token_is(tmp_path):
+    # experts 1 and 9 (one from each shard) served locally on every rank: same layer output
+    check(run(tmp_path, dict(BASE, seed=12, zipf=1.1, n_tok=[8, 6], replicas=(9, 1))))
+
+
+def test_route_table_of_replicas():
+    r = ep_model.route_table(16, 2, 1, replicas=(9, 1))
+    assert r[9].tolist() == [-1, 1] and r[1].tolist() == [-1, 8 + 1] and r[0].tolist() == [0, 0]
+    ids = np.array([[1, 2], [9, 12]])
+    pos_of, sends = ep_model.plan(ids, np.ones((2, 2), np.float32), 16, 2, rank=1, replicas=(9, 1))
+    assert sends[0][0].tolist() == [0] and sends[1][0].tolist() == [0, 1]
+    assert sends[1][1].tolist() == [[9, ep_model.NO_SLOT], [1, 4]]
+
+
 def test_rank_that_never_joins_ends_the_exchange_with_an_error(tmp_path):
     t0 = time.time()
     res = run(tmp_path, dict(BASE, seed=10, n_tok=[3, 3], leave_rank=1, timeout=5.0))

@@ -77,3 +77,18 @@ def test_device_calls_twice_and_noalloc_refused(ranks):
             if x.shape[0]:
                 check(oracle.moe_ffn(layer, x)[0], y)
         assert int(res["noalloc_rc"]) == -5
+
+
+def test_replicated_experts_keep_outputs_and_counts(ranks):
+    import ep_gpu_worker
+    layer = ep_gpu_worker.make(ep_gpu_worker.REPLICATION_LAYER)
+    for res in ranks:
+        x = res["rep_x"]
+        want, wids, _ = oracle.moe_ffn(layer, x)
+        check(want, res["rep_y0"])
+        check(want, res["rep_y1"])
+        assert metrics.topk_sets(wids, res["rep_ids1"])["flips"] == 0
+        # counts are this rank's routed slots per global expert, before and after replication
+        assert res["rep_counts0"].sum() == x.shape[0] * layer["n_used"]
+        np.testing.assert_array_equal(res["rep_counts1"], np.bincount(wids.ravel(), minlength=32))
+        assert int(res["rep_dup_rc"]) == -1
