@@ -109,6 +109,7 @@ struct gx_context {
         uint32_t *recv_ids = nullptr;                   // [recv_rows][U]
         float *recv_w = nullptr;
         int *counts = nullptr;                          // device: send counts [world], recv counts [world]
+        std::vector<int> src_ntok;                      // tokens of every rank in the current call
         int *h_counts = nullptr;                        // pinned copy
         cudaEvent_t counts_ready = nullptr;
     } ep;
@@ -464,10 +465,14 @@ gx_result enqueue_layer_prefill(gx_context *c, const Layer &L, const void *x, ui
 }
 
 // ---- expert parallelism (world > 1) ------------------------------------------------------
-// Rank r serves experts [r*NE/W, (r+1)*NE/W). Per layer, every rank takes the same NCCL steps in
-// the same order, also with no tokens of its own: count exchange, dispatch of rotated token rows
-// (with their destination-local slots), the expert phase on what it received, and the return of
-// one weighted partial row per received row; the source adds the partial rows (+ residual).
+// Rank r serves experts [r*NE/W, (r+1)*NE/W) (and, after gx_replicate_experts, the replicated
+// experts for its own tokens). A forward call first exchanges every rank's token count (one host
+// round trip per call). Per layer, every rank then takes the same NCCL steps in the same order,
+// also with no tokens of its own: dispatch of n_tok rotated token rows (with their
+// destination-local slots; rows no slot of the destination needs carry none) to every rank, the
+// expert phase on what it received, and the return of one weighted partial row per received row;
+// the source adds the partial rows (+ residual). No step waits on the host, so the layers of a
+// stack queue back to back.
 
 gx_result comm_result(gx_context *c, ncclResult_t r, const char *what) {
     if (r == ncclSuccess) return GX_OK;
@@ -542,6 +547,35 @@ gx_result ensure_ep_recv(gx_context *c, size_t R) {
     return GX_OK;
 }
 
+// Exchanges every rank's token count for the call that follows (a collective; blocking).
+gx_result ep_sync_ntok(gx_context *c, uint32_t n_tok) {
+    auto &e = c->ep;
+    const int W = (int)c->world;
+    if (!e.counts) {
+        GX_CUDA(cudaMalloc(&e.counts, 2 * W * sizeof(int)));
+        GX_CUDA(cudaMallocHost(&e.h_counts, 2 * W * sizeof(int)));
+        GX_CUDA(cudaEventCreateWithFlags(&e.counts_ready, cudaEventDisableTiming));
+    }
+    e.h_counts[0] = (int)n_tok;
+    GX_CUDA(cudaMemcpyAsync(e.counts, e.h_counts, sizeof(int), cudaMemcpyHostToDevice, c->stream));
+    c->nccl->GroupStart();
+    for (int d = 0; d < W; ++d) {
+        c->nccl->Send(e.counts, 1, ncclInt32, d, c->comm, c->stream);
+        c->nccl->Recv(e.counts + W + d, 1, ncclInt32, d, c->comm, c->stream);
+    }
+    gx_result r = comm_group_end(c, "token-count exchange");
+    if (r != GX_OK) return r;
+    GX_CUDA(cudaMemcpyAsync(e.h_counts + W, e.counts + W, W * sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+    GX_CUDA(cudaEventRecord(e.counts_ready, c->stream));
+    r = wait_event(c, e.counts_ready, c->comm_timeout_ms);
+    if (r == GX_E_TIMEOUT) return comm_result(c, ncclInProgress, "token-count exchange");
+    if (r != GX_OK) return r;
+    e.src_ntok.assign(e.h_counts + W, e.h_counts + 2 * W);
+    for (int v : e.src_ntok)
+        if (v < 0 || (uint32_t)v > c->max_tokens) return comm_result(c, ncclInvalidUsage, "token-count exchange");
+    return GX_OK;
+}
+
 // One layer across the expert-parallel group. ev (GX_FLAG_PROFILE): start, after the dispatch
 // exchange (selection, rotation, plan, counts, rows), after the gate/up GEMM, end (down GEMM,
 // partial rows, return exchange, sum).
@@ -591,6 +625,7 @@ gx_result enqueue_layer_ep(gx_context *c, const Layer &L, const void *x, uint32_
     pa.route = L.route;
     pa.expert_count = L.expert_count;
     pa.stride = (int)stride;
+    pa.pad_rows = (int)n_tok;
     pa.pos_of = e.pos_of;
     pa.send_ids = e.send_ids;
     pa.send_w = e.send_w;
@@ -599,24 +634,12 @@ gx_result enqueue_layer_ep(gx_context *c, const Layer &L, const void *x, uint32_
     GX_CUDA(gx::launch_ep_plan(pa, c->stream));
     GX_CUDA(gx::launch_rotate_tokens(x, xb, norm_eps > 0.f ? c->xscale : nullptr, L.gate_signs, (int)n_tok, (int)E,
                                      e.send_rows, c->stream, e.pos_of, W));
-    // counts: rank d learns how many rows each source sends it
-    c->nccl->GroupStart();
-    for (int d = 0; d < W; ++d) {
-        c->nccl->Send(e.counts + d, 1, ncclInt32, d, c->comm, c->stream);
-        c->nccl->Recv(e.counts + W + d, 1, ncclInt32, d, c->comm, c->stream);
-    }
-    r = comm_group_end(c, "count exchange");
-    if (r != GX_OK) return r;
-    GX_CUDA(cudaMemcpyAsync(e.h_counts, e.counts, 2 * W * sizeof(int), cudaMemcpyDeviceToHost, c->stream));
-    GX_CUDA(cudaEventRecord(e.counts_ready, c->stream));
-    r = wait_event(c, e.counts_ready, c->comm_timeout_ms);
-    if (r == GX_E_TIMEOUT) return comm_result(c, ncclInProgress, "count exchange");
-    if (r != GX_OK) return r;
-    std::vector<size_t> scnt(W), rcnt(W), roff(W);
+    // every source sends its n_tok rows to every rank (rows without a slot there are empty)
+    if ((int)e.src_ntok.size() != W) return GX_E_STATE;
+    std::vector<size_t> scnt(W, n_tok), rcnt(W), roff(W);
     size_t R = 0;
     for (int d = 0; d < W; ++d) {
-        scnt[d] = (size_t)e.h_counts[d];
-        rcnt[d] = (size_t)e.h_counts[W + d];
+        rcnt[d] = (size_t)e.src_ntok[d];
         roff[d] = R;
         R += rcnt[d];
     }
@@ -1188,6 +1211,10 @@ GX_API gx_result gx_moe_forward(gx_context *c, uint32_t layer, const void *x, ui
     GX_CUDA(cudaSetDevice(c->device));
     const Layer &L = c->layers[layer];
     if (n_tok > 0 || c->world > 1) {  // with world > 1 every rank takes part in the exchange
+        if (c->world > 1) {
+            r = ep_sync_ntok(c, n_tok);
+            if (r != GX_OK) return r;
+        }
         const bool prof = (c->flags & GX_FLAG_PROFILE) != 0;
         if (prof) {
             c->prof_layers = 1;
@@ -1216,6 +1243,10 @@ GX_API gx_result gx_moe_forward_host(gx_context *c, uint32_t layer, const void *
     if (in_b) {
         std::memcpy(c->h_in, x, in_b);
         GX_CUDA(cudaMemcpyAsync(c->x_stage, c->h_in, in_b, cudaMemcpyHostToDevice, c->stream));
+    }
+    if (c->world > 1) {
+        r = ep_sync_ntok(c, n_tok);
+        if (r != GX_OK) return r;
     }
     const bool prof = (c->flags & GX_FLAG_PROFILE) != 0;
     if (prof) {
@@ -1264,7 +1295,9 @@ GX_API gx_result gx_stack_forward(gx_context *c, uint32_t first, uint32_t n_laye
         return record_ticket(c, out_ticket);
     }
     if (c->world > 1) {
-        // The exchange sizes are read back per layer, so the chain runs eagerly (no graph).
+        // One token-count exchange per call, then the layers queue without host round trips.
+        gx_result rs = ep_sync_ntok(c, n_tok);
+        if (rs != GX_OK) return rs;
         if (in_b) GX_CUDA(cudaMemcpyAsync(c->x_stage, x, in_b, cudaMemcpyDeviceToDevice, c->stream));
         gx_result r = stack_enqueue(c, first, n_layers, c->x_stage, x_dtype, n_tok, c->y_stage, y_dtype);
         if (r != GX_OK) return r;

@@ -32,7 +32,9 @@ __device__ __forceinline__ uint32_t local_expert(const EpPlanArgs &a, uint32_t e
 }
 
 // One CTA of 1024 threads per destination rank d: send rows for d are the tokens with a slot on
-// d, in token order (so each destination sees a stable order), at rows [d*stride, d*stride+count).
+// d, in token order (so each destination sees a stable order), at rows [d*stride, d*stride+count);
+// rows [count, pad_rows) are filled with empty slots, since a destination receives pad_rows rows
+// from every source without learning the count first.
 __global__ void __launch_bounds__(1024) ep_plan_kernel(EpPlanArgs a) {
     __shared__ int wsum[32];
     __shared__ int base, chunk;
@@ -89,6 +91,14 @@ __global__ void __launch_bounds__(1024) ep_plan_kernel(EpPlanArgs a) {
         __syncthreads();
     }
     if (tid == 0) a.send_count[d] = base;
+    // every destination receives pad_rows rows from this rank; the unused ones carry no slot
+    for (int r = base + tid; r < a.pad_rows; r += 1024) {
+        const size_t row = (size_t)d * a.stride + r;
+        for (int k = 0; k < a.U; ++k) {
+            a.send_ids[row * a.U + k] = kNoSlot;
+            a.send_w[row * a.U + k] = 0.f;
+        }
+    }
 }
 
 // out[t] = resid[t] + sum over destinations of the returned partial row of (t, d).

@@ -182,6 +182,7 @@ struct EpPlanArgs {
     const int2 *route;       // [NE] (serving rank or -1, local expert id there), or nullptr
     unsigned *expert_count;  // [NE] slots routed to each expert, accumulated, or nullptr
     int stride;              // send-buffer rows reserved per destination (>= n_tok)
+    int pad_rows;            // rows [count, pad_rows) of every destination are marked empty
     int *pos_of;             // [n_tok][W] send row of (token, destination), -1 if none
     uint32_t *send_ids;      // [W*stride][U] destination-local expert id or kNoSlot
     float *send_w;           // [W*stride][U] routing weight (0 for kNoSlot)
