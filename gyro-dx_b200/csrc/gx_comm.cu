@@ -38,16 +38,19 @@ const NcclApi *nccl_api() {
 }
 
 ncclResult_t nccl_settle(const NcclApi *api, ncclComm_t comm, uint32_t timeout_ms) {
+    // Enqueueing a group normally settles within microseconds, and the GPU waits for the next
+    // launch meanwhile: poll without sleeping for the first 2 ms, then back off.
     const auto start = std::chrono::steady_clock::now();
     for (;;) {
         ncclResult_t st = ncclSuccess;
         const ncclResult_t r = api->CommGetAsyncError(comm, &st);
         if (r != ncclSuccess) return r;
         if (st != ncclInProgress) return st;
-        const auto ms =
-            std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - start).count();
-        if ((uint64_t)ms >= timeout_ms) return ncclInProgress;
-        std::this_thread::sleep_for(std::chrono::microseconds(50));
+        const auto us =
+            std::chrono::duration_cast<std::chrono::microseconds>(std::chrono::steady_clock::now() - start).count();
+        if ((uint64_t)us >= (uint64_t)timeout_ms * 1000u) return ncclInProgress;
+        if (us < 2000) std::this_thread::yield();
+        else std::this_thread::sleep_for(std::chrono::microseconds(50));
     }
 }
 
