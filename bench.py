@@ -81,6 +81,12 @@ def peaks() -> dict:
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 
 
+def traffic_bytes(key: str):
+    """DRAM bytes per launch of a kernel from the committed ncu summary (profiles/traffic.json)."""
+    f = ROOT / "profiles" / "traffic.json"
+    return json.loads(f.read_text()).get(key) if f.exists() else None
+
+
 def make_layers(n_layers: int):
     from gyro_moe import synth
     for l in range(n_layers):
@@ -456,7 +462,8 @@ def run_prefill(args):
         "roofline": {
             "kernel": "moe_gemm_kernel<gate/up> (tcgen05 grouped GEMM, in-smem trellis decode, SwiGLU epilogue)",
             "bound": "tensor", "achieved": achieved, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
-            "frac": achieved / pk["bf16_tflops"], "traffic": None,
+            "frac": achieved / pk["bf16_tflops"], "traffic": traffic_bytes("moe_gemm_gateup_prefill_per_launch"),
+            "traffic_unit": "DRAM bytes per launch (ncu capture of this workload)",
             "algorithmic_flops_per_launch": gu_flops, "launch_us": gu_s * 1e6,
             "padded_flops_per_launch": tiles * 128 * 2 * F * E * 2,
             "peak_source": f"{pk['source']} (MEASURED_PEAKS.json bf16_tflops, burst; f16 has the same dense rate)",
