@@ -99,6 +99,13 @@ pub extern fn gx_upload_matrix(context: *gx_context, type_id: u32, rows: u32, co
 pub extern fn gx_matvec(context: *gx_context, handle: u32, x: [*]const f32, n_tok: u32, y: [*]f32,
     ticket: ?*u64) gx_result;
 pub extern fn gx_read_timings(context: *gx_context, timings: *gx_timings) gx_result;
+pub extern fn gx_comm_unique_id(out_id: [*]u8, bytes: u64) gx_result;
+pub extern fn gx_read_expert_counts(context: *gx_context, layer: u32, counts: [*]u32, reset: u32,
+    timeout_ms: u32) gx_result;
+pub extern fn gx_replicate_experts(context: *gx_context, layer: u32, experts: ?[*]const u32, n: u32,
+    timeout_ms: u32) gx_result;
+pub extern fn gx_moe_forward_noalloc(context: *gx_context, layer: u32, x: ?*const anyopaque, x_dtype: u32,
+    n_tok: u32, y: ?*anyopaque, y_dtype: u32, ids: ?[*]u32, weights: ?[*]f32, ticket: ?*u64) gx_result;
 pub extern fn gx_set_flags(context: *gx_context, flags: u32) gx_result;
 pub extern fn gx_destroy(context: *gx_context, timeout_ms: u32) gx_result;
 
