@@ -574,6 +574,7 @@ def run_ep(args):
             ticket = ctx.stack_forward(0, args.layers, xs[i % 2], y)
         ctx.wait(ticket)
     torch.cuda.synchronize(dev)
+    exchange = ctx.caps().ep_exchange
     stream = torch.cuda.ExternalStream(ctx.stream(), device=dev)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if dist:
@@ -624,7 +625,10 @@ def run_ep(args):
     if dist:
         dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
     e2e_s = float(e2e_t.item())
-    launches_per_layer = 11 if world > 1 else 9
+    # router, top-k, rotation (push with peer memory), three grouping kernels, two packs, two
+    # GEMMs, combine (return with peer memory); expert parallel adds the plan and the sum of
+    # partial rows, and with peer memory the two bounded waits
+    launches_per_layer = 11 if world == 1 else 15 if exchange == abi.GX_EP_PEER else 13
     line = {
         "metric": METRIC, "value": K * T / (ms / 1e3), "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
         "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
@@ -633,7 +637,9 @@ def run_ep(args):
                                f"{T} tokens) through the {args.layers}-layer stack of the config-0 layer, Zipf(1.1)",
                    "tokens": T, "sequences": EP_SEQS, "layers": args.layers, "hidden": E, "experts": NE,
                    "experts_per_gpu": per, "top_k": U, "ffn": F, "type": "TQ2_T",
-                   "parallelism": f"expert parallel x{world} (NCCL dispatch/combine)" if world > 1 else "single GPU",
+                   "parallelism": (f"expert parallel x{world} (dispatch/combine over "
+                                   f"{'NVLink peer memory' if exchange == abi.GX_EP_PEER else 'NCCL'})")
+                                  if world > 1 else "single GPU",
                    "replicated_experts_per_layer": (sum(replicas) / len(replicas)) if replicas else 0,
                    "tokens_per_rank_max": max_tok,
                    "l2": "inputs larger than L2: a step reads every touched expert of 40 layers"},

@@ -110,6 +110,13 @@ struct gx_context {
         float *recv_w = nullptr;
         int *counts = nullptr;                          // device: send counts [world], recv counts [world]
         std::vector<int> src_ntok;                      // tokens of every rank in the current call
+        // exchange over NVLink peer memory (state 0: not set up, 1: in use, -1: NCCL rows instead)
+        int peer_state = 0;
+        int T = 0, pE = 0, pU = 0;
+        uint8_t *block = nullptr;                       // this rank's exchange block
+        uint8_t *peers[gx::kMaxPeers] = {};             // every rank's block, mapped here
+        gx::EpBlock off{};
+        unsigned epoch = 0;
         int *h_counts = nullptr;                        // pinned copy
         cudaEvent_t counts_ready = nullptr;
     } ep;
@@ -268,6 +275,9 @@ void release_all(gx_context *c) {
     for (void *p : dev) if (p) cudaFree(p);
     if (c->h_in) cudaFreeHost(c->h_in);
     if (c->h_out) cudaFreeHost(c->h_out);
+    for (uint32_t r = 0; r < c->world && r < (uint32_t)gx::kMaxPeers; ++r)
+        if (c->ep.peers[r] && r != c->rank) cudaIpcCloseMemHandle(c->ep.peers[r]);
+    if (c->ep.block) cudaFree(c->ep.block);
     void *ep[] = {c->ep.pos_of, c->ep.send_ids, c->ep.send_w, c->ep.send_rows, c->ep.ret_rows, c->ep.recv_rows,
                   c->ep.part_rows, c->ep.recv_ids, c->ep.recv_w, c->ep.counts};
     for (void *p : ep) if (p) cudaFree(p);
@@ -576,6 +586,233 @@ gx_result ep_sync_ntok(gx_context *c, uint32_t n_tok) {
     return GX_OK;
 }
 
+// Exchanges `bytes` of this rank's device buffer src with every rank into dst[W][bytes] (a
+// collective; blocking).
+gx_result ep_allgather(gx_context *c, const void *src, void *dst, size_t bytes, const char *what) {
+    c->nccl->GroupStart();
+    for (int d = 0; d < (int)c->world; ++d) {
+        c->nccl->Send(src, bytes, ncclUint8, d, c->comm, c->stream);
+        c->nccl->Recv(static_cast<uint8_t *>(dst) + (size_t)d * bytes, bytes, ncclUint8, d, c->comm, c->stream);
+    }
+    gx_result r = comm_group_end(c, what);
+    if (r != GX_OK) return r;
+    GX_CUDA(cudaEventRecord(c->ep.counts_ready, c->stream));
+    r = wait_event(c, c->ep.counts_ready, c->comm_timeout_ms);
+    return r == GX_E_TIMEOUT ? comm_result(c, ncclInProgress, what) : r;
+}
+
+// Sets up the exchange over peer memory (a collective, on the first expert-parallel layer): every
+// rank allocates its block for T = max_tokens rows per source and the largest E and U uploaded,
+// shares it by CUDA IPC, and maps every other rank's block. Every rank takes the peer path only
+// if every rank could map every block and all agree on T, E, U; otherwise all keep the NCCL rows
+// (GX_EP_NCCL=1 asks for those).
+gx_result ep_peer_setup(gx_context *c) {
+    auto &e = c->ep;
+    const int W = (int)c->world;
+    int E = 0, U = 0;
+    for (const Layer &L : c->layers)
+        if (L.ready) {
+            E = std::max<int>(E, (int)L.E);
+            U = std::max<int>(U, (int)L.U);
+        }
+    const char *force = std::getenv("GX_EP_NCCL");
+    int ok = W <= gx::kMaxPeers && !(force && force[0] == '1') ? 1 : 0;
+    cudaIpcMemHandle_t handle{};
+    if (ok) {
+        e.off = gx::ep_block_layout(W, (int)c->max_tokens, E, U);
+        if (cudaMalloc(&e.block, e.off.bytes) != cudaSuccess ||
+            cudaMemset(e.block, 0, e.off.bytes) != cudaSuccess ||
+            cudaIpcGetMemHandle(&handle, e.block) != cudaSuccess) {
+            cudaGetLastError();
+            ok = 0;
+        }
+    }
+    // record: ok, T, E, U, handle
+    // ranks whose waits depend on each other must be on different GPUs (device UUIDs compared)
+    cudaDeviceProp prop{};
+    if (cudaGetDeviceProperties(&prop, c->device) != cudaSuccess) {
+        cudaGetLastError();
+        ok = 0;
+    }
+    struct Rec {
+        int ok, T, E, U;
+        cudaIpcMemHandle_t h;
+        char uuid[16];
+    } mine{ok, (int)c->max_tokens, E, U, handle, {}};
+    std::memcpy(mine.uuid, prop.uuid.bytes, 16);
+    std::vector<Rec> all(W);
+    uint8_t *dev = nullptr;
+    GX_CUDA(cudaMalloc(&dev, sizeof(Rec) * (W + 1)));
+    gx_result r = GX_OK;
+    do {
+        if (cudaMemcpy(dev, &mine, sizeof(Rec), cudaMemcpyHostToDevice) != cudaSuccess) { r = GX_E_DEVICE; break; }
+        r = ep_allgather(c, dev, dev + sizeof(Rec), sizeof(Rec), "exchange setup");
+        if (r != GX_OK) break;
+        if (cudaMemcpy(all.data(), dev + sizeof(Rec), sizeof(Rec) * W, cudaMemcpyDeviceToHost) != cudaSuccess) {
+            r = GX_E_DEVICE;
+            break;
+        }
+        for (const Rec &x : all) ok = ok && x.ok && x.T == mine.T && x.E == E && x.U == U;
+        for (int p = 0; p < W; ++p)
+            for (int q = p + 1; q < W; ++q)
+                if (std::memcmp(all[p].uuid, all[q].uuid, 16) == 0) ok = 0;
+        for (int p = 0; ok && p < W; ++p) {
+            if (p == (int)c->rank) { e.peers[p] = e.block; continue; }
+            void *m = nullptr;
+            if (cudaIpcOpenMemHandle(&m, all[p].h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+                cudaGetLastError();
+                ok = 0;
+            } else {
+                e.peers[p] = static_cast<uint8_t *>(m);
+            }
+        }
+        // all ranks agree on the outcome
+        int flag = ok;
+        if (cudaMemcpy(dev, &flag, sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess) { r = GX_E_DEVICE; break; }
+        r = ep_allgather(c, dev, dev + sizeof(Rec), sizeof(int), "exchange setup");
+        if (r != GX_OK) break;
+        std::vector<int> flags(W);
+        if (cudaMemcpy(flags.data(), dev + sizeof(Rec), sizeof(int) * W, cudaMemcpyDeviceToHost) != cudaSuccess) {
+            r = GX_E_DEVICE;
+            break;
+        }
+        for (int f : flags) ok = ok && f;
+    } while (false);
+    cudaFree(dev);
+    if (r != GX_OK) return r;
+    if (!ok) {
+        for (int p = 0; p < W; ++p)
+            if (e.peers[p] && p != (int)c->rank) cudaIpcCloseMemHandle(e.peers[p]);
+        for (auto &p : e.peers) p = nullptr;
+        if (e.block) cudaFree(e.block);
+        e.block = nullptr;
+        e.peer_state = -1;
+        return GX_OK;
+    }
+    e.T = (int)c->max_tokens;
+    e.pE = E;
+    e.pU = U;
+    e.peer_state = 1;
+    return GX_OK;
+}
+
+// The layer's exchange over peer memory, after selection and the plan (stride T): push the rows,
+// wait for every source's rows, the expert phase on the rx region ([W][T] rows, empty ones carry
+// no slot), partial rows straight into the sources' ret regions, wait for every destination,
+// and the source sum.
+gx_result enqueue_layer_ep_peer(gx_context *c, const Layer &L, const void *x, int xb, uint32_t n_tok,
+                                const void *resid, uint32_t resid_dtype, void *out, uint32_t out_dtype, float norm_eps,
+                                cudaEvent_t *ev) {
+    auto &e = c->ep;
+    const int W = (int)c->world;
+    const size_t E = L.E, U = L.U, T = (size_t)e.T;
+    gx::EpPeerArgs pa{};
+    for (int p = 0; p < W; ++p) pa.peer[p] = e.peers[p];
+    pa.off = e.off;
+    pa.W = W;
+    pa.rank = (int)c->rank;
+    pa.T = e.T;
+    pa.E = (int)E;
+    pa.U = (int)U;
+    pa.epoch = ++e.epoch;
+    pa.err = c->err;
+    // the blocks are laid out for the largest E and U; a smaller layer uses the same offsets
+    gx::EpPushArgs ps{};
+    ps.p = pa;
+    ps.x = x;
+    ps.x_bf16 = xb;
+    ps.n_tok = (int)n_tok;
+    ps.xscale = norm_eps > 0.f ? c->xscale : nullptr;
+    ps.signs = L.gate_signs;
+    ps.pos_of = e.pos_of;
+    ps.send_ids = e.send_ids;
+    ps.send_w = e.send_w;
+    ps.send_count = e.counts;
+    GX_CUDA(gx::launch_ep_push(ps, c->stream));
+    GX_CUDA(gx::launch_ep_wait_rx(pa, c->stream));
+    if (ev) GX_CUDA(record_phase(ev[1], c->stream));
+    const size_t rows = (size_t)W * T;
+    gx_result r = ensure_prefill(c, L, rows * U);
+    if (r != GX_OK) return r;
+    auto &p = c->pf;
+    gx::GroupArgs ga{};
+    ga.ids = reinterpret_cast<const uint32_t *>(e.block + e.off.rx_ids);
+    ga.n_slots = (int)(rows * U);
+    ga.NE = (int)(L.local_experts + L.replica_slots);
+    ga.expert_count = p.expert_count;
+    ga.cursor = p.cursor;
+    ga.tile_expert = p.tile_expert;
+    ga.tile_rows = p.tile_rows;
+    ga.n_mtiles = p.n_mtiles;
+    ga.row_slot = p.row_slot;
+    ga.slot_row = p.slot_row;
+    ga.err = c->err;
+    GX_CUDA(gx::launch_group(ga, c->stream));
+    gx::PackArgs pk{};
+    pk.by_token = 1;
+    pk.U = (int)U;
+    pk.K = (int)E;
+    pk.xh = reinterpret_cast<const __half *>(e.block + e.off.rx_rows);
+    pk.row_slot = p.row_slot;
+    pk.tile_rows = p.tile_rows;
+    pk.n_mtiles = p.n_mtiles;
+    pk.dst = p.A;
+    GX_CUDA(gx::launch_pack_rows(pk, (int)p.max_tiles, c->stream));
+    gx::GemmArgs gm{};
+    gm.type = L.type;
+    gm.w0 = L.gate;
+    gm.w1 = L.up;
+    gm.expert_bytes = L.gate_expert_bytes;
+    gm.K = (int)L.E;
+    gm.n_ntiles = (int)(L.F / 128);
+    gm.n_expert = (int)(L.local_experts + L.replica_slots);
+    gm.A = p.A;
+    gm.tile_expert = p.tile_expert;
+    gm.tile_rows = p.tile_rows;
+    gm.n_mtiles = p.n_mtiles;
+    gm.act = p.act;
+    gm.F = (int)L.F;
+    gm.Y = p.Y;
+    gm.E = (int)L.E;
+    gm.codebook = c->codebook;
+    gm.err = c->err;
+    GX_CUDA(gx::launch_moe_gemm(gm, 0, c->sm_count, c->stream));
+    if (ev) GX_CUDA(record_phase(ev[2], c->stream));
+    gx::PackArgs pd{};
+    pd.src = p.act;
+    pd.by_token = 0;
+    pd.U = (int)U;
+    pd.K = (int)L.F;
+    pd.signs = L.down_signs;
+    pd.row_slot = p.row_slot;
+    pd.tile_rows = p.tile_rows;
+    pd.n_mtiles = p.n_mtiles;
+    pd.dst = p.A2;
+    GX_CUDA(gx::launch_pack_rows(pd, (int)p.max_tiles, c->stream));
+    gm.w0 = L.down;
+    gm.w1 = nullptr;
+    gm.expert_bytes = L.down_expert_bytes;
+    gm.K = (int)L.F;
+    gm.n_ntiles = (int)(L.E / 256);
+    gm.A = p.A2;
+    GX_CUDA(gx::launch_moe_gemm(gm, 1, c->sm_count, c->stream));
+    GX_CUDA(gx::launch_ep_return(pa, p.Y, p.slot_row, c->stream));
+    GX_CUDA(gx::launch_ep_wait_ret(pa, c->stream));
+    gx::EpCombineArgs ec{};
+    ec.ret = reinterpret_cast<const __half *>(e.block + e.off.ret_rows);
+    ec.pos_of = e.pos_of;
+    ec.W = W;
+    ec.resid = resid;
+    ec.resid_bf16 = resid_dtype == GX_BF16;
+    ec.out = out;
+    ec.out_bf16 = out_dtype == GX_BF16;
+    ec.n_tok = (int)n_tok;
+    ec.E = (int)E;
+    GX_CUDA(gx::launch_ep_combine(ec, c->stream));
+    if (ev) GX_CUDA(record_phase(ev[3], c->stream));
+    return GX_OK;
+}
+
 // One layer across the expert-parallel group. ev (GX_FLAG_PROFILE): start, after the dispatch
 // exchange (selection, rotation, plan, counts, rows), after the gate/up GEMM, end (down GEMM,
 // partial rows, return exchange, sum).
@@ -587,8 +824,14 @@ gx_result enqueue_layer_ep(gx_context *c, const Layer &L, const void *x, uint32_
     gx_result r = ensure_ep_send(c, L);
     if (r != GX_OK) return r;
     auto &e = c->ep;
+    if (e.peer_state == 0) {
+        r = ep_peer_setup(c);
+        if (r != GX_OK) return r;
+    }
+    const bool peer = e.peer_state == 1 && (int)L.E <= e.pE && (int)L.U <= e.pU;
     const int xb = x_dtype == GX_BF16;
-    const size_t stride = n_tok ? n_tok : 1;  // send rows reserved per destination
+    // send rows reserved per destination: the peer regions hold T rows per source
+    const size_t stride = peer ? (size_t)e.T : (n_tok ? n_tok : 1);
     if (ev) GX_CUDA(record_phase(ev[0], c->stream));
     if (n_tok > 0) {
         int splits;
@@ -625,13 +868,14 @@ gx_result enqueue_layer_ep(gx_context *c, const Layer &L, const void *x, uint32_
     pa.route = L.route;
     pa.expert_count = L.expert_count;
     pa.stride = (int)stride;
-    pa.pad_rows = (int)n_tok;
+    pa.pad_rows = peer ? 0 : (int)n_tok;
     pa.pos_of = e.pos_of;
     pa.send_ids = e.send_ids;
     pa.send_w = e.send_w;
     pa.send_count = e.counts;
     pa.err = c->err;
     GX_CUDA(gx::launch_ep_plan(pa, c->stream));
+    if (peer) return enqueue_layer_ep_peer(c, L, x, xb, n_tok, resid, resid_dtype, out, out_dtype, norm_eps, ev);
     GX_CUDA(gx::launch_rotate_tokens(x, xb, norm_eps > 0.f ? c->xscale : nullptr, L.gate_signs, (int)n_tok, (int)E,
                                      e.send_rows, c->stream, e.pos_of, W));
     // every source sends its n_tok rows to every rank (rows without a slot there are empty)
@@ -1053,6 +1297,7 @@ GX_API gx_result gx_get_caps(gx_context *c, gx_caps *caps) {
     for (auto &l : c->layers) caps->arena_bytes += l.bytes;
     for (auto &m : c->mats) caps->arena_bytes += (uint64_t)m.rows / 8 * (m.cols / 128) * gx::tile_bytes(m.type);
     std::strncpy(caps->device_name, prop.name, sizeof(caps->device_name) - 1);
+    caps->ep_exchange = c->ep.peer_state == 1 ? GX_EP_PEER : c->ep.peer_state == -1 ? GX_EP_NCCL : GX_EP_NONE;
     return GX_OK;
 }
 

@@ -8,6 +8,8 @@
 // adds the partial rows of all destinations. This is the scatter / gather around the expert
 // phase of src/engine.zig:547-641; the grouping, GEMMs and per-row combine are the same kernels as
 // the single-GPU many-token path.
+#include <algorithm>
+
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -143,4 +145,243 @@ cudaError_t launch_ep_combine(const EpCombineArgs &a, cudaStream_t s) {
     return cudaGetLastError();
 }
 
+// ---- exchange over NVLink peer memory -------------------------------------------------------
+// A source writes only the rows a destination needs, straight into the destination's memory
+// (plain stores through the IPC mapping; no TMA and no multicast), and publishes them with a
+// release store of the epoch into the destination's flag word after a system-scope fence. The
+// destination acquires the flag before it reads. Every wait is bounded by kWaitLimitNs.
+
+namespace {
+
+__device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Bounded wait until *flag >= epoch; false (and KERR_WAIT) when the limit passes.
+__device__ bool wait_flag(const unsigned *flag, unsigned epoch, int *err) {
+    const uint64_t t0 = globaltimer_ns();
+    while (ld_acquire_sys(flag) < epoch) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            atomicExch(err, KERR_WAIT);
+            return false;
+        }
+        __nanosleep(64);
+    }
+    return true;
+}
+
+// The CTA that finishes last (every thread's writes fenced at system scope first) returns true.
+__device__ bool last_cta(unsigned *done) {
+    __threadfence_system();
+    __syncthreads();
+    __shared__ bool is_last;
+    if (threadIdx.x == 0) is_last = atomicAdd(done, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (is_last && threadIdx.x == 0) {
+        __threadfence();
+        *done = 0;  // every CTA has counted: ready for the next transfer
+    }
+    return is_last;
+}
+
+__global__ void __launch_bounds__(256) ep_push_kernel(EpPushArgs a, int row_ctas) {
+    const EpPeerArgs &p = a.p;
+    const int lane = threadIdx.x & 31;
+    if ((int)blockIdx.x < row_ctas) {
+        // rows: one warp per (token, 4 column blocks) in a grid-stride loop, rotation as
+        // rotate_tokens_kernel
+        const int nb = p.E / 128, groups = (nb + 3) / 4;
+        const long long n_w = (long long)a.n_tok * groups, step = (long long)row_ctas * 8;
+        for (long long w = (long long)blockIdx.x * 8 + (threadIdx.x >> 5); w < n_w; w += step) {
+            const int t = (int)(w / groups), b0 = (int)(w % groups) * 4;
+            const float sc = a.xscale ? a.xscale[t] : 1.f;
+            float v[4][4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int b = b0 + q;
+                if (b >= nb) break;
+                const size_t base = (size_t)t * p.E + b * 128 + 4 * lane;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) v[q][j] = load_act(a.x, a.x_bf16, base + j) * sc;
+                if (a.signs) {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) v[q][j] *= a.signs[b * 128 + 4 * lane + j];
+                }
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int b = b0 + q;
+                if (b >= nb) break;
+                if (a.signs) fwht128_warp(v[q], lane);
+                uint2 o;
+                o.x = pack_half2(v[q][0], v[q][1]);
+                o.y = pack_half2(v[q][2], v[q][3]);
+                for (int d = 0; d < p.W; ++d) {
+                    const int row = a.pos_of[(size_t)t * p.W + d];
+                    if (row < 0) continue;
+                    const size_t pos = (size_t)(row - d * p.T);
+                    __half *dst = reinterpret_cast<__half *>(p.peer[d] + p.off.rx_rows) +
+                                  ((size_t)p.rank * p.T + pos) * p.E + b * 128 + 4 * lane;
+                    *reinterpret_cast<uint2 *>(dst) = o;
+                }
+            }
+        }
+    } else {
+        // slot metadata: thread per (destination, position) of the used rows, grid-stride
+        const long long n_r = a.n_tok > 0 ? (long long)p.W * a.n_tok : 0;
+        const long long step = (long long)(gridDim.x - row_ctas) * 256;
+        for (long long r = (long long)(blockIdx.x - row_ctas) * 256 + threadIdx.x; r < n_r; r += step) {
+            const int d = (int)(r / a.n_tok), pos = (int)(r % a.n_tok);
+            if (pos < a.send_count[d]) {
+                const size_t src = ((size_t)d * p.T + pos) * p.U;
+                const size_t dst = ((size_t)p.rank * p.T + pos) * p.U;
+                uint32_t *ids = reinterpret_cast<uint32_t *>(p.peer[d] + p.off.rx_ids);
+                float *wts = reinterpret_cast<float *>(p.peer[d] + p.off.rx_w);
+                for (int k = 0; k < p.U; ++k) {
+                    ids[dst + k] = a.send_ids[src + k];
+                    wts[dst + k] = a.send_w[src + k];
+                }
+            }
+        }
+    }
+    unsigned *done = reinterpret_cast<unsigned *>(p.peer[p.rank] + p.off.done);
+    if (last_cta(done) && threadIdx.x < (unsigned)p.W) {
+        const int d = threadIdx.x;
+        *reinterpret_cast<volatile int *>(p.peer[d] + p.off.rx_count + 4 * p.rank) = a.send_count[d];
+        __threadfence_system();
+        st_release_sys(reinterpret_cast<unsigned *>(p.peer[d] + p.off.rx_flag) + p.rank, p.epoch);
+    }
+}
+
+__global__ void __launch_bounds__(1024) ep_wait_rx_kernel(EpPeerArgs a) {
+    __shared__ int cnt[kMaxPeers];
+    uint8_t *own = a.peer[a.rank];
+    if (threadIdx.x < (unsigned)a.W) {
+        const int s = threadIdx.x;
+        const bool ok = wait_flag(reinterpret_cast<const unsigned *>(own + a.off.rx_flag) + s, a.epoch, a.err);
+        const int c = *reinterpret_cast<volatile const int *>(own + a.off.rx_count + 4 * s);
+        cnt[s] = ok ? min(max(c, 0), a.T) : 0;
+    }
+    __syncthreads();
+    uint32_t *ids = reinterpret_cast<uint32_t *>(own + a.off.rx_ids);
+    const long long n = (long long)a.W * a.T * a.U;
+    for (long long i = threadIdx.x; i < n; i += blockDim.x) {
+        const int s = (int)(i / ((long long)a.T * a.U)), row = (int)((i / a.U) % a.T);
+        if (row >= cnt[s]) ids[i] = kNoSlot;
+    }
+}
+
+// One warp per received row (grid-stride): the row's U slots are read once (lane k holds slot k)
+// and every lane sums 8 columns at a time into one 16-byte store to the source's ret region.
+__global__ void __launch_bounds__(256) ep_return_kernel(EpPeerArgs a, const __half *Y, const int *slot_row) {
+    const int lane = threadIdx.x & 31;
+    uint8_t *own = a.peer[a.rank];
+    const int *cnt = reinterpret_cast<const int *>(own + a.off.rx_count);
+    const float *rw = reinterpret_cast<const float *>(own + a.off.rx_w);
+    const long long n_r = (long long)a.W * a.T, step = (long long)gridDim.x * 8;
+    for (long long r = (long long)blockIdx.x * 8 + (threadIdx.x >> 5); r < n_r; r += step) {
+        const int s = (int)(r / a.T), pos = (int)(r % a.T);
+        if (pos >= min(cnt[s], a.T)) continue;  // the same for the whole warp
+        int row_k = -1;
+        float w_k = 0.f;
+        if (lane < a.U) {
+            row_k = slot_row[(size_t)r * a.U + lane];
+            w_k = rw[(size_t)r * a.U + lane];
+        }
+        __half *dst = reinterpret_cast<__half *>(a.peer[s] + a.off.ret_rows) + ((size_t)a.rank * a.T + pos) * a.E;
+        for (int c = lane * 8; c < a.E; c += 256) {
+            float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            for (int k = 0; k < a.U; ++k) {
+                const int row = __shfl_sync(0xffffffffu, row_k, k);
+                const float wk = __shfl_sync(0xffffffffu, w_k, k);
+                if (row < 0) continue;
+                const uint4 q = *reinterpret_cast<const uint4 *>(Y + (size_t)row * a.E + c);
+                const __half2 *h = reinterpret_cast<const __half2 *>(&q);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float2 f = __half22float2(h[j]);
+                    v[2 * j] += wk * f.x;
+                    v[2 * j + 1] += wk * f.y;
+                }
+            }
+            uint4 o;
+            o.x = pack_half2(v[0], v[1]);
+            o.y = pack_half2(v[2], v[3]);
+            o.z = pack_half2(v[4], v[5]);
+            o.w = pack_half2(v[6], v[7]);
+            *reinterpret_cast<uint4 *>(dst + c) = o;
+        }
+    }
+    unsigned *done = reinterpret_cast<unsigned *>(own + a.off.done) + 1;
+    if (last_cta(done) && threadIdx.x < (unsigned)a.W) {
+        __threadfence_system();
+        st_release_sys(reinterpret_cast<unsigned *>(a.peer[threadIdx.x] + a.off.ret_flag) + a.rank, a.epoch);
+    }
+}
+
+__global__ void ep_wait_ret_kernel(EpPeerArgs a) {
+    if (threadIdx.x < (unsigned)a.W)
+        wait_flag(reinterpret_cast<const unsigned *>(a.peer[a.rank] + a.off.ret_flag) + threadIdx.x, a.epoch, a.err);
+}
+
+size_t align_up(size_t v) { return (v + 255) & ~(size_t)255; }
+
+// grid bounds of the exchange kernels (CTAs of 256 threads; a few per SM of 148)
+constexpr long long kPushRowCtas = 148 * 6, kPushMetaCtas = 148, kReturnCtas = 148 * 6;
+
+}  // namespace
+
+EpBlock ep_block_layout(int W, int T, int E, int U) {
+    EpBlock b{};
+    size_t off = 0;
+    b.rx_rows = off; off = align_up(off + (size_t)W * T * E * 2);
+    b.rx_ids = off; off = align_up(off + (size_t)W * T * U * 4);
+    b.rx_w = off; off = align_up(off + (size_t)W * T * U * 4);
+    b.ret_rows = off; off = align_up(off + (size_t)W * T * E * 2);
+    b.rx_count = off; off = align_up(off + (size_t)W * 4);
+    b.rx_flag = off; off = align_up(off + (size_t)W * 4);
+    b.ret_flag = off; off = align_up(off + (size_t)W * 4);
+    b.done = off; off = align_up(off + 8);
+    b.bytes = off;
+    return b;
+}
+
+cudaError_t launch_ep_push(const EpPushArgs &a, cudaStream_t s) {
+    if (a.p.W > kMaxPeers || a.p.W > 256) return cudaErrorInvalidValue;
+    // grid-stride kernels: a bounded grid keeps the completion count (one atomic per CTA) small
+    const long long warps = (long long)a.n_tok * ((a.p.E / 128 + 3) / 4);
+    const int row_ctas = (int)std::min<long long>((warps + 7) / 8, kPushRowCtas);
+    const int meta_ctas = (int)std::min<long long>(((long long)a.p.W * a.n_tok + 255) / 256, kPushMetaCtas);
+    const int grid = row_ctas + meta_ctas > 0 ? row_ctas + meta_ctas : 1;
+    ep_push_kernel<<<grid, 256, 0, s>>>(a, row_ctas);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ep_wait_rx(const EpPeerArgs &a, cudaStream_t s) {
+    if (a.W > kMaxPeers) return cudaErrorInvalidValue;
+    ep_wait_rx_kernel<<<1, 1024, 0, s>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ep_return(const EpPeerArgs &a, const __half *Y, const int *slot_row, cudaStream_t s) {
+    if (a.W > kMaxPeers || a.W > 256) return cudaErrorInvalidValue;
+    if (a.E % 8 || a.U > 32) return cudaErrorInvalidValue;
+    const long long warps = (long long)a.W * a.T;
+    const unsigned grid = (unsigned)std::max<long long>(1, std::min<long long>((warps + 7) / 8, kReturnCtas));
+    ep_return_kernel<<<grid, 256, 0, s>>>(a, Y, slot_row);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ep_wait_ret(const EpPeerArgs &a, cudaStream_t s) {
+    if (a.W > kMaxPeers) return cudaErrorInvalidValue;
+    ep_wait_ret_kernel<<<1, 32, 0, s>>>(a);
+    return cudaGetLastError();
+}
+
 }  // namespace gx
+

@@ -201,7 +201,52 @@ struct EpCombineArgs {
     int n_tok, E;
 };
 
+// ---- expert-parallel exchange over NVLink peer memory -------------------------------------
+// Every rank owns one exchange block, mapped into every other rank by CUDA IPC, laid out alike
+// on all ranks for W ranks, T rows per source and E, U of the largest layer:
+//   rx_rows [W src][T][E] f16 | rx_ids [W][T][U] | rx_w [W][T][U] | ret_rows [W dst][T][E] f16 |
+//   rx_count [W] | rx_flag [W] | ret_flag [W] | done [2]
+// A flag holds the epoch (layer call number) of the last completed transfer from that rank.
+constexpr int kMaxPeers = 16;
+
+struct EpBlock {
+    size_t rx_rows, rx_ids, rx_w, ret_rows, rx_count, rx_flag, ret_flag, done, bytes;
+};
+EpBlock ep_block_layout(int W, int T, int E, int U);
+
+struct EpPeerArgs {
+    uint8_t *peer[kMaxPeers];  // every rank's exchange block in this process's address space
+    EpBlock off;
+    int W, rank, T, E, U;
+    unsigned epoch;
+    int *err;
+};
+
+// Rotated f16 rows of this rank's tokens straight into the destinations' rx regions (row
+// positions from the plan, stride T), the slot metadata beside them, then count + flag per
+// destination from the last CTA.
+struct EpPushArgs {
+    EpPeerArgs p;
+    const void *x;
+    int x_bf16, n_tok;
+    const float *xscale;     // [n_tok] or nullptr
+    const float *signs;      // [E] or nullptr
+    const int *pos_of;       // [n_tok][W] = d * T + position, or -1
+    const uint32_t *send_ids;
+    const float *send_w;     // [W * T][U] plan output
+    const int *send_count;   // [W]
+};
+
 cudaError_t launch_ep_plan(const EpPlanArgs &a, cudaStream_t s);
+cudaError_t launch_ep_push(const EpPushArgs &a, cudaStream_t s);
+// Waits (bounded) for every source's flag of this epoch, then marks rx rows past each source's
+// count as carrying no slot.
+cudaError_t launch_ep_wait_rx(const EpPeerArgs &a, cudaStream_t s);
+// Weighted sum of the U expert rows of every received row (Y, slot_row as the combine kernel)
+// written as f16 into the source's ret region, then a flag per source from the last CTA.
+cudaError_t launch_ep_return(const EpPeerArgs &a, const __half *Y, const int *slot_row, cudaStream_t s);
+// Waits (bounded) for every destination's return flag of this epoch.
+cudaError_t launch_ep_wait_ret(const EpPeerArgs &a, cudaStream_t s);
 cudaError_t launch_ep_combine(const EpCombineArgs &a, cudaStream_t s);
 cudaError_t launch_group(const GroupArgs &a, cudaStream_t s);
 cudaError_t launch_pack_rows(const PackArgs &a, int max_tiles, cudaStream_t s);

@@ -20,6 +20,7 @@ ERRORS = {-1: "GX_E_INVALIDARG", -2: "GX_E_OUTOFMEMORY", -3: "GX_E_TIMEOUT", -4:
           -5: "GX_E_UNSUPPORTED", -6: "GX_E_STATE", -7: "GX_E_MISMATCH", -8: "GX_E_COMM", -9: "GX_E_KERNEL"}
 GX_F32, GX_BF16 = 0, 30
 GX_FLAG_PROFILE = 1
+GX_EP_NONE, GX_EP_NCCL, GX_EP_PEER = 0, 1, 2     # gx_caps.ep_exchange
 
 
 class GxError(RuntimeError):
@@ -40,7 +41,7 @@ class Caps(ctypes.Structure):
                 ("cc_minor", ctypes.c_uint32), ("rank", ctypes.c_uint32), ("world", ctypes.c_uint32),
                 ("max_tokens", ctypes.c_uint32), ("max_layers", ctypes.c_uint32), ("hbm_bytes", ctypes.c_uint64),
                 ("free_bytes", ctypes.c_uint64), ("l2_bytes", ctypes.c_uint64), ("arena_bytes", ctypes.c_uint64),
-                ("device_name", ctypes.c_char * 128)]
+                ("device_name", ctypes.c_char * 120), ("ep_exchange", ctypes.c_uint32), ("reserved", ctypes.c_uint32)]
 
 
 class LayerDesc(ctypes.Structure):

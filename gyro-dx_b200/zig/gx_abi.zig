@@ -20,6 +20,9 @@ pub const e_kernel: gx_result = -9;
 pub const dtype_f32: u32 = 0;
 pub const dtype_bf16: u32 = 30;
 pub const flag_profile: u32 = 1;
+pub const ep_none: u32 = 0;
+pub const ep_nccl: u32 = 1;
+pub const ep_peer: u32 = 2;
 
 pub const gx_options = extern struct {
     device: u32,
@@ -46,7 +49,9 @@ pub const gx_caps = extern struct {
     free_bytes: u64,
     l2_bytes: u64,
     arena_bytes: u64,
-    device_name: [128]u8,
+    device_name: [120]u8,
+    ep_exchange: u32,
+    reserved: u32,
 };
 
 pub const gx_layer_desc = extern struct {
@@ -115,6 +120,7 @@ comptime {
     assert(@offsetOf(gx_options, "nccl_id") == 40);
     assert(@sizeOf(gx_caps) == 192);
     assert(@offsetOf(gx_caps, "device_name") == 64);
+    assert(@offsetOf(gx_caps, "ep_exchange") == 184);
     assert(@sizeOf(gx_layer_desc) == 112);
     assert(@offsetOf(gx_layer_desc, "router") == 72);
     assert(@sizeOf(gx_timings) == 48);

@@ -85,8 +85,15 @@ typedef struct gx_caps {
     uint64_t free_bytes;      /* free device memory now */
     uint64_t l2_bytes;
     uint64_t arena_bytes;     /* bytes held by uploaded layers on this device */
-    char device_name[128];
+    char device_name[120];
+    uint32_t ep_exchange;     /* expert-parallel rows: GX_EP_NONE until the first layer, then one of
+                                 GX_EP_PEER (NVLink peer memory) or GX_EP_NCCL */
+    uint32_t reserved;
 } gx_caps;                    /* 192 bytes */
+
+#define GX_EP_NONE 0u
+#define GX_EP_NCCL 1u
+#define GX_EP_PEER 2u
 
 /* One routed-expert layer as the Zig host holds it (src/model.zig:97-124, :408-421). */
 typedef struct gx_layer_desc {

@@ -106,4 +106,20 @@ def worker(rank: int, world: int, out_dir: str) -> None:
             res["rep_dup_rc"] = np.array(0)
         except abi.GxError as e:
             res["rep_dup_rc"] = np.array(e.code)
+        res["exchange"] = np.array(ctx.caps().ep_exchange)
+    # the same layer cases with the rows exchanged over NCCL (read when the first layer runs)
+    os.environ["GX_EP_NCCL"] = "1"
+    try:
+        with abi.Context(device=rank, max_tokens=max_tok, max_layers=1, rank=rank, world=world,
+                         nccl_id=nccl_id) as ctx:
+            res["nccl_exchange0"] = np.array(ctx.caps().ep_exchange)
+            for i, (name, kw, n_tok) in enumerate(CASES):
+                layer = make(kw)
+                ctx.upload_layer(0, layer)
+                x = tokens(i, rank, n_tok[rank], layer["n_embd"])
+                y, ids, w = ctx.forward_host(0, x, want_routing=True)
+                res[f"nccl_{name}_y"], res[f"nccl_{name}_ids"] = y, ids
+            res["nccl_exchange"] = np.array(ctx.caps().ep_exchange)
+    finally:
+        del os.environ["GX_EP_NCCL"]
     np.savez(Path(out_dir) / f"rank{rank}.npz", **res)

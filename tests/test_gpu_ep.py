@@ -1,5 +1,6 @@
 """Expert parallelism on 2 GPUs through the C ABI: two processes, one context each (world 2),
-experts sharded 50/50, NCCL dispatch and combine. Every rank's output must match the CPU oracle
+experts sharded 50/50, rows exchanged over NVLink peer memory (and, for the layer cases, over
+NCCL as well). Every rank's output must match the CPU oracle
 of the whole layer (src/engine.zig:520-642) on its own tokens, within the tolerance of the
 tensor-core path (its f16 operands). Cases:
 
@@ -8,7 +9,9 @@ tensor-core path (its f16 operands). Cases:
 - the config-0 layer shape with ragged per-expert segments;
 - a two-layer pre-norm stack on bf16 tokens;
 - device-pointer calls twice in a row;
-- the no-alloc decode entry, which the expert-parallel context must refuse."""
+- the no-alloc decode entry, which the expert-parallel context must refuse;
+- replicated experts;
+- the exchange in use (peer memory on distinct GPUs, NCCL when asked for)."""
 import numpy as np
 import pytest
 
@@ -45,13 +48,22 @@ def test_group_caps(ranks):
         assert res["caps_world"].tolist() == [r, 2]
 
 
+def test_exchange_kind(ranks):
+    from gyro_moe import abi
+    for res in ranks:
+        assert int(res["exchange"]) == abi.GX_EP_PEER
+        assert int(res["nccl_exchange0"]) == abi.GX_EP_NONE
+        assert int(res["nccl_exchange"]) == abi.GX_EP_NCCL
+
+
+@pytest.mark.parametrize("exchange", ["", "nccl_"])
 @pytest.mark.parametrize("case", [c[0] for c in __import__("ep_gpu_worker").CASES])
-def test_layer_matches_oracle_on_every_rank(ranks, case):
+def test_layer_matches_oracle_on_every_rank(ranks, case, exchange):
     import ep_gpu_worker
     kw = dict(next(c for c in ep_gpu_worker.CASES if c[0] == case)[1])
     layer = ep_gpu_worker.make(kw)
     for res in ranks:
-        x, y, ids = res[f"{case}_x"], res[f"{case}_y"], res[f"{case}_ids"]
+        x, y, ids = res[f"{case}_x"], res[f"{exchange}{case}_y"], res[f"{exchange}{case}_ids"]
         if x.shape[0] == 0:
             assert y.shape[0] == 0
             continue
