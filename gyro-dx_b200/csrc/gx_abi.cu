@@ -64,6 +64,8 @@ struct gx_context {
     int sm_count = 0;
     cudaStream_t stream = nullptr;
     uint32_t *codebook = nullptr;  // 2048 words = 4096 fp16
+    uint32_t *codebook_image = nullptr;  // the decode kernels' shared-memory codebook (interleaved copies)
+    unsigned *router_done = nullptr;     // completion count of the selecting router launch (0 between launches)
     std::vector<Layer> layers;
     std::vector<Matrix> mats;
     // scratch sized for max_tokens
@@ -102,6 +104,8 @@ struct gx_context {
     struct Ep {
         size_t src_cap = 0, recv_cap = 0, E = 0, U = 0;   // rows the buffers hold
         int *pos_of = nullptr;                          // [max_tokens][world]
+        uint64_t *dest_mask = nullptr;                  // plan scratch [max_tokens]
+        int *block_count = nullptr;                     // plan scratch [CTAs][kMaxEpWorld]
         uint32_t *send_ids = nullptr;                   // [world * max_tokens][U]
         float *send_w = nullptr;
         __half *send_rows = nullptr, *ret_rows = nullptr;   // [world * max_tokens][E]
@@ -270,8 +274,8 @@ void release_all(gx_context *c) {
     void *pf[] = {c->pf.A, c->pf.A2, c->pf.act, c->pf.Y, c->pf.ints, c->pf.xh};
     for (void *p : pf) if (p) cudaFree(p);
     for (auto &m : c->mats) if (m.tiles) cudaFree(m.tiles);
-    void *dev[] = {c->codebook, c->logits, c->weights, c->xscale, c->ss, c->ids, c->act, c->xbuf[0], c->xbuf[1],
-                   c->x_stage, c->y_stage, c->err, c->stack_table, c->stack_sync};
+    void *dev[] = {c->codebook, c->codebook_image, c->router_done, c->logits, c->weights, c->xscale, c->ss, c->ids,
+                   c->act, c->xbuf[0], c->xbuf[1], c->x_stage, c->y_stage, c->err, c->stack_table, c->stack_sync};
     for (void *p : dev) if (p) cudaFree(p);
     if (c->h_in) cudaFreeHost(c->h_in);
     if (c->h_out) cudaFreeHost(c->h_out);
@@ -279,7 +283,8 @@ void release_all(gx_context *c) {
         if (c->ep.peers[r] && r != c->rank) cudaIpcCloseMemHandle(c->ep.peers[r]);
     if (c->ep.block) cudaFree(c->ep.block);
     void *ep[] = {c->ep.pos_of, c->ep.send_ids, c->ep.send_w, c->ep.send_rows, c->ep.ret_rows, c->ep.recv_rows,
-                  c->ep.part_rows, c->ep.recv_ids, c->ep.recv_w, c->ep.counts};
+                  c->ep.part_rows, c->ep.recv_ids, c->ep.recv_w, c->ep.counts, c->ep.dest_mask,
+                  c->ep.block_count};
     for (void *p : ep) if (p) cudaFree(p);
     if (c->ep.h_counts) cudaFreeHost(c->ep.h_counts);
     if (c->ep.counts_ready) cudaEventDestroy(c->ep.counts_ready);
@@ -520,9 +525,13 @@ gx_result ensure_ep_send(gx_context *c, const Layer &L) {
     free_dev(e.send_w);
     free_dev(e.send_rows);
     free_dev(e.ret_rows);
+    free_dev(e.dest_mask);
+    free_dev(e.block_count);
     e.src_cap = 0;
     const size_t E = std::max<size_t>(e.E, L.E), U = std::max<size_t>(e.U, L.U);
     GX_CUDA(cudaMalloc(&e.pos_of, T * W * sizeof(int)));
+    GX_CUDA(cudaMalloc(&e.dest_mask, T * sizeof(uint64_t)));
+    GX_CUDA(cudaMalloc(&e.block_count, (size_t)std::max(1, gx::ep_plan_ctas((int)T)) * gx::kMaxEpWorld * sizeof(int)));
     GX_CUDA(cudaMalloc(&e.send_ids, rows * U * sizeof(uint32_t)));
     GX_CUDA(cudaMalloc(&e.send_w, rows * U * sizeof(float)));
     GX_CUDA(cudaMalloc(&e.send_rows, rows * E * sizeof(__half)));
@@ -873,6 +882,8 @@ gx_result enqueue_layer_ep(gx_context *c, const Layer &L, const void *x, uint32_
     pa.send_ids = e.send_ids;
     pa.send_w = e.send_w;
     pa.send_count = e.counts;
+    pa.dest_mask = e.dest_mask;
+    pa.block_count = e.block_count;
     pa.err = c->err;
     GX_CUDA(gx::launch_ep_plan(pa, c->stream));
     if (peer) return enqueue_layer_ep_peer(c, L, x, xb, n_tok, resid, resid_dtype, out, out_dtype, norm_eps, ev);
@@ -1045,11 +1056,14 @@ gx_result enqueue_layer(gx_context *c, const Layer &L, const void *x, uint32_t x
     ra.ids = c->ids;
     ra.weights = c->weights;
     ra.err = c->err;
-    const bool fused = gx::gate_up_fuses_topk((int)L.E, (int)L.F, (int)L.U, (int)n_tok, c->sm_count);
+    // the router's last CTA selects for a few tokens; otherwise gate_up_kernel or topk_kernel
+    const bool sel_router = n_tok <= (uint32_t)gx::kRouterSelectTok;
+    ra.done = sel_router ? c->router_done : nullptr;
+    const bool fused = !sel_router && gx::gate_up_fuses_topk((int)L.E, (int)L.F, (int)L.U, (int)n_tok, c->sm_count);
     // Programmatic overlap only between kernels of this chain: never across the phase events
     // of a profiled call, and not for the first kernel of a call (its predecessor is a copy).
     const bool pdl = ev == nullptr && chained;
-    GX_CUDA(gx::launch_router(ra, c->stream, pdl, !fused));
+    GX_CUDA(gx::launch_router(ra, c->stream, pdl, !fused && !sel_router));
     if (ev) GX_CUDA(record_phase(ev[1], c->stream));
 
     gx::GateUpArgs ga{};
@@ -1073,6 +1087,7 @@ gx_result enqueue_layer(gx_context *c, const Layer &L, const void *x, uint32_t x
     ga.weights_out = c->weights;
     ga.act = c->act;
     ga.codebook = c->codebook;
+    ga.codebook_image = c->codebook_image;
     ga.E = (int)L.E;
     ga.F = (int)L.F;
     ga.U = (int)L.U;
@@ -1095,6 +1110,7 @@ gx_result enqueue_layer(gx_context *c, const Layer &L, const void *x, uint32_t x
     da.out = out;
     da.out_bf16 = out_dtype == GX_BF16;
     da.codebook = c->codebook;
+    da.codebook_image = c->codebook_image;
     da.E = (int)L.E;
     da.F = (int)L.F;
     da.U = (int)L.U;
@@ -1233,7 +1249,7 @@ GX_API gx_result gx_comm_unique_id(uint8_t *out_id, uint64_t bytes) {
 
 GX_API gx_result gx_create(const gx_options *o, gx_context **out) {
     if (!o || !out || !o->codebook || o->codebook_bytes != 8192 || o->world == 0 || o->rank >= o->world ||
-        o->max_tokens == 0 || o->max_layers == 0 || o->max_tokens > (1u << 20) || o->world > 512)
+        o->max_tokens == 0 || o->max_layers == 0 || o->max_tokens > (1u << 20) || o->world > (uint32_t)gx::kMaxEpWorld)
         return GX_E_INVALIDARG;
     *out = nullptr;
     int n = 0;
@@ -1262,6 +1278,20 @@ GX_API gx_result gx_create(const gx_options *o, gx_context **out) {
         if (!ok) { r = GX_E_DEVICE; break; }
         if (cudaMalloc(&c->codebook, 8192) != cudaSuccess) { r = GX_E_OUTOFMEMORY; break; }
         if (cudaMemcpy(c->codebook, o->codebook, 8192, cudaMemcpyHostToDevice) != cudaSuccess) { r = GX_E_DEVICE; break; }
+        {
+            // word w of the image is codebook word w / kCodebookCopies (copy w % kCodebookCopies)
+            std::vector<uint32_t> image(2048 * (size_t)gx::kCodebookCopies);
+            const uint32_t *words = static_cast<const uint32_t *>(o->codebook);
+            for (size_t w = 0; w < image.size(); ++w) image[w] = words[w / gx::kCodebookCopies];
+            const size_t bytes = image.size() * sizeof(uint32_t);
+            if (cudaMalloc(&c->codebook_image, bytes) != cudaSuccess) { r = GX_E_OUTOFMEMORY; break; }
+            if (cudaMemcpy(c->codebook_image, image.data(), bytes, cudaMemcpyHostToDevice) != cudaSuccess) {
+                r = GX_E_DEVICE;
+                break;
+            }
+        }
+        if (cudaMalloc(&c->router_done, sizeof(unsigned)) != cudaSuccess) { r = GX_E_OUTOFMEMORY; break; }
+        if (cudaMemset(c->router_done, 0, sizeof(unsigned)) != cudaSuccess) { r = GX_E_DEVICE; break; }
         r = ensure_scratch(c);
         if (r != GX_OK || c->world == 1) break;
         r = open_group(c, o);
@@ -1882,8 +1912,10 @@ GX_API gx_result gx_moe_forward_noalloc(gx_context *c, uint32_t layer, const voi
     ra.ids = sel_ids;
     ra.weights = sel_w;
     ra.err = c->err;
-    const bool fused = gx::gate_up_fuses_topk((int)L.E, (int)L.F, (int)L.U, (int)n_tok, c->sm_count);
-    GX_CUDA(gx::launch_router(ra, c->stream, false, !fused));
+    const bool sel_router = n_tok <= (uint32_t)gx::kRouterSelectTok;
+    ra.done = sel_router ? c->router_done : nullptr;
+    const bool fused = !sel_router && gx::gate_up_fuses_topk((int)L.E, (int)L.F, (int)L.U, (int)n_tok, c->sm_count);
+    GX_CUDA(gx::launch_router(ra, c->stream, false, !fused && !sel_router));
 
     gx::GateUpArgs ga{};
     ga.type = L.type;
@@ -1906,6 +1938,7 @@ GX_API gx_result gx_moe_forward_noalloc(gx_context *c, uint32_t layer, const voi
     ga.weights_out = sel_w;
     ga.act = act;
     ga.codebook = c->codebook;
+    ga.codebook_image = c->codebook_image;
     ga.E = (int)L.E;
     ga.F = (int)L.F;
     ga.U = (int)L.U;
@@ -1927,6 +1960,7 @@ GX_API gx_result gx_moe_forward_noalloc(gx_context *c, uint32_t layer, const voi
     da.out = y;
     da.out_bf16 = y_dtype == GX_BF16;
     da.codebook = c->codebook;
+    da.codebook_image = c->codebook_image;
     da.E = (int)L.E;
     da.F = (int)L.F;
     da.U = (int)L.U;

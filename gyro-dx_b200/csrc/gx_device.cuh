@@ -41,6 +41,9 @@ struct Codebook {
 #pragma unroll 16
         for (int w = tid; w < WORDS; w += nthreads) smem[w] = __ldg(global_table + w / NCOPY);
     }
+    // The same words by bulk copies of a prebuilt image (image[w] = table[w / NCOPY]) into
+    // shared memory, completing on mbarrier bar (initialised, count 1). Thread 0 only.
+    __device__ static void stage_bulk(uint32_t *smem, const uint32_t *image, uint64_t *bar);
     // Word index of codebook entry idx in this lane's copy (copy_off = lane % NCOPY).
     __device__ static __forceinline__ uint32_t word(uint32_t idx, uint32_t copy_off) { return idx * NCOPY + copy_off; }
     __device__ static __forceinline__ uint32_t copy_off(int lane) { return (uint32_t)(lane % NCOPY); }
@@ -85,6 +88,15 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
 }
+template <int NCOPY>
+__device__ void Codebook<NCOPY>::stage_bulk(uint32_t *smem, const uint32_t *image, uint64_t *bar) {
+    constexpr uint32_t kChunk = 16384;
+    static_assert(BYTES % kChunk == 0, "codebook image in whole chunks");
+    mbar_expect_tx(bar, (uint32_t)BYTES);
+    for (uint32_t o = 0; o < (uint32_t)BYTES; o += kChunk)
+        bulk_g2s(reinterpret_cast<uint8_t *>(smem) + o, reinterpret_cast<const uint8_t *>(image) + o, kChunk, bar);
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
@@ -137,16 +149,20 @@ __device__ __forceinline__ void fwht128_warp(float (&v)[4], int lane) {
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
-// Optional phase trace (build with -DGX_TRACE): thread 0 of each CTA stores clock64 deltas from
-// the CTA's start at numbered points into gx_trace[kernel][cta][point]. Off in normal builds; the
-// array lives in the translation unit that defines GX_TRACE_OWNER (gx_kernels.cu).
+// Optional phase trace (build with -DGX_TRACE): thread 0 of each CTA stores %globaltimer (ns) at
+// numbered points into gx_trace[kernel][cta][point], and the CTA's start at point 7. Off in normal
+// builds; the array lives in the translation unit that defines GX_TRACE_OWNER (gx_kernels.cu).
 #if defined(GX_TRACE) && defined(GX_TRACE_OWNER)
 constexpr int kTraceKernels = 4, kTraceCtas = 160, kTracePoints = 8;
 __device__ long long gx_trace[kTraceKernels][kTraceCtas][kTracePoints];
-#define GX_TRACE_START(k) const long long gx_t0_ = clock64(); const int gx_tk_ = (k)
+#define GX_TRACE_START(k)                                                                   \
+    const int gx_tk_ = (k);                                                                 \
+    do {                                                                                    \
+        if (threadIdx.x == 0 && blockIdx.x < kTraceCtas) gx_trace[gx_tk_][blockIdx.x][7] = (long long)globaltimer_ns(); \
+    } while (0)
 #define GX_TRACE_POINT(p)                                                                  \
     do {                                                                                   \
-        if (threadIdx.x == 0 && blockIdx.x < kTraceCtas) gx_trace[gx_tk_][blockIdx.x][p] = clock64() - gx_t0_; \
+        if (threadIdx.x == 0 && blockIdx.x < kTraceCtas) gx_trace[gx_tk_][blockIdx.x][p] = (long long)globaltimer_ns(); \
     } while (0)
 #else
 #define GX_TRACE_START(k) do {} while (0)

@@ -33,74 +33,109 @@ __device__ __forceinline__ uint32_t local_expert(const EpPlanArgs &a, uint32_t e
     return a.route ? (uint32_t)a.route[e].y : e - lo;
 }
 
-// One CTA of 1024 threads per destination rank d: send rows for d are the tokens with a slot on
-// d, in token order (so each destination sees a stable order), at rows [d*stride, d*stride+count);
-// rows [count, pad_rows) are filled with empty slots, since a destination receives pad_rows rows
+// The plan is two token-parallel passes over CTAs of kPlanTok tokens. Pass 1 marks, per token,
+// the ranks that serve one of its slots (bit d of dest_mask) and counts them per CTA; pass 2 gives
+// each marked (token, d) its row: the CTA's base for d (the counts of the CTAs before it) plus its
+// rank among the CTA's marked tokens. So the send rows for d are the tokens with a slot on d, in
+// token order (each destination sees a stable order), at rows [d*stride, d*stride+count); rows
+// [count, pad_rows) are marked empty, since with NCCL rows a destination receives pad_rows rows
 // from every source without learning the count first.
-__global__ void __launch_bounds__(1024) ep_plan_kernel(EpPlanArgs a) {
-    __shared__ int wsum[32];
-    __shared__ int base, chunk;
-    const int d = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const uint32_t per = (uint32_t)(a.NE / a.W), lo = (uint32_t)d * per;
-    if (tid == 0) base = 0;
+__global__ void __launch_bounds__(kPlanTok) ep_plan_mask_kernel(EpPlanArgs a) {
+    __shared__ int cnt[kMaxEpWorld];
+    const int tid = threadIdx.x, lane = tid & 31;
+    const int t = blockIdx.x * kPlanTok + tid;
+    const uint32_t per = (uint32_t)(a.NE / a.W);
+    for (int d = tid; d < a.W; d += kPlanTok) cnt[d] = 0;
     __syncthreads();
-    for (int t0 = 0; t0 < a.n_tok; t0 += 1024) {
-        const int t = t0 + tid;
-        bool mine = false;
-        if (t < a.n_tok) {
-            for (int k = 0; k < a.U; ++k) {
-                const uint32_t e = a.ids[(size_t)t * a.U + k];
-                if (e >= (uint32_t)a.NE) {
-                    atomicExch(a.err, KERR_BOUNDS);
-                    continue;
-                }
-                if (d == 0 && a.expert_count) atomicAdd(a.expert_count + e, 1u);
-                if (serving_rank(a, e, per) == d) mine = true;
-            }
-        }
-        const unsigned vote = __ballot_sync(0xffffffffu, mine);
-        if (lane == 0) wsum[warp] = __popc(vote);
-        __syncthreads();
-        if (warp == 0) {
-            const int v = wsum[lane];
-            int incl = v;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const int u = __shfl_up_sync(0xffffffffu, incl, o);
-                if (lane >= o) incl += u;
-            }
-            wsum[lane] = incl - v;  // exclusive prefix of warp counts
-            if (lane == 31) chunk = incl;
-        }
-        __syncthreads();
-        const int pos = base + wsum[warp] + __popc(vote & ((1u << lane) - 1u));
-        if (t < a.n_tok) {
-            if (mine) {
-                const size_t row = (size_t)d * a.stride + pos;
-                a.pos_of[(size_t)t * a.W + d] = (int)row;
-                for (int k = 0; k < a.U; ++k) {
-                    const uint32_t e = a.ids[(size_t)t * a.U + k];
-                    const bool here = e < (uint32_t)a.NE && serving_rank(a, e, per) == d;
-                    a.send_ids[row * a.U + k] = here ? local_expert(a, e, lo) : kNoSlot;
-                    a.send_w[row * a.U + k] = here ? a.weights[(size_t)t * a.U + k] : 0.f;
-                }
-            } else {
-                a.pos_of[(size_t)t * a.W + d] = -1;
-            }
-        }
-        __syncthreads();
-        if (tid == 0) base += chunk;
-        __syncthreads();
-    }
-    if (tid == 0) a.send_count[d] = base;
-    // every destination receives pad_rows rows from this rank; the unused ones carry no slot
-    for (int r = base + tid; r < a.pad_rows; r += 1024) {
-        const size_t row = (size_t)d * a.stride + r;
+    uint64_t mask = 0;
+    if (t < a.n_tok) {
         for (int k = 0; k < a.U; ++k) {
-            a.send_ids[row * a.U + k] = kNoSlot;
-            a.send_w[row * a.U + k] = 0.f;
+            const uint32_t e = a.ids[(size_t)t * a.U + k];
+            if (e >= (uint32_t)a.NE) {
+                atomicExch(a.err, KERR_BOUNDS);
+                continue;
+            }
+            mask |= 1ull << serving_rank(a, e, per);
+        }
+        a.dest_mask[t] = mask;
+    }
+    if (a.expert_count) {
+        // routed-slot counts, one atomic per distinct expert in the warp
+        for (int k = 0; k < a.U; ++k) {
+            const uint32_t e = t < a.n_tok ? a.ids[(size_t)t * a.U + k] : kNoSlot;
+            const unsigned same = __match_any_sync(0xffffffffu, e);
+            if (e < (uint32_t)a.NE && lane == __ffs(same) - 1) atomicAdd(a.expert_count + e, (unsigned)__popc(same));
         }
     }
+    for (int d = 0; d < a.W; ++d) {
+        const unsigned v = __ballot_sync(0xffffffffu, (mask >> d) & 1);
+        if (lane == 0 && v) atomicAdd(&cnt[d], __popc(v));
+    }
+    __syncthreads();
+    for (int d = tid; d < a.W; d += kPlanTok) a.block_count[(size_t)blockIdx.x * kMaxEpWorld + d] = cnt[d];
+}
+
+__global__ void __launch_bounds__(kPlanTok) ep_plan_place_kernel(EpPlanArgs a) {
+    constexpr int kWarps = kPlanTok / 32;
+    __shared__ int base[kMaxEpWorld], total[kMaxEpWorld];
+    __shared__ int wcnt[kMaxEpWorld][kWarps];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int t = blockIdx.x * kPlanTok + tid;
+    const uint32_t per = (uint32_t)(a.NE / a.W);
+    // base and total of every destination: warp w sums destinations w, w + kWarps, ...
+    for (int d = warp; d < a.W; d += kWarps) {
+        int before = 0, all = 0;
+        for (int j = lane; j < (int)gridDim.x; j += 32) {
+            const int v = a.block_count[(size_t)j * kMaxEpWorld + d];
+            all += v;
+            if (j < (int)blockIdx.x) before += v;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            before += __shfl_xor_sync(0xffffffffu, before, o);
+            all += __shfl_xor_sync(0xffffffffu, all, o);
+        }
+        if (lane == 0) {
+            base[d] = before;
+            total[d] = all;
+        }
+    }
+    const uint64_t mask = t < a.n_tok ? a.dest_mask[t] : 0;
+    for (int d = 0; d < a.W; ++d) {
+        const unsigned v = __ballot_sync(0xffffffffu, (mask >> d) & 1);
+        if (lane == 0) wcnt[d][warp] = __popc(v);
+    }
+    __syncthreads();
+    if (blockIdx.x == 0)
+        for (int d = tid; d < a.W; d += kPlanTok) a.send_count[d] = total[d];
+    for (int d = 0; d < a.W; ++d) {
+        const unsigned v = __ballot_sync(0xffffffffu, (mask >> d) & 1);
+        if (t >= a.n_tok) continue;
+        if (!((mask >> d) & 1)) {
+            a.pos_of[(size_t)t * a.W + d] = -1;
+            continue;
+        }
+        int pos = base[d] + __popc(v & ((1u << lane) - 1u));
+        for (int w = 0; w < warp; ++w) pos += wcnt[d][w];
+        const size_t row = (size_t)d * a.stride + pos;
+        a.pos_of[(size_t)t * a.W + d] = (int)row;
+        const uint32_t lo = (uint32_t)d * per;
+        for (int k = 0; k < a.U; ++k) {
+            const uint32_t e = a.ids[(size_t)t * a.U + k];
+            const bool here = e < (uint32_t)a.NE && serving_rank(a, e, per) == d;
+            a.send_ids[row * a.U + k] = here ? local_expert(a, e, lo) : kNoSlot;
+            a.send_w[row * a.U + k] = here ? a.weights[(size_t)t * a.U + k] : 0.f;
+        }
+    }
+    // every destination receives pad_rows rows from this rank (NCCL rows); the unused ones carry no slot
+    for (int d = 0; d < a.W; ++d)
+        for (int r = total[d] + (int)blockIdx.x * kPlanTok + tid; r < a.pad_rows; r += (int)gridDim.x * kPlanTok) {
+            const size_t row = (size_t)d * a.stride + r;
+            for (int k = 0; k < a.U; ++k) {
+                a.send_ids[row * a.U + k] = kNoSlot;
+                a.send_w[row * a.U + k] = 0.f;
+            }
+        }
 }
 
 // out[t] = resid[t] + sum over destinations of the returned partial row of (t, d).
@@ -133,8 +168,10 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(EpCombineArgs a) {
 }
 
 cudaError_t launch_ep_plan(const EpPlanArgs &a, cudaStream_t s) {
-    if (a.W <= 0 || a.NE % a.W) return cudaErrorInvalidValue;
-    ep_plan_kernel<<<a.W, 1024, 0, s>>>(a);
+    if (a.W <= 0 || a.W > kMaxEpWorld || a.NE % a.W || a.n_tok < 0) return cudaErrorInvalidValue;
+    const int grid = std::max(1, ep_plan_ctas(a.n_tok));
+    ep_plan_mask_kernel<<<grid, kPlanTok, 0, s>>>(a);
+    ep_plan_place_kernel<<<grid, kPlanTok, 0, s>>>(a);
     return cudaGetLastError();
 }
 

@@ -105,4 +105,18 @@ __device__ __forceinline__ bool stage_wait(const StageCtl &c, int s, int *err) {
     return false;
 }
 
+// Waits for the bulk-staged codebook (barrier cb_bar, phase 0). On an expired wait every thread
+// sees false; the stage copies this CTA issued (up to two) and the codebook copy get one more
+// bounded wait before the CTA returns.
+__device__ __forceinline__ bool codebook_wait(uint64_t *cb_bar, const StageCtl &c, int *err) {
+    const bool ok = mbar_wait(cb_bar, 0u, err);
+    if (__syncthreads_and(ok)) return true;
+    if (threadIdx.x == 0) {
+        mbar_wait(cb_bar, 0u, nullptr);
+        for (int t = 0; t < 2 && t < c.n_stages; ++t) mbar_wait(&c.bar[t & 1], 0u, nullptr);
+    }
+    __syncthreads();
+    return false;
+}
+
 }  // namespace gx

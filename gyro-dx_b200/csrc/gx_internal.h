@@ -27,7 +27,14 @@ struct RouterArgs {
     uint32_t *ids;           // [n_tok][U]
     float *weights;          // [n_tok][U]
     int *err;
+    // Selection in the router's last CTA (few tokens): every CTA counts itself done here, and the
+    // last one selects the experts of every token and sets the counter back to 0. nullptr: a
+    // separate selection kernel (or gate_up_kernel) selects.
+    unsigned *done;
 };
+
+// Tokens up to which router_kernel selects the experts itself (in its last CTA).
+constexpr int kRouterSelectTok = 4;
 
 struct GateUpArgs {
     uint32_t type;
@@ -41,6 +48,7 @@ struct GateUpArgs {
     const uint32_t *ids;     // [n_slots] local expert of each slot (unfused only)
     float *act;              // [n_slots][F] silu(gate) * up
     const uint32_t *codebook;// 2048 words in global memory
+    const uint32_t *codebook_image;  // the shared-memory codebook image (kCodebookCopies copies)
     int E, F, U, n_slots, n_expert;
     int *err;
     // Fused selection (few tokens): each CTA selects the experts of its own tokens from the
@@ -71,6 +79,7 @@ struct DownArgs {
     void *out;               // [n_tok][E]
     int out_bf16;
     const uint32_t *codebook;
+    const uint32_t *codebook_image;  // the shared-memory codebook image (kCodebookCopies copies)
     int E, F, U, n_tok, n_expert;
     int *err;
 };
@@ -174,6 +183,11 @@ cudaError_t launch_decode_stack(const StackArgs &a, uint32_t type, int sm_count,
 // Slot id meaning "no expert of this rank" in expert-parallel rows.
 constexpr uint32_t kNoSlot = 0xffffffffu;
 
+// Expert-parallel groups hold at most kMaxEpWorld ranks; the plan handles kPlanTok tokens per CTA.
+constexpr int kMaxEpWorld = 64;
+constexpr int kPlanTok = 256;
+inline int ep_plan_ctas(int n_tok) { return (n_tok + kPlanTok - 1) / kPlanTok; }
+
 struct EpPlanArgs {
     const uint32_t *ids;     // [n_tok][U] global expert ids from the selection
     const float *weights;    // [n_tok][U]
@@ -187,6 +201,8 @@ struct EpPlanArgs {
     uint32_t *send_ids;      // [W*stride][U] destination-local expert id or kNoSlot
     float *send_w;           // [W*stride][U] routing weight (0 for kNoSlot)
     int *send_count;         // [W] rows per destination
+    uint64_t *dest_mask;     // [n_tok] scratch: bit d set if rank d serves one of the token's slots
+    int *block_count;        // [ep_plan_ctas(n_tok)][kMaxEpWorld] scratch: marked tokens per CTA
     int *err;
 };
 

@@ -37,7 +37,43 @@ namespace gx {
 // unit weight), logits = scale * (W x) + bias, softmax (src/kernels.zig:340-349), top-U with
 // lower-index ties (src/engine.zig:671-686), renormalisation by max(sum, 2^-14) and the optional
 // expert_weights_scale (src/engine.zig:533-539).
-__device__ void topk_token(const RouterArgs &a, int t, int lane) {
+// Tree reductions over a lane's slots (depth log2 N instead of a chain of N).
+template <int N>
+__device__ __forceinline__ float tree_max(const float (&v)[N]) {
+    float t[N];
+#pragma unroll
+    for (int j = 0; j < N; ++j) t[j] = v[j];
+#pragma unroll
+    for (int w = N / 2; w > 0; w >>= 1)
+#pragma unroll
+        for (int j = 0; j < w; ++j) t[j] = fmaxf(t[j], t[j + w]);
+    return t[0];
+}
+template <int N>
+__device__ __forceinline__ float tree_sum(const float (&v)[N]) {
+    float t[N];
+#pragma unroll
+    for (int j = 0; j < N; ++j) t[j] = v[j];
+#pragma unroll
+    for (int w = N / 2; w > 0; w >>= 1)
+#pragma unroll
+        for (int j = 0; j < w; ++j) t[j] = t[j] + t[j + w];
+    return t[0];
+}
+template <int N>
+__device__ __forceinline__ unsigned long long tree_max_u64(const unsigned long long (&v)[N]) {
+    unsigned long long t[N];
+#pragma unroll
+    for (int j = 0; j < N; ++j) t[j] = v[j];
+#pragma unroll
+    for (int w = N / 2; w > 0; w >>= 1)
+#pragma unroll
+        for (int j = 0; j < w; ++j) t[j] = t[j] > t[j + w] ? t[j] : t[j + w];
+    return t[0];
+}
+
+template <int NV>
+__device__ void topk_token_nv(const RouterArgs &a, int t, int lane) {
     const float *row = a.logits + (size_t)t * a.NE;
     float ss = 0.f;
     if (a.norm_eps > 0.f) {
@@ -71,66 +107,68 @@ __device__ void topk_token(const RouterArgs &a, int t, int lane) {
         }
     }
     const float scale = a.norm_eps > 0.f ? 1.0f / sqrtf(ss / (float)a.E + a.norm_eps) : 1.f;
-    float v[16];
+    // Expert lane + 32 j in slot j (NV slots per lane, NE <= 32 NV). Every logit and bias load of
+    // the lane goes out before the first is used (one round trip), then the split-K partials in
+    // split order.
+    float v[NV], bias[NV];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
+    for (int j = 0; j < NV; ++j) {
         const int i = lane + 32 * j;
-        float raw = 0.f;
-        if (i < a.NE) {
-            raw = __ldcg(row + i);
-            for (int z = 1; z < a.logit_splits; ++z) raw += __ldcg(row + (size_t)z * a.n_tok * a.NE + i);
-        }
-        v[j] = i < a.NE ? raw * scale + (a.bias ? __ldg(a.bias + i) : 0.f) : -INFINITY;
+        const bool on = i < a.NE;
+        v[j] = on ? __ldcg(row + i) : 0.f;
+        bias[j] = on && a.bias ? __ldg(a.bias + i) : 0.f;
     }
-    float m = v[0];
+    for (int z = 1; z < a.logit_splits; ++z) {
+        const float *rz = row + (size_t)z * a.n_tok * a.NE;
+        float p[NV];
 #pragma unroll
-    for (int j = 1; j < 16; ++j) m = fmaxf(m, v[j]);
+        for (int j = 0; j < NV; ++j) p[j] = lane + 32 * j < a.NE ? __ldcg(rz + lane + 32 * j) : 0.f;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    float s = 0.f;
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-        v[j] = (lane + 32 * j) < a.NE ? expf(v[j] - m) : 0.f;
-        s += v[j];
+        for (int j = 0; j < NV; ++j) v[j] += p[j];
     }
+#pragma unroll
+    for (int j = 0; j < NV; ++j) v[j] = lane + 32 * j < a.NE ? v[j] * scale + bias[j] : -INFINITY;
+    // softmax (src/kernels.zig:340-349): the maximum by one warp-wide integer maximum of the
+    // order-preserving image of the floats, the sum by a tree in the lane and across lanes
+    float m = tree_max(v);
+    {
+        int o = __float_as_int(m);
+        o = __reduce_max_sync(0xffffffffu, o >= 0 ? o : o ^ 0x7fffffff);
+        m = __int_as_float(o >= 0 ? o : o ^ 0x7fffffff);
+    }
+#pragma unroll
+    for (int j = 0; j < NV; ++j) v[j] = lane + 32 * j < a.NE ? expf(v[j] - m) : 0.f;
+    float s = tree_sum(v);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    // Selection key: probability bits (order-preserving for p >= 0) above the complemented
-    // index, so one unsigned max picks the largest probability and, among equal ones, the
-    // lowest index (the tie rule of src/engine.zig:671-686). Absent experts have key 0.
-    unsigned long long key[16];
+    // Selection key: probability bits (order-preserving for p >= 0) above the complemented index,
+    // so the largest key is the largest probability and, among equal ones, the lowest index (the
+    // tie rule of src/engine.zig:671-686). A round takes the lane's largest key by a tree, then
+    // two warp-wide unsigned maxima (probability, then index among equal probabilities). Absent
+    // and taken experts have key 0; present ones have a nonzero complemented index.
+    unsigned long long key[NV];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
+    for (int j = 0; j < NV; ++j) {
         const int i = lane + 32 * j;
         key[j] = i < a.NE ? ((unsigned long long)__float_as_uint(v[j] / s) << 32) | (0xffffffffu - (uint32_t)i) : 0ull;
     }
-    float my_w = 0.f;
+    float my_w = 0.f, total = 0.f;
     uint32_t my_id = 0;
     for (int k = 0; k < a.U; ++k) {
-        unsigned long long b8[8];
+        const unsigned long long best = tree_max_u64(key);
+        const uint32_t hm = __reduce_max_sync(0xffffffffu, (uint32_t)(best >> 32));
+        const uint32_t lm = __reduce_max_sync(0xffffffffu, (uint32_t)(best >> 32) == hm ? (uint32_t)best : 0u);
+        const unsigned long long win = ((unsigned long long)hm << 32) | lm;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) b8[j] = key[j] > key[j + 8] ? key[j] : key[j + 8];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) b8[j] = b8[j] > b8[j + 4] ? b8[j] : b8[j + 4];
-        b8[0] = b8[0] > b8[2] ? b8[0] : b8[2];
-        b8[1] = b8[1] > b8[3] ? b8[1] : b8[3];
-        unsigned long long best = b8[0] > b8[1] ? b8[0] : b8[1];
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
-            best = other > best ? other : best;
-        }
-#pragma unroll
-        for (int j = 0; j < 16; ++j)
-            if (key[j] == best) key[j] = 0ull;
+        for (int j = 0; j < NV; ++j)
+            if (key[j] == win) key[j] = 0ull;
+        // renormalisation sum in selection order (src/engine.zig:533-539)
+        total += __uint_as_float(hm);
         if (lane == k) {
-            my_w = __uint_as_float((uint32_t)(best >> 32));
-            my_id = 0xffffffffu - (uint32_t)best;
+            my_w = __uint_as_float(hm);
+            my_id = 0xffffffffu - lm;
         }
     }
-    // Renormalisation in selection order (src/engine.zig:533-539).
-    float total = 0.f;
-    for (int k = 0; k < a.U; ++k) total += __shfl_sync(0xffffffffu, my_w, k);
     total = fmaxf(total, 6.103515625e-5f);
     if (lane < a.U) {
         float w = my_w / total;
@@ -139,6 +177,13 @@ __device__ void topk_token(const RouterArgs &a, int t, int lane) {
         a.weights[(size_t)t * a.U + lane] = w;
     }
     if (lane == 0) a.xscale[t] = scale;
+}
+
+__device__ __forceinline__ void topk_token(const RouterArgs &a, int t, int lane) {
+    if (a.NE <= 256)
+        topk_token_nv<8>(a, t, lane);
+    else
+        topk_token_nv<16>(a, t, lane);
 }
 
 // Block-wide selection for one token by a 512-thread CTA (thread i scores expert i): the same
@@ -243,6 +288,58 @@ __global__ void __launch_bounds__(64) router_kernel(RouterArgs a) {
     GX_TRACE_POINT(0);
     pdl_wait();
     GX_TRACE_POINT(1);
+    if (NJ <= 16 && a.n_tok <= kRouterTok) {
+        // Few tokens: every warp reads the token rows straight into registers (all loads of a row
+        // out at once), four independent FMA chains, and warp 0 of CTA 0 takes the sums of squares.
+        // (E <= 2048: a row and the warp's weights fit in registers.)
+        for (int t = 0; t < (NJ <= 16 ? a.n_tok : 0); ++t) {
+            float4 xv[NJ];
+#pragma unroll
+            for (int j = 0; j < NJ; ++j) {
+                const int c = 128 * j + 4 * lane;
+                if (c < a.E) {
+                    const size_t g = (size_t)t * a.E + c;
+                    if (a.x_bf16) {
+                        const uint2 q = *reinterpret_cast<const uint2 *>(reinterpret_cast<const __nv_bfloat16 *>(a.x) + g);
+                        xv[j] = make_float4(__uint_as_float(q.x << 16), __uint_as_float(q.x & 0xffff0000u),
+                                            __uint_as_float(q.y << 16), __uint_as_float(q.y & 0xffff0000u));
+                    } else {
+                        xv[j] = *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(a.x) + g);
+                    }
+                } else {
+                    xv[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+            }
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int j = 0; j < NJ; ++j) {
+                float &q = acc[j & 3];
+                q = fmaf(wv[j].x, xv[j].x, q);
+                q = fmaf(wv[j].y, xv[j].y, q);
+                q = fmaf(wv[j].z, xv[j].z, q);
+                q = fmaf(wv[j].w, xv[j].w, q);
+            }
+            float dot = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+            if (lane == 0 && has_row) a.logits[(size_t)t * a.NE + r] = dot;
+            if (a.norm_eps > 0.f && blockIdx.x == 0 && warp == 0) {
+                float sq[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int j = 0; j < NJ; ++j) {
+                    float &q = sq[j & 3];
+                    q = fmaf(xv[j].x, xv[j].x, q);
+                    q = fmaf(xv[j].y, xv[j].y, q);
+                    q = fmaf(xv[j].z, xv[j].z, q);
+                    q = fmaf(xv[j].w, xv[j].w, q);
+                }
+                float ss = (sq[0] + sq[1]) + (sq[2] + sq[3]);
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+                if (lane == 0) a.ss[t] = ss;
+            }
+        }
+    } else
     for (int t0 = 0; t0 < a.n_tok; t0 += kRouterTok) {
         const int nt = min(kRouterTok, a.n_tok - t0);
         __syncthreads();
@@ -313,6 +410,20 @@ __global__ void __launch_bounds__(64) router_kernel(RouterArgs a) {
             for (int t = 0; t < nt; ++t) a.logits[(size_t)(t0 + t) * a.NE + r] = acc[t];
     }
     GX_TRACE_POINT(2);
+    if (a.done) {
+        // Lane 0 of every warp wrote this warp's logits (and CTA 0's warp 0 the sums of squares);
+        // it counts the warp done with one acquire-release add. The warp that counts last has
+        // acquired every other warp's writes: it selects the experts of every token and resets
+        // the count for the next launch.
+        unsigned old = 0;
+        if (lane == 0) asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(a.done) : "memory");
+        old = __shfl_sync(0xffffffffu, old, 0);
+        __syncwarp();  // the other lanes read after lane 0's acquire
+        if (old == gridDim.x * kRouterWarps - 1) {
+            for (int t = 0; t < a.n_tok; ++t) topk_token(a, t, lane);
+            if (lane == 0) *a.done = 0u;
+        }
+    }
 }
 
 __global__ void __launch_bounds__(256) topk_kernel(RouterArgs a) {
@@ -365,7 +476,10 @@ __global__ void __launch_bounds__(512, 1) gate_up_kernel(GateUpArgs a, int P) {
     if (tid == 0) {
         mbar_init(&bar[0], 1);
         mbar_init(&bar[1], 1);
+        mbar_init(&bar[2], 1);
         fence_barrier_init();
+        // the codebook streams in from its prebuilt image while the router still runs
+        CB::stage_bulk(cb, a.codebook_image, &bar[2]);
     }
     __syncthreads();
 
@@ -394,7 +508,6 @@ __global__ void __launch_bounds__(512, 1) gate_up_kernel(GateUpArgs a, int P) {
                      &bar[s & 1]);
         }
     };
-    CB::stage(cb, a.codebook, tid, blockDim.x);
     GX_TRACE_POINT(0);
     pdl_wait();
     GX_TRACE_POINT(1);
@@ -412,11 +525,11 @@ __global__ void __launch_bounds__(512, 1) gate_up_kernel(GateUpArgs a, int P) {
             }
         }
     }
+    // no CTA barrier here: the other warps rotate their input while warp 0 issues the copies
     if (warp == 0) {
         if (ctl.n_stages > 0) issue(0);
         if (ctl.n_stages > 1) issue(1);
     }
-    __syncthreads();
 
     GX_TRACE_POINT(2);
     const bool active = warp < WB * RG;
@@ -444,6 +557,7 @@ __global__ void __launch_bounds__(512, 1) gate_up_kernel(GateUpArgs a, int P) {
         build_a(cur_tok);
     }
     GX_TRACE_POINT(3);
+    if (!codebook_wait(&bar[2], ctl, a.err)) return;
 
     for (int s = 0; s < ctl.n_stages; ++s) {
         if (!stage_wait(ctl, s, a.err)) return;
@@ -531,7 +645,9 @@ __global__ void __launch_bounds__(512, 1) down_kernel(DownArgs a, int P) {
     if (tid == 0) {
         mbar_init(&bar[0], 1);
         mbar_init(&bar[1], 1);
+        mbar_init(&bar[2], 1);
         fence_barrier_init();
+        CB::stage_bulk(cb, a.codebook_image, &bar[2]);
     }
     __syncthreads();
 
@@ -553,7 +669,6 @@ __global__ void __launch_bounds__(512, 1) down_kernel(DownArgs a, int P) {
                      a.down + (uint64_t)e * a.expert_bytes + (uint64_t)i * slot_bytes, (uint32_t)slot_bytes, &bar[s & 1]);
         }
     };
-    CB::stage(cb, a.codebook, tid, blockDim.x);
     GX_TRACE_POINT(0);
     pdl_wait();
     GX_TRACE_POINT(1);
@@ -561,7 +676,6 @@ __global__ void __launch_bounds__(512, 1) down_kernel(DownArgs a, int P) {
         if (ctl.n_stages > 0) issue(0);
         if (ctl.n_stages > 1) issue(1);
     }
-    __syncthreads();
 
     GX_TRACE_POINT(2);
     const uint32_t copy_off = CB::copy_off(lane);
@@ -607,6 +721,7 @@ __global__ void __launch_bounds__(512, 1) down_kernel(DownArgs a, int P) {
         build_a(cur_tok);
     }
     GX_TRACE_POINT(3);
+    if (!codebook_wait(&bar[2], ctl, a.err)) return;
 
     for (int s = 0; s < ctl.n_stages; ++s) {
         if (!stage_wait(ctl, s, a.err)) return;

@@ -65,7 +65,7 @@ enum {
 typedef struct gx_options {
     uint32_t device;          /* CUDA device ordinal */
     uint32_t rank;            /* expert-parallel rank in [0, world) */
-    uint32_t world;           /* expert-parallel group size; 1 = single GPU */
+    uint32_t world;           /* expert-parallel group size, 1..64; 1 = single GPU */
     uint32_t max_tokens;      /* largest n_tok of one forward call on this rank */
     uint32_t max_layers;      /* number of layer slots (gx_upload_layer indices) */
     uint32_t flags;           /* GX_FLAG_* */

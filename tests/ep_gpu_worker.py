@@ -48,17 +48,22 @@ def worker(rank: int, world: int, out_dir: str) -> None:
     import torch
     torch.cuda.set_device(rank)
     from gyro_moe import abi
-    idf = Path(out_dir) / "nccl_id"
-    if rank == 0:
-        tmp = idf.with_suffix(".tmp")
-        tmp.write_bytes(abi.unique_id())
-        tmp.rename(idf)
-    t0 = time.time()
-    while not idf.exists():
-        if time.time() - t0 > 60:
-            raise RuntimeError("no NCCL id from rank 0")
-        time.sleep(0.05)
-    nccl_id = idf.read_bytes()
+
+    def shared_id(name: str) -> bytes:
+        """A fresh NCCL id from rank 0 (one per communicator), passed through a file."""
+        idf = Path(out_dir) / name
+        if rank == 0:
+            tmp = idf.with_suffix(".tmp")
+            tmp.write_bytes(abi.unique_id())
+            tmp.rename(idf)
+        t0 = time.time()
+        while not idf.exists():
+            if time.time() - t0 > 60:
+                raise RuntimeError("no NCCL id from rank 0")
+            time.sleep(0.05)
+        return idf.read_bytes()
+
+    nccl_id = shared_id("nccl_id")
     res = {}
     max_tok = max(max(n) for _, _, n in CASES)
     with abi.Context(device=rank, max_tokens=max_tok, max_layers=2, rank=rank, world=world, nccl_id=nccl_id) as ctx:
@@ -111,7 +116,7 @@ def worker(rank: int, world: int, out_dir: str) -> None:
     os.environ["GX_EP_NCCL"] = "1"
     try:
         with abi.Context(device=rank, max_tokens=max_tok, max_layers=1, rank=rank, world=world,
-                         nccl_id=nccl_id) as ctx:
+                         nccl_id=shared_id("nccl_id2")) as ctx:
             res["nccl_exchange0"] = np.array(ctx.caps().ep_exchange)
             for i, (name, kw, n_tok) in enumerate(CASES):
                 layer = make(kw)
