@@ -506,17 +506,31 @@ def ep_batch():
     return lengths, offsets, x
 
 
+def rank_sequences(lengths, world: int) -> list:
+    """Sequences of every rank: longest first, each to the rank with the fewest tokens so far
+    (ties to the lower rank), so the busiest rank holds close to 1/world of the batch; a rank
+    keeps its sequences in batch order."""
+    load = [0] * world
+    seqs = [[] for _ in range(world)]
+    for i in sorted(range(len(lengths)), key=lambda i: (-int(lengths[i]), i)):
+        r = min(range(world), key=lambda r: (load[r], r))
+        load[r] += int(lengths[i])
+        seqs[r].append(i)
+    return [sorted(q) for q in seqs]
+
+
 def rank_tokens(offsets, x, rank: int, world: int) -> np.ndarray:
-    """A rank's slice of the ragged batch: sequences rank, rank + world, ..."""
-    seqs = range(rank, len(offsets) - 1, world)
-    parts = [x[offsets[i]:offsets[i + 1]] for i in seqs]
+    """A rank's slice of the ragged batch (its sequences from rank_sequences, concatenated)."""
+    lengths = np.diff(offsets)
+    parts = [x[offsets[i]:offsets[i + 1]] for i in rank_sequences(lengths, world)[rank]]
     return np.concatenate(parts) if parts else np.zeros((0, E), np.uint16)
 
 
 def run_ep(args):
     """the packed batch through the 40-layer stack (Zipf(1.1) routing per
-    layer). With N ranks each rank holds 256/N experts of every layer and routes its own
-    sequences; dispatch and combine are NCCL exchanges inside the library. The total batch is
+    layer). With N ranks each rank holds 256/N experts of every layer (plus replicas of the hot
+    ones) and routes its own sequences (rank_sequences balances their tokens); dispatch and
+    combine run inside the library, over NVLink peer memory or NCCL. The total batch is
     fixed, so scaling is strong: value = all tokens / max-over-ranks time per step."""
     import datetime
     import torch
