@@ -7,6 +7,7 @@ fallback for any entry point.
 from __future__ import annotations
 
 import ctypes
+import os
 from pathlib import Path
 
 import numpy as np
@@ -91,11 +92,12 @@ _LIB = None
 
 
 def load(path: Path | str | None = None) -> ctypes.CDLL:
-    """Loads libgyromoe.so (raises if it was not built)."""
+    """Loads libgyromoe.so (raises if it was not built). GYRO_MOE_LIB in the environment names
+    another build of the same library (for side-by-side timing)."""
     global _LIB
     if _LIB is not None and path is None:
         return _LIB
-    p = Path(path) if path else LIB_PATH
+    p = Path(path) if path else Path(os.environ.get("GYRO_MOE_LIB", "") or LIB_PATH)
     if not p.exists():
         raise RuntimeError(f"{p} is missing: build it with gyro-dx_b200/gyro_moe/build.py (no CPU fallback exists)")
     lib = ctypes.CDLL(str(p))
