@@ -1887,6 +1887,8 @@ GX_API gx_result gx_moe_forward_noalloc(gx_context *c, uint32_t layer, const voi
 
     // Every scratch word a kernel reads is written earlier in the same call (logits by the
     // router, selections by the top-k step, activations by gate/up), so nothing is cleared.
+    // For up to kRouterSelectTok tokens the router's arrival count is the context's own
+    // counter (allocated by gx_create, zero between launches), not a word of this array.
     float *logits = reinterpret_cast<float *>(base + kNaLogits);
     float *ss = reinterpret_cast<float *>(base + kNaSs);
     float *xscale = reinterpret_cast<float *>(base + kNaXscale);
