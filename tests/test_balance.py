@@ -28,3 +28,24 @@ def test_zipf_popularity_is_evened_out():
 def test_even_load_needs_no_replicas():
     assert balance.choose_replicas(np.ones(64), 8) == []
     assert balance.choose_replicas(np.ones(64), 1) == []
+
+
+def test_bench_sequence_placement_covers_the_batch_evenly():
+    # bench.rank_sequences: every sequence on exactly one rank, in batch order within a rank, and
+    # the busiest rank within one sequence of an even share (longest-first greedy placement)
+    import sys
+    from pathlib import Path
+    root = Path(__file__).resolve().parents[1]
+    if str(root) not in sys.path:
+        sys.path.insert(0, str(root))
+    import bench
+    lengths, offsets, _ = bench.ep_batch()
+    for world in (1, 2, 4, 8):
+        seqs = bench.rank_sequences(lengths, world)
+        flat = sorted(i for q in seqs for i in q)
+        assert flat == list(range(len(lengths)))
+        assert all(q == sorted(q) for q in seqs)
+        loads = [int(sum(lengths[i] for i in q)) for q in seqs]
+        assert max(loads) <= lengths.sum() / world + lengths.max()
+        assert sum(bench.rank_tokens(offsets, np.zeros((offsets[-1], 1), np.uint16), r, world).shape[0]
+                   for r in range(world)) == offsets[-1]
