@@ -573,7 +573,7 @@ def run_ep(args):
     for i in range(W):
         ticket = ctx.stack_forward(0, args.layers, xs[i % 2], y)
     ctx.wait(ticket)
-    replicas = []
+    replicas, rep0 = [], []
     if dist and not args.no_replicas:
         # expert-parallel load balance: the warm-up's routed-slot counts, summed over ranks,
         # choose per layer the popular experts every rank serves for its own tokens
@@ -584,6 +584,8 @@ def run_ep(args):
             rep = balance.choose_replicas(cnt.cpu().numpy(), world)
             ctx.replicate_experts(l, rep)
             replicas.append(len(rep))
+            if l == 0:
+                rep0 = list(rep)
         for i in range(W):
             ticket = ctx.stack_forward(0, args.layers, xs[i % 2], y)
         ctx.wait(ticket)
@@ -614,11 +616,15 @@ def run_ep(args):
     ph = ctx.timings()
     ctx.set_flags(0)
     per = NE // world
-    own = np.bincount(ids.cpu().numpy().reshape(-1).astype(np.int64) // per, minlength=world).astype(np.float64)
+    # slots each rank serves: a shard expert's slots on its owner, a replicated expert's slots on
+    # the token's own rank (layer 0's replica list)
+    flat = ids.cpu().numpy().reshape(-1).astype(np.int64)
+    replicated = np.isin(flat, np.array(rep0, np.int64))
+    own = np.bincount(flat[~replicated] // per, minlength=world).astype(np.float64)
     sent = torch.from_numpy(own).to(dev)
     if dist:
-        dist.all_reduce(sent)                     # slots every rank serves, summed over sources
-    slots_here = float(sent[rank].item())
+        dist.all_reduce(sent)                     # shard slots every rank serves, summed over sources
+    slots_here = float(sent[rank].item()) + float(replicated.sum())
     gu_flops = slots_here * 2 * F * E * 2
     agg = torch.tensor([gu_flops, ph.gate_up_ns * 1e-9, ph.router_ns * 1e-9, ph.down_ns * 1e-9, ph.total_ns * 1e-9],
                        dtype=torch.float64, device=dev)
