@@ -120,6 +120,27 @@ def test_zipf_routing_with_empty_experts(ctx):
     check(want, got)
 
 
+@pytest.mark.parametrize("n_tok", [1, 3, 12, 80])
+def test_tied_experts_selected_in_index_order(ctx, n_tok):
+    # Ten experts share one router row and a large bias, so their probabilities tie exactly and
+    # always win: every token must select the eight lowest of them, in index order
+    # (src/engine.zig:671-686). 1 and 3 tokens take the router's own selection, 12 gate_up's,
+    # 80 the many-token path.
+    layer = synth.make_layer(21, n_expert=256, E=256, F=128, U=8)
+    group = [5, 9, 17, 33, 40, 41, 100, 200, 201, 255]
+    layer["router"][group] = layer["router"][group[0]]
+    layer["router_bias"] = np.zeros(256, np.float32)
+    layer["router_bias"][group] = 10.0
+    x = synth.tokens(22, n_tok, E=256)
+    ctx.upload_layer(1, layer)
+    want, wids, _ = oracle.moe_ffn(layer, x)
+    got, ids, w = ctx.forward_host(1, x, want_routing=True)
+    assert wids.tolist() == [group[:8]] * n_tok
+    assert ids.tolist() == [group[:8]] * n_tok
+    np.testing.assert_allclose(w, np.full((n_tok, 8), 0.125, np.float32), rtol=1e-6)
+    check(want, got, tight=5e-3 if n_tok >= 64 else TIGHT)   # 80: the f16 tensor-core path
+
+
 def test_stack_matches_oracle_chain(ctx):
     layers = [synth.make_layer(40 + i, n_expert=16, E=256, F=128, U=4) for i in range(3)]
     for i, l in enumerate(layers):
