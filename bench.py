@@ -646,9 +646,9 @@ def run_ep(args):
         dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
     e2e_s = float(e2e_t.item())
     # router, top-k, rotation (push with peer memory), three grouping kernels, two packs, two
-    # GEMMs, combine (return with peer memory); expert parallel adds the plan and the sum of
-    # partial rows, and with peer memory the two bounded waits
-    launches_per_layer = 11 if world == 1 else 15 if exchange == abi.GX_EP_PEER else 13
+    # GEMMs, combine (return with peer memory); expert parallel adds the two plan kernels and the
+    # sum of partial rows, and with peer memory the two bounded waits
+    launches_per_layer = 11 if world == 1 else 16 if exchange == abi.GX_EP_PEER else 14
     line = {
         "metric": METRIC, "value": K * T / (ms / 1e3), "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
         "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
