@@ -34,12 +34,10 @@ def packed_matrix(rng: np.random.Generator, type_id: int, rows: int, cols: int,
     1/sqrt(cols)); returns uint8 [rows, row_bytes]."""
     bb = BLOCK_BYTES[type_id]
     nb = cols // 128
-    n = rows * nb * bb
-    raw = rng.bit_generator.random_raw((n + 7) // 8).view(np.uint8)[:n]
-    data = raw.reshape(rows, nb, bb)
+    data = rng.integers(0, 256, rows * nb * bb, dtype=np.uint8)
     d = fp16_bits(1.0 / np.sqrt(cols) if scale is None else scale)
-    data[:, :, 0] = d & 0xFF
-    data[:, :, 1] = d >> 8
+    # every block size is even, so each block's little-endian fp16 scale is one uint16 word
+    data.view("<u2").reshape(rows * nb, bb // 2)[:, 0] = d
     return data.reshape(rows, nb * bb)
 
 

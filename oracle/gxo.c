@@ -7,6 +7,9 @@
  *                      own CPU engine is Zig, and no Zig toolchain exists on these machines).
  * Every function names the reference lines it restates.
  */
+#ifdef GXO_THREADS
+#define _GNU_SOURCE /* syscall() for the futex waits of the worker pool */
+#endif
 #include "gxo.h"
 
 #include <math.h>
@@ -40,25 +43,77 @@ int gxo_max_threads(void) {
 }
 
 /* Chunked parallel-for in the manner of src/pool.zig:84-114: an atomic cursor hands out
- * [start, start + chunk) ranges; the calling thread participates. */
+ * [start, start + chunk) ranges and the calling thread participates. The fast build keeps one
+ * pool of parked worker threads for the life of the process, as the reference engine does
+ * (src/pool.zig:63-81: a generation counter wakes the workers, a pending count tells the caller
+ * when they are done; both waits spin briefly, then sleep on a futex), so a call pays a wake-up,
+ * not a thread start. */
 typedef void (*range_fn)(void *ctx, size_t start, size_t end);
 #ifdef GXO_THREADS
-typedef struct pool_job {
+#include <linux/futex.h>
+#include <sys/syscall.h>
+
+#define GXO_MAX_WORKERS 255
+typedef struct pool_state {
+    pthread_mutex_t init_lock;
+    int workers;                 /* parked threads, started once */
+    int active;                  /* workers that drain the current job */
     range_fn fn;
     void *ctx;
     size_t count, chunk;
     atomic_size_t next;
-} pool_job;
+    atomic_uint generation;      /* bumped once per job */
+    atomic_uint pending;         /* workers still inside the current job */
+} pool_state;
+static pool_state g_pool = {PTHREAD_MUTEX_INITIALIZER, 0, 0, NULL, NULL, 0, 0, 0, 0, 0};
 
-static void *pool_drain(void *arg) {
-    pool_job *job = (pool_job *)arg;
+static void futex_wait_u32(atomic_uint *addr, unsigned expected) {
+    syscall(SYS_futex, (unsigned *)addr, FUTEX_WAIT_PRIVATE, expected, NULL, NULL, 0);
+}
+static void futex_wake_u32(atomic_uint *addr, int n) {
+    syscall(SYS_futex, (unsigned *)addr, FUTEX_WAKE_PRIVATE, n, NULL, NULL, 0);
+}
+
+static void pool_drain(void) {
     for (;;) {
-        size_t start = atomic_fetch_add_explicit(&job->next, job->chunk, memory_order_relaxed);
-        if (start >= job->count) break;
-        size_t end = start + job->chunk < job->count ? start + job->chunk : job->count;
-        job->fn(job->ctx, start, end);
+        size_t start = atomic_fetch_add_explicit(&g_pool.next, g_pool.chunk, memory_order_relaxed);
+        if (start >= g_pool.count) break;
+        size_t end = start + g_pool.chunk < g_pool.count ? start + g_pool.chunk : g_pool.count;
+        g_pool.fn(g_pool.ctx, start, end);
+    }
+}
+
+static void *pool_worker(void *arg) {
+    const int index = (int)(intptr_t)arg;
+    unsigned seen = 0;
+    for (;;) {
+        unsigned spins = 0, g;
+        while ((g = atomic_load_explicit(&g_pool.generation, memory_order_acquire)) == seen) {
+            if (++spins < 4096) continue;
+            futex_wait_u32(&g_pool.generation, seen);
+        }
+        seen = g;
+        if (index < g_pool.active) pool_drain();
+        if (atomic_fetch_sub_explicit(&g_pool.pending, 1, memory_order_acq_rel) == 1)
+            futex_wake_u32(&g_pool.pending, 1);
     }
     return NULL;
+}
+
+/* Starts the parked workers once (threads - 1 of them, at most GXO_MAX_WORKERS). */
+static int pool_start(int threads) {
+    pthread_mutex_lock(&g_pool.init_lock);
+    if (g_pool.workers == 0) {
+        int want = threads - 1 < GXO_MAX_WORKERS ? threads - 1 : GXO_MAX_WORKERS;
+        for (int i = 0; i < want; ++i) {
+            pthread_t t;
+            if (pthread_create(&t, NULL, pool_worker, (void *)(intptr_t)i) != 0) break;
+            pthread_detach(t);
+            g_pool.workers++;
+        }
+    }
+    pthread_mutex_unlock(&g_pool.init_lock);
+    return g_pool.workers;
 }
 #endif
 
@@ -66,14 +121,22 @@ static void pool_run(int threads, size_t count, size_t chunk, range_fn fn, void 
     if (count == 0) return;
     if (chunk == 0) chunk = 1;
 #ifdef GXO_THREADS
-    if (threads > 1 && count > chunk) {
-        pool_job job = {fn, ctx, count, chunk, 0};
-        pthread_t tid[256];
-        int started = 0;
-        for (int i = 0; i < threads - 1 && i < 256; ++i)
-            if (pthread_create(&tid[i], NULL, pool_drain, &job) == 0) started++;
-        pool_drain(&job);
-        for (int i = 0; i < started; ++i) pthread_join(tid[i], NULL);
+    if (threads > 1 && count > chunk && pool_start(threads) > 0) {
+        g_pool.fn = fn;
+        g_pool.ctx = ctx;
+        g_pool.count = count;
+        g_pool.chunk = chunk;
+        g_pool.active = threads - 1 < g_pool.workers ? threads - 1 : g_pool.workers;
+        atomic_store_explicit(&g_pool.next, 0, memory_order_relaxed);
+        atomic_store_explicit(&g_pool.pending, (unsigned)g_pool.workers, memory_order_release);
+        atomic_fetch_add_explicit(&g_pool.generation, 1, memory_order_acq_rel);
+        futex_wake_u32(&g_pool.generation, GXO_MAX_WORKERS);
+        pool_drain();
+        unsigned spins = 0, left;
+        while ((left = atomic_load_explicit(&g_pool.pending, memory_order_acquire)) != 0) {
+            if (++spins < (1u << 16)) continue;
+            futex_wait_u32(&g_pool.pending, left);
+        }
         return;
     }
 #else

@@ -1,9 +1,11 @@
 """gx_moe_forward_noalloc (the decode layer on the library's static scratch, no allocation on
-any call) against gx_moe_forward on the same layer and tokens, through the C ABI. The file sorts
-last so the check also runs after every other GPU test in one process; it passes alone too."""
+any call) against gx_moe_forward on the same layer and tokens, through the C ABI, and against the
+CPU oracle directly. The file sorts last so the check also runs after every other GPU test in one
+process; it passes alone too."""
 import numpy as np
 import pytest
 
+from oracle import oracle
 from gyro_moe import abi, metrics, synth
 from layer_case import small_layer
 
@@ -41,10 +43,13 @@ def test_noalloc_matches_forward_on_two_calls_in_a_row(type_id):
         for idx, x, U in cases:
             xt = torch.from_numpy(x).cuda()
             want = run(ctx, ctx.forward, idx, xt, U)
+            ref, ref_ids, _ = oracle.moe_ffn(layer if idx == 0 else big, x)
             for _ in range(2):                         # two calls in a row on the same scratch
                 got = run(ctx, ctx.forward_noalloc, idx, xt, U)
                 close(want[0], got[0])
+                close(ref, got[0])                     # and on its own against the oracle
                 assert metrics.topk_sets(want[1], got[1])["flips"] == 0
+                assert metrics.topk_sets(ref_ids, got[1])["flips"] == 0
                 np.testing.assert_allclose(got[2], want[2], rtol=1e-6, atol=0)
 
 
