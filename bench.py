@@ -73,6 +73,8 @@ def parse():
     p.add_argument("--cpu-seconds", type=float, default=15.0)
     p.add_argument("--parity-tokens", type=int, default=4, help="ep-prefill: tokens per rank checked")
     p.add_argument("--no-replicas", action="store_true", help="ep-prefill: plain expert sharding, no replicas")
+    p.add_argument("--sweep-only", default="", help="sweep: one case, e.g. TQ2_T:512x2048 (profiling)")
+    p.add_argument("--sweep-l2x", type=float, default=4.5, help="sweep: matrix bytes per launch in units of L2")
     return p.parse_args()
 
 
@@ -412,17 +414,21 @@ def reference_decode(type_id: int, packed: np.ndarray, n: int) -> np.ndarray:
     return oracle.decode_row(type_id, packed.tobytes(), n)
 
 
-def measure_sweep(torch, dev, l2_bytes: int, reps: int = 5, warm: int = 3) -> dict:
+def measure_sweep(torch, dev, l2_bytes: int, reps: int = 5, warm: int = 3, only: str = "",
+                  l2x: float = 4.5) -> dict:
     """Every Gyro type at [512x2048] and [2048x512]: n distinct matrices of the projection shape,
     together more than 4.5x the L2, stored as one tall matrix (rows are independent, so row block
-    i is matrix i) and multiplied in one launch per batch size."""
+    i is matrix i) and multiplied in one launch per batch size. only = "TYPE:ROWSxCOLS" runs one
+    case (profiling)."""
     from gyro_moe import abi, synth
     pk = peaks()
     rows_out = []
     for type_id in sorted(synth.BLOCK_BYTES):
         for rows, cols in SWEEP_SHAPES:
+            if only and only != f"{synth.TYPE_NAMES[type_id]}:{rows}x{cols}":
+                continue
             proj = rows * (cols // 128) * synth.BLOCK_BYTES[type_id]
-            n_mats = int(np.ceil(4.5 * l2_bytes / proj))
+            n_mats = int(np.ceil(l2x * l2_bytes / proj))
             W = synth.packed_matrix(np.random.default_rng(type_id * 100 + rows), type_id, rows * n_mats, cols)
             # bit-exact decoded weights: a sample of 64 rows against the reference CPU decoder
             sample = np.ascontiguousarray(W[:64]).reshape(-1)
@@ -456,7 +462,7 @@ def measure_sweep(torch, dev, l2_bytes: int, reps: int = 5, warm: int = 3) -> di
                     "batch 1/4/16, f32 activations",
         "unit": "GB/s", "peak": pk["hbm_gbs"], "peak_source": f"{pk['source']} (MEASURED_PEAKS.json hbm_gbs)",
         "bytes": "packed codes + scales of all matrices + batch x (rows + cols) x 4 B of activations per matrix",
-        "timing": f"CUDA events around {reps} launches after {warm} warm-up launches; one launch covers > 4.5x L2 "
+        "timing": f"CUDA events around {reps} launches after {warm} warm-up launches; one launch covers {l2x}x L2 "
                   "of distinct matrices (no L2 reuse between launches)",
         "kernel": "matvec_kernel (bulk-copied tiles, 16 bank-interleaved shared-memory codebooks, mma.sync)",
         "results": rows_out,
@@ -678,12 +684,13 @@ def run_single(args):
         r = measure_prefill(torch, dev, args.tokens, args.steps, args.warmup)
         dtype, scaling = "f16", "weak"
     else:
-        r = measure_sweep(torch, dev, int(torch.cuda.get_device_properties(dev).L2_cache_size))
-        tq2 = next(e for e in r["results"] if e["type"] == "TQ2_T" and e["shape"] == "512x2048")
+        r = measure_sweep(torch, dev, int(torch.cuda.get_device_properties(dev).L2_cache_size),
+                          only=args.sweep_only, l2x=args.sweep_l2x)
+        tq2 = next((e for e in r["results"] if e["type"] == "TQ2_T" and e["shape"] == "512x2048"), r["results"][0])
         line = {"metric": METRIC, "value": tq2["batch1"]["gbs"], "unit": "GB/s", "n_gpus": 1, "steps": 5, "warmup": 3,
                 "ms_per_step": tq2["batch1"]["launch_us"] / 1e3, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded; BASELINE.json config 3)",
-                "config": {"workload": r["workload"], "headline": "TQ2_T 512x2048 batch 1"},
+                "config": {"workload": r["workload"], "headline": f"{tq2['type']} {tq2['shape']} batch 1"},
                 "roofline": {"kernel": r["kernel"], "bound": "hbm", "achieved": tq2["batch1"]["gbs"], "peak": r["peak"],
                              "unit": "GB/s", "frac": tq2["batch1"]["frac"], "traffic": None},
                 "sweep": r, "gpu_launches": 8 * 2 * 3 * 8}

@@ -121,6 +121,9 @@ struct gx_context {
         uint8_t *peers[gx::kMaxPeers] = {};             // every rank's block, mapped here
         gx::EpBlock off{};
         unsigned epoch = 0;
+        uint64_t wait_ns = 2000000000ull;               // bound of the device-side flag waits
+        unsigned fault_skip_push = 0;                   // test hook: epoch whose push is not launched
+        uint32_t peer_layers = 0;                       // layer calls that took the peer exchange
         int *h_counts = nullptr;                        // pinned copy
         cudaEvent_t counts_ready = nullptr;
     } ep;
@@ -182,6 +185,9 @@ gx_result wait_event(gx_context *c, cudaEvent_t ev, uint32_t timeout_ms) {
     if (err != 0) {
         if (debug_enabled()) std::fprintf(stderr, "gyro_moe: kernel error word %d (1 = expired wait, 2 = bad expert id)\n", err);
         cudaMemset(c->err, 0, sizeof(int));
+        // an expired wait in an expert-parallel group means a peer fell out of step: the exchange
+        // epochs of the ranks no longer agree, so the context takes no further calls
+        if (c->world > 1 && err == gx::KERR_WAIT) c->broken = true;
         return GX_E_KERNEL;
     }
     return GX_OK;
@@ -610,7 +616,22 @@ gx_result ep_allgather(gx_context *c, const void *src, void *dst, size_t bytes, 
     return r == GX_E_TIMEOUT ? comm_result(c, ncclInProgress, what) : r;
 }
 
-// Sets up the exchange over peer memory (a collective, on the first expert-parallel layer): every
+// Releases this rank's exchange block and its mappings of the other ranks' blocks, after the
+// work queued on the stream (which may still use them) has finished.
+gx_result ep_peer_teardown(gx_context *c) {
+    auto &e = c->ep;
+    GX_CUDA(cudaStreamSynchronize(c->stream));
+    for (int p = 0; p < (int)c->world && p < gx::kMaxPeers; ++p)
+        if (e.peers[p] && p != (int)c->rank) cudaIpcCloseMemHandle(e.peers[p]);
+    for (auto &p : e.peers) p = nullptr;
+    if (e.block) cudaFree(e.block);
+    e.block = nullptr;
+    e.peer_state = 0;
+    return GX_OK;
+}
+
+// Sets up the exchange over peer memory (a collective, on the first expert-parallel layer, and
+// again when a later layer is wider than the blocks): every
 // rank allocates its block for T = max_tokens rows per source and the largest E and U uploaded,
 // shares it by CUDA IPC, and maps every other rank's block. Every rank takes the peer path only
 // if every rank could map every block and all agree on T, E, U; otherwise all keep the NCCL rows
@@ -709,22 +730,34 @@ gx_result ep_peer_setup(gx_context *c) {
 // wait for every source's rows, the expert phase on the rx region ([W][T] rows, empty ones carry
 // no slot), partial rows straight into the sources' ret regions, wait for every destination,
 // and the source sum.
-gx_result enqueue_layer_ep_peer(gx_context *c, const Layer &L, const void *x, int xb, uint32_t n_tok,
+gx_result enqueue_layer_ep_peer(gx_context *c, const Layer &L, const void *x, int xb, uint32_t n_tok, size_t S,
                                 const void *resid, uint32_t resid_dtype, void *out, uint32_t out_dtype, float norm_eps,
                                 cudaEvent_t *ev) {
     auto &e = c->ep;
     const int W = (int)c->world;
-    const size_t E = L.E, U = L.U, T = (size_t)e.T;
+    const size_t E = L.E, U = L.U, T = S;
+    // buffers of the expert phase first: growing them synchronises the device, which must not
+    // happen between this rank's push and the peers' waits for it
+    const size_t rows = (size_t)W * T;
+    {
+        const size_t cap = (size_t)W * e.T * U;
+        size_t want = rows * U;
+        if (c->pf.slots < want) want = std::min(cap, std::max(want, c->pf.slots + c->pf.slots / 2));
+        gx_result r0 = ensure_prefill(c, L, want);
+        if (r0 != GX_OK) return r0;
+    }
     gx::EpPeerArgs pa{};
     for (int p = 0; p < W; ++p) pa.peer[p] = e.peers[p];
     pa.off = e.off;
     pa.W = W;
     pa.rank = (int)c->rank;
-    pa.T = e.T;
+    pa.T = (int)T;
     pa.E = (int)E;
     pa.U = (int)U;
     pa.epoch = ++e.epoch;
+    pa.wait_ns = e.wait_ns;
     pa.err = c->err;
+    ++e.peer_layers;
     // the blocks are laid out for the largest E and U; a smaller layer uses the same offsets
     gx::EpPushArgs ps{};
     ps.p = pa;
@@ -737,12 +770,11 @@ gx_result enqueue_layer_ep_peer(gx_context *c, const Layer &L, const void *x, in
     ps.send_ids = e.send_ids;
     ps.send_w = e.send_w;
     ps.send_count = e.counts;
-    GX_CUDA(gx::launch_ep_push(ps, c->stream));
+    // GX_EP_FAULT_SKIP_PUSH=<n> (failure-detection tests): this rank does not send its rows of its
+    // n-th peer-exchange layer call, so its peers' bounded waits run out
+    if (pa.epoch != e.fault_skip_push) GX_CUDA(gx::launch_ep_push(ps, c->stream));
     GX_CUDA(gx::launch_ep_wait_rx(pa, c->stream));
     if (ev) GX_CUDA(record_phase(ev[1], c->stream));
-    const size_t rows = (size_t)W * T;
-    gx_result r = ensure_prefill(c, L, rows * U);
-    if (r != GX_OK) return r;
     auto &p = c->pf;
     gx::GroupArgs ga{};
     ga.ids = reinterpret_cast<const uint32_t *>(e.block + e.off.rx_ids);
@@ -833,14 +865,24 @@ gx_result enqueue_layer_ep(gx_context *c, const Layer &L, const void *x, uint32_
     gx_result r = ensure_ep_send(c, L);
     if (r != GX_OK) return r;
     auto &e = c->ep;
+    if (e.peer_state == 1 && ((int)L.E > e.pE || (int)L.U > e.pU)) {
+        // a layer wider than the blocks (uploaded after the set-up): every rank reaches this
+        // point in the same call, so all of them set the exchange up again at the new size
+        r = ep_peer_teardown(c);
+        if (r != GX_OK) return r;
+    }
     if (e.peer_state == 0) {
         r = ep_peer_setup(c);
         if (r != GX_OK) return r;
     }
-    const bool peer = e.peer_state == 1 && (int)L.E <= e.pE && (int)L.U <= e.pU;
+    const bool peer = e.peer_state == 1;
     const int xb = x_dtype == GX_BF16;
-    // send rows reserved per destination: the peer regions hold T rows per source
-    const size_t stride = peer ? (size_t)e.T : (n_tok ? n_tok : 1);
+    // send rows reserved per destination: with peer memory, the largest token count of any rank
+    // in this call (every rank knows all counts from ep_sync_ntok), the stride of the rx regions
+    size_t S = 1;
+    for (int v : e.src_ntok) S = std::max<size_t>(S, (size_t)v);
+    if ((int)e.src_ntok.size() != W || S > (size_t)c->max_tokens) return GX_E_STATE;
+    const size_t stride = peer ? S : (n_tok ? n_tok : 1);
     if (ev) GX_CUDA(record_phase(ev[0], c->stream));
     if (n_tok > 0) {
         int splits;
@@ -886,7 +928,7 @@ gx_result enqueue_layer_ep(gx_context *c, const Layer &L, const void *x, uint32_
     pa.block_count = e.block_count;
     pa.err = c->err;
     GX_CUDA(gx::launch_ep_plan(pa, c->stream));
-    if (peer) return enqueue_layer_ep_peer(c, L, x, xb, n_tok, resid, resid_dtype, out, out_dtype, norm_eps, ev);
+    if (peer) return enqueue_layer_ep_peer(c, L, x, xb, n_tok, S, resid, resid_dtype, out, out_dtype, norm_eps, ev);
     GX_CUDA(gx::launch_rotate_tokens(x, xb, norm_eps > 0.f ? c->xscale : nullptr, L.gate_signs, (int)n_tok, (int)E,
                                      e.send_rows, c->stream, e.pos_of, W));
     // every source sends its n_tok rows to every rank (rows without a slot there are empty)
@@ -1294,6 +1336,11 @@ GX_API gx_result gx_create(const gx_options *o, gx_context **out) {
         if (cudaMemset(c->router_done, 0, sizeof(unsigned)) != cudaSuccess) { r = GX_E_DEVICE; break; }
         r = ensure_scratch(c);
         if (r != GX_OK || c->world == 1) break;
+        if (const char *v = std::getenv("GX_EP_WAIT_MS")) {
+            const long ms = std::strtol(v, nullptr, 10);
+            if (ms > 0) c->ep.wait_ns = (uint64_t)ms * 1000000ull;
+        }
+        if (const char *v = std::getenv("GX_EP_FAULT_SKIP_PUSH")) c->ep.fault_skip_push = (unsigned)std::strtoul(v, nullptr, 10);
         r = open_group(c, o);
     } while (false);
     if (r != GX_OK) {
@@ -1328,6 +1375,7 @@ GX_API gx_result gx_get_caps(gx_context *c, gx_caps *caps) {
     for (auto &m : c->mats) caps->arena_bytes += (uint64_t)m.rows / 8 * (m.cols / 128) * gx::tile_bytes(m.type);
     std::strncpy(caps->device_name, prop.name, sizeof(caps->device_name) - 1);
     caps->ep_exchange = c->ep.peer_state == 1 ? GX_EP_PEER : c->ep.peer_state == -1 ? GX_EP_NCCL : GX_EP_NONE;
+    caps->ep_peer_layers = c->ep.peer_layers;
     return GX_OK;
 }
 

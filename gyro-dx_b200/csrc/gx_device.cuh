@@ -4,12 +4,10 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include "gx_internal.h"
 #include "gx_tile.h"
 
 namespace gx {
-
-// Error codes a kernel can leave in the context's device error word.
-enum : int { KERR_NONE = 0, KERR_WAIT = 1, KERR_BOUNDS = 2 };
 
 // Wall-clock bound of every mbarrier / flag wait: after this many nanoseconds the wait gives
 // up, records an error for the host, and the kernel returns.

@@ -186,7 +186,9 @@ cudaError_t launch_ep_combine(const EpCombineArgs &a, cudaStream_t s) {
 // A source writes only the rows a destination needs, straight into the destination's memory
 // (plain stores through the IPC mapping; no TMA and no multicast), and publishes them with a
 // release store of the epoch into the destination's flag word after a system-scope fence. The
-// destination acquires the flag before it reads. Every wait is bounded by kWaitLimitNs.
+// destination acquires the flag before it reads. Every wait is bounded (EpPeerArgs::wait_ns),
+// and a failure travels on: a rank whose receive failed publishes its return flags with
+// kFlagFailed, so no rank completes the call with another rank's rows missing.
 
 namespace {
 
@@ -199,15 +201,21 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
     return v;
 }
 
-// Bounded wait until *flag >= epoch; false (and KERR_WAIT) when the limit passes.
-__device__ bool wait_flag(const unsigned *flag, unsigned epoch, int *err) {
+// Bounded wait until the flag carries this epoch (or a later one); false (and KERR_WAIT) when the
+// limit passes or the peer published the epoch with kFlagFailed.
+__device__ bool wait_flag(const unsigned *flag, unsigned epoch, uint64_t wait_ns, int *err) {
     const uint64_t t0 = globaltimer_ns();
-    while (ld_acquire_sys(flag) < epoch) {
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    unsigned v;
+    while (((v = ld_acquire_sys(flag)) & ~kFlagFailed) < epoch) {
+        if (globaltimer_ns() - t0 > wait_ns) {
             atomicExch(err, KERR_WAIT);
             return false;
         }
         __nanosleep(64);
+    }
+    if (v & kFlagFailed) {
+        atomicExch(err, KERR_WAIT);
+        return false;
     }
     return true;
 }
@@ -269,20 +277,23 @@ __global__ void __launch_bounds__(256) ep_push_kernel(EpPushArgs a, int row_ctas
             }
         }
     } else {
-        // slot metadata: thread per (destination, position) of the used rows, grid-stride
-        const long long n_r = a.n_tok > 0 ? (long long)p.W * a.n_tok : 0;
+        // slot metadata: thread per (destination, position) of this call's T rows per source,
+        // grid-stride; rows past the destination's count carry no slot
+        const long long n_r = (long long)p.W * p.T;
         const long long step = (long long)(gridDim.x - row_ctas) * 256;
         for (long long r = (long long)(blockIdx.x - row_ctas) * 256 + threadIdx.x; r < n_r; r += step) {
-            const int d = (int)(r / a.n_tok), pos = (int)(r % a.n_tok);
+            const int d = (int)(r / p.T), pos = (int)(r % p.T);
+            const size_t src = ((size_t)d * p.T + pos) * p.U;
+            const size_t dst = ((size_t)p.rank * p.T + pos) * p.U;
+            uint32_t *ids = reinterpret_cast<uint32_t *>(p.peer[d] + p.off.rx_ids);
+            float *wts = reinterpret_cast<float *>(p.peer[d] + p.off.rx_w);
             if (pos < a.send_count[d]) {
-                const size_t src = ((size_t)d * p.T + pos) * p.U;
-                const size_t dst = ((size_t)p.rank * p.T + pos) * p.U;
-                uint32_t *ids = reinterpret_cast<uint32_t *>(p.peer[d] + p.off.rx_ids);
-                float *wts = reinterpret_cast<float *>(p.peer[d] + p.off.rx_w);
                 for (int k = 0; k < p.U; ++k) {
                     ids[dst + k] = a.send_ids[src + k];
                     wts[dst + k] = a.send_w[src + k];
                 }
+            } else {
+                for (int k = 0; k < p.U; ++k) ids[dst + k] = kNoSlot;
             }
         }
     }
@@ -296,20 +307,29 @@ __global__ void __launch_bounds__(256) ep_push_kernel(EpPushArgs a, int row_ctas
 }
 
 __global__ void __launch_bounds__(1024) ep_wait_rx_kernel(EpPeerArgs a) {
-    __shared__ int cnt[kMaxPeers];
+    __shared__ int failed[kMaxPeers];
+    __shared__ int any_failed;
     uint8_t *own = a.peer[a.rank];
+    if (threadIdx.x == 0) any_failed = 0;
+    __syncthreads();
     if (threadIdx.x < (unsigned)a.W) {
         const int s = threadIdx.x;
-        const bool ok = wait_flag(reinterpret_cast<const unsigned *>(own + a.off.rx_flag) + s, a.epoch, a.err);
-        const int c = *reinterpret_cast<volatile const int *>(own + a.off.rx_count + 4 * s);
-        cnt[s] = ok ? min(max(c, 0), a.T) : 0;
+        const bool ok = wait_flag(reinterpret_cast<const unsigned *>(own + a.off.rx_flag) + s, a.epoch, a.wait_ns, a.err);
+        failed[s] = !ok;
+        if (!ok) atomicExch(&any_failed, 1);
     }
     __syncthreads();
+    if (threadIdx.x == 0) *reinterpret_cast<volatile int *>(own + a.off.status) = any_failed;
+    if (!any_failed) return;
+    // the rows of a source that never published this call hold another call's slots: none of
+    // them takes part (the sources that did publish marked their own rows past the count)
+    int *cnt = reinterpret_cast<int *>(own + a.off.rx_count);
     uint32_t *ids = reinterpret_cast<uint32_t *>(own + a.off.rx_ids);
-    const long long n = (long long)a.W * a.T * a.U;
-    for (long long i = threadIdx.x; i < n; i += blockDim.x) {
-        const int s = (int)(i / ((long long)a.T * a.U)), row = (int)((i / a.U) % a.T);
-        if (row >= cnt[s]) ids[i] = kNoSlot;
+    for (int s = 0; s < a.W; ++s) {
+        if (!failed[s]) continue;
+        if (threadIdx.x == 0) cnt[s] = 0;
+        const long long n = (long long)a.T * a.U, base = (long long)s * a.T * a.U;
+        for (long long i = threadIdx.x; i < n; i += blockDim.x) ids[base + i] = kNoSlot;
     }
 }
 
@@ -320,7 +340,8 @@ __global__ void __launch_bounds__(256) ep_return_kernel(EpPeerArgs a, const __ha
     uint8_t *own = a.peer[a.rank];
     const int *cnt = reinterpret_cast<const int *>(own + a.off.rx_count);
     const float *rw = reinterpret_cast<const float *>(own + a.off.rx_w);
-    const long long n_r = (long long)a.W * a.T, step = (long long)gridDim.x * 8;
+    const bool failed = *reinterpret_cast<volatile const int *>(own + a.off.status) != 0;
+    const long long n_r = failed ? 0 : (long long)a.W * a.T, step = (long long)gridDim.x * 8;
     for (long long r = (long long)blockIdx.x * 8 + (threadIdx.x >> 5); r < n_r; r += step) {
         const int s = (int)(r / a.T), pos = (int)(r % a.T);
         if (pos >= min(cnt[s], a.T)) continue;  // the same for the whole warp
@@ -357,13 +378,15 @@ __global__ void __launch_bounds__(256) ep_return_kernel(EpPeerArgs a, const __ha
     unsigned *done = reinterpret_cast<unsigned *>(own + a.off.done) + 1;
     if (last_cta(done) && threadIdx.x < (unsigned)a.W) {
         __threadfence_system();
-        st_release_sys(reinterpret_cast<unsigned *>(a.peer[threadIdx.x] + a.off.ret_flag) + a.rank, a.epoch);
+        st_release_sys(reinterpret_cast<unsigned *>(a.peer[threadIdx.x] + a.off.ret_flag) + a.rank,
+                       a.epoch | (failed ? kFlagFailed : 0u));
     }
 }
 
 __global__ void ep_wait_ret_kernel(EpPeerArgs a) {
     if (threadIdx.x < (unsigned)a.W)
-        wait_flag(reinterpret_cast<const unsigned *>(a.peer[a.rank] + a.off.ret_flag) + threadIdx.x, a.epoch, a.err);
+        wait_flag(reinterpret_cast<const unsigned *>(a.peer[a.rank] + a.off.ret_flag) + threadIdx.x, a.epoch,
+                  a.wait_ns, a.err);
 }
 
 size_t align_up(size_t v) { return (v + 255) & ~(size_t)255; }
@@ -384,6 +407,7 @@ EpBlock ep_block_layout(int W, int T, int E, int U) {
     b.rx_flag = off; off = align_up(off + (size_t)W * 4);
     b.ret_flag = off; off = align_up(off + (size_t)W * 4);
     b.done = off; off = align_up(off + 8);
+    b.status = off; off = align_up(off + 4);
     b.bytes = off;
     return b;
 }
@@ -391,9 +415,10 @@ EpBlock ep_block_layout(int W, int T, int E, int U) {
 cudaError_t launch_ep_push(const EpPushArgs &a, cudaStream_t s) {
     if (a.p.W > kMaxPeers || a.p.W > 256) return cudaErrorInvalidValue;
     // grid-stride kernels: a bounded grid keeps the completion count (one atomic per CTA) small
+    if (a.n_tok > a.p.T || a.p.epoch == 0 || a.p.epoch >= kFlagFailed) return cudaErrorInvalidValue;
     const long long warps = (long long)a.n_tok * ((a.p.E / 128 + 3) / 4);
     const int row_ctas = (int)std::min<long long>((warps + 7) / 8, kPushRowCtas);
-    const int meta_ctas = (int)std::min<long long>(((long long)a.p.W * a.n_tok + 255) / 256, kPushMetaCtas);
+    const int meta_ctas = (int)std::min<long long>(((long long)a.p.W * a.p.T + 255) / 256, kPushMetaCtas);
     const int grid = row_ctas + meta_ctas > 0 ? row_ctas + meta_ctas : 1;
     ep_push_kernel<<<grid, 256, 0, s>>>(a, row_ctas);
     return cudaGetLastError();

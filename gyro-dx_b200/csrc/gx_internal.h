@@ -7,6 +7,9 @@
 
 namespace gx {
 
+// Error codes a kernel can leave in the context's device error word.
+enum : int { KERR_NONE = 0, KERR_WAIT = 1, KERR_BOUNDS = 2 };
+
 // Shared-memory codebook copies of the decode-GEMV kernels (2 banks per copy, so at most two
 // lanes of a warp contend for a bank during a lookup).
 constexpr int kCodebookCopies = 16;
@@ -219,28 +222,36 @@ struct EpCombineArgs {
 
 // ---- expert-parallel exchange over NVLink peer memory -------------------------------------
 // Every rank owns one exchange block, mapped into every other rank by CUDA IPC, laid out alike
-// on all ranks for W ranks, T rows per source and E, U of the largest layer:
+// on all ranks for W ranks, up to T rows per source and E, U of the largest layer:
 //   rx_rows [W src][T][E] f16 | rx_ids [W][T][U] | rx_w [W][T][U] | ret_rows [W dst][T][E] f16 |
-//   rx_count [W] | rx_flag [W] | ret_flag [W] | done [2]
-// A flag holds the epoch (layer call number) of the last completed transfer from that rank.
+//   rx_count [W] | rx_flag [W] | ret_flag [W] | done [2] | status [1]
+// A call uses the first S <= T rows of every source's region, S = the largest token count of any
+// rank in that call (every rank knows all counts), so the rows a call touches are [W][S]
+// contiguous. A flag holds the epoch (layer call number) of the last transfer from that rank;
+// kFlagFailed set beside the epoch means that rank's side of the exchange failed (an expired
+// wait), and the rank that reads it fails the call too instead of using the rows.
 constexpr int kMaxPeers = 16;
+constexpr unsigned kFlagFailed = 0x80000000u;
 
 struct EpBlock {
-    size_t rx_rows, rx_ids, rx_w, ret_rows, rx_count, rx_flag, ret_flag, done, bytes;
+    size_t rx_rows, rx_ids, rx_w, ret_rows, rx_count, rx_flag, ret_flag, done, status, bytes;
 };
 EpBlock ep_block_layout(int W, int T, int E, int U);
 
 struct EpPeerArgs {
     uint8_t *peer[kMaxPeers];  // every rank's exchange block in this process's address space
     EpBlock off;
-    int W, rank, T, E, U;
-    unsigned epoch;
+    int W, rank;
+    int T;                     // row stride of a source's region in this call (S above)
+    int E, U;
+    unsigned epoch;            // < kFlagFailed
+    uint64_t wait_ns;          // bound of every flag wait
     int *err;
 };
 
 // Rotated f16 rows of this rank's tokens straight into the destinations' rx regions (row
-// positions from the plan, stride T), the slot metadata beside them, then count + flag per
-// destination from the last CTA.
+// positions from the plan, stride T), the slot metadata beside them (rows [count, T) of every
+// destination marked kNoSlot), then count + flag per destination from the last CTA.
 struct EpPushArgs {
     EpPeerArgs p;
     const void *x;
@@ -255,13 +266,16 @@ struct EpPushArgs {
 
 cudaError_t launch_ep_plan(const EpPlanArgs &a, cudaStream_t s);
 cudaError_t launch_ep_push(const EpPushArgs &a, cudaStream_t s);
-// Waits (bounded) for every source's flag of this epoch, then marks rx rows past each source's
-// count as carrying no slot.
+// Waits (bounded) for every source's flag of this epoch. A source whose wait expires or whose
+// flag carries kFlagFailed gives KERR_WAIT, its rows are marked as carrying no slot, and the
+// block's status word records the failure for ep_return.
 cudaError_t launch_ep_wait_rx(const EpPeerArgs &a, cudaStream_t s);
 // Weighted sum of the U expert rows of every received row (Y, slot_row as the combine kernel)
-// written as f16 into the source's ret region, then a flag per source from the last CTA.
+// written as f16 into the source's ret region, then a flag per source from the last CTA. After a
+// failed receive it writes no rows and publishes the epoch with kFlagFailed, so every source
+// fails the call as well.
 cudaError_t launch_ep_return(const EpPeerArgs &a, const __half *Y, const int *slot_row, cudaStream_t s);
-// Waits (bounded) for every destination's return flag of this epoch.
+// Waits (bounded) for every destination's return flag of this epoch (kFlagFailed: KERR_WAIT).
 cudaError_t launch_ep_wait_ret(const EpPeerArgs &a, cudaStream_t s);
 cudaError_t launch_ep_combine(const EpCombineArgs &a, cudaStream_t s);
 cudaError_t launch_group(const GroupArgs &a, cudaStream_t s);

@@ -42,7 +42,7 @@ class Caps(ctypes.Structure):
                 ("cc_minor", ctypes.c_uint32), ("rank", ctypes.c_uint32), ("world", ctypes.c_uint32),
                 ("max_tokens", ctypes.c_uint32), ("max_layers", ctypes.c_uint32), ("hbm_bytes", ctypes.c_uint64),
                 ("free_bytes", ctypes.c_uint64), ("l2_bytes", ctypes.c_uint64), ("arena_bytes", ctypes.c_uint64),
-                ("device_name", ctypes.c_char * 120), ("ep_exchange", ctypes.c_uint32), ("reserved", ctypes.c_uint32)]
+                ("device_name", ctypes.c_char * 120), ("ep_exchange", ctypes.c_uint32), ("ep_peer_layers", ctypes.c_uint32)]
 
 
 class LayerDesc(ctypes.Structure):

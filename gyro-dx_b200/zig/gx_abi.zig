@@ -51,7 +51,7 @@ pub const gx_caps = extern struct {
     arena_bytes: u64,
     device_name: [120]u8,
     ep_exchange: u32,
-    reserved: u32,
+    ep_peer_layers: u32,
 };
 
 pub const gx_layer_desc = extern struct {

@@ -88,7 +88,7 @@ typedef struct gx_caps {
     char device_name[120];
     uint32_t ep_exchange;     /* expert-parallel rows: GX_EP_NONE until the first layer, then one of
                                  GX_EP_PEER (NVLink peer memory) or GX_EP_NCCL */
-    uint32_t reserved;
+    uint32_t ep_peer_layers;  /* layer calls so far whose rows crossed by NVLink peer memory */
 } gx_caps;                    /* 192 bytes */
 
 #define GX_EP_NONE 0u

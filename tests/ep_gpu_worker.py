@@ -75,6 +75,8 @@ def worker(rank: int, world: int, out_dir: str) -> None:
             x = tokens(i, rank, n_tok[rank], layer["n_embd"])
             y, ids, w = ctx.forward_host(0, x, want_routing=True)
             res[f"{name}_x"], res[f"{name}_y"], res[f"{name}_ids"] = x, y, ids
+            # which exchange this call took: the count of peer-memory layer calls so far
+            res[f"{name}_peer_layers"] = np.array(ctx.caps().ep_peer_layers)
         # a two-layer pre-norm stack, bf16 tokens in
         layers = [make(dict(seed=41 + l, n_expert=16, E=256, F=128, U=4)) for l in range(2)]
         for l, layer in enumerate(layers):
@@ -128,3 +130,54 @@ def worker(rank: int, world: int, out_dir: str) -> None:
     finally:
         del os.environ["GX_EP_NCCL"]
     np.savez(Path(out_dir) / f"rank{rank}.npz", **res)
+
+
+def fault_worker(rank: int, world: int, out_dir: str) -> None:
+    """Failure detection without a GPU fault: rank 0 does not send its rows for its first
+    peer-exchange layer call (the GX_EP_FAULT_SKIP_PUSH host hook), while staying alive with its
+    exchange block mapped. Rank 1's bounded wait for those rows runs out (GX_EP_WAIT_MS), rank 1
+    fails its return so rank 0 fails too, and both report GX_E_KERNEL instead of a result. The
+    contexts then refuse further calls and close cleanly."""
+    os.environ.setdefault("GX_COMM_TIMEOUT_MS", "30000")
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    os.environ["GX_EP_WAIT_MS"] = "300"
+    if rank == 0:
+        os.environ["GX_EP_FAULT_SKIP_PUSH"] = "1"
+    import torch
+    torch.cuda.set_device(rank)
+    from gyro_moe import abi
+
+    idf = Path(out_dir) / "nccl_id_fault"
+    if rank == 0:
+        tmp = idf.with_suffix(".tmp")
+        tmp.write_bytes(abi.unique_id())
+        tmp.rename(idf)
+    t0 = time.time()
+    while not idf.exists():
+        if time.time() - t0 > 60:
+            raise RuntimeError("no NCCL id from rank 0")
+        time.sleep(0.05)
+    res = {}
+    ctx = abi.Context(device=rank, max_tokens=64, max_layers=1, rank=rank, world=world, nccl_id=idf.read_bytes())
+    layer = make(dict(seed=51, n_expert=16, E=256, F=128, U=4))
+    ctx.upload_layer(0, layer)
+    x = tokens(50, rank, 20, 256)
+    t0 = time.time()
+    try:
+        ctx.forward_host(0, x, timeout_ms=20000)
+        res["first_rc"] = np.array(0)
+    except abi.GxError as e:
+        res["first_rc"] = np.array(e.code)
+    res["first_s"] = np.array(time.time() - t0)
+    try:
+        ctx.forward_host(0, x, timeout_ms=20000)
+        res["second_rc"] = np.array(0)
+    except abi.GxError as e:
+        res["second_rc"] = np.array(e.code)
+    res["exchange"] = np.array(ctx.caps().ep_exchange)
+    try:
+        ctx.close()
+        res["destroy_rc"] = np.array(0)
+    except abi.GxError as e:
+        res["destroy_rc"] = np.array(e.code)
+    np.savez(Path(out_dir) / f"fault{rank}.npz", **res)

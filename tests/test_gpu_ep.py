@@ -50,10 +50,39 @@ def test_group_caps(ranks):
 
 def test_exchange_kind(ranks):
     from gyro_moe import abi
+    import ep_gpu_worker
     for res in ranks:
         assert int(res["exchange"]) == abi.GX_EP_PEER
         assert int(res["nccl_exchange0"]) == abi.GX_EP_NONE
         assert int(res["nccl_exchange"]) == abi.GX_EP_NCCL
+        # every layer case took the peer exchange, the config-0 shape included although a
+        # narrower layer set the exchange up first
+        assert [int(res[f"{c[0]}_peer_layers"]) for c in ep_gpu_worker.CASES] == \
+            list(range(1, len(ep_gpu_worker.CASES) + 1))
+
+
+@pytest.fixture(scope="module")
+def fault(tmp_path_factory):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    import ep_gpu_worker
+    out = tmp_path_factory.mktemp("ep2fault")
+    mp.spawn(ep_gpu_worker.fault_worker, args=(2, str(out)), nprocs=2, join=True)
+    return [dict(np.load(out / f"fault{r}.npz")) for r in range(2)]
+
+
+def test_missing_rows_end_in_an_error_on_every_rank(fault):
+    """One rank skips its push: the peer's bounded device-side wait expires, the failure is passed
+    on through the return flags, both ranks report GX_E_KERNEL within seconds (not a result with
+    rows missing), later calls are refused, and both contexts close."""
+    from gyro_moe import abi
+    for res in fault:
+        assert int(res["exchange"]) == abi.GX_EP_PEER
+        assert int(res["first_rc"]) == -9
+        assert float(res["first_s"]) < 10.0
+        assert int(res["second_rc"]) == -4
+        assert int(res["destroy_rc"]) == 0
 
 
 @pytest.mark.parametrize("exchange", ["", "nccl_"])
