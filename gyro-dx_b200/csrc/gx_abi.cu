@@ -44,6 +44,12 @@ struct Layer {
     std::vector<uint32_t> replicas;
     int2 *route = nullptr;
     unsigned *expert_count = nullptr;
+    // shared expert (gx_upload_shared), in an arena of its own: W_Q8 or W_F16 matrices
+    uint32_t sh_wt = 0, SF = 0;
+    uint8_t *sh_arena = nullptr;
+    uint64_t sh_bytes = 0;
+    gx::SharedMat sh_gate{}, sh_up{}, sh_down{};
+    float *sh_gate_inp = nullptr;
 };
 
 // Copies of hot experts one expert-parallel rank can hold per layer, beside its own shard.
@@ -83,6 +89,17 @@ struct gx_context {
             *n_mtiles = nullptr;
         int *row_slot = nullptr, *slot_row = nullptr;
     } pf;
+    // shared-expert work buffers for max_tokens tokens of the widest shared expert uploaded:
+    // decode path (act, gated output term), tensor-core path (operand tiles, act, f16 rows, tile
+    // list), and the gate logits of both
+    struct Shared {
+        size_t E = 0, SF = 0;
+        float *logit = nullptr, *act = nullptr, *y = nullptr;
+        uint8_t *A = nullptr, *A2 = nullptr;
+        float *pact = nullptr;
+        __half *Ysh = nullptr;
+        int *ints = nullptr;  // tile_expert | tile_rows | n_mtiles
+    } sh;
     uint32_t *ids = nullptr;
     int *err = nullptr;
     void *x_stage = nullptr, *y_stage = nullptr;     // device staging (graphs, host calls)
@@ -276,7 +293,12 @@ void release_all(gx_context *c) {
         if (kv.second.first) cudaGraphDestroy(kv.second.first);
     }
     c->graphs.clear();
-    for (auto &l : c->layers) if (l.arena) cudaFree(l.arena);
+    for (auto &l : c->layers) {
+        if (l.arena) cudaFree(l.arena);
+        if (l.sh_arena) cudaFree(l.sh_arena);
+    }
+    void *sh[] = {c->sh.logit, c->sh.act, c->sh.y, c->sh.A, c->sh.A2, c->sh.pact, c->sh.Ysh, c->sh.ints};
+    for (void *p : sh) if (p) cudaFree(p);
     void *pf[] = {c->pf.A, c->pf.A2, c->pf.act, c->pf.Y, c->pf.ints, c->pf.xh};
     for (void *p : pf) if (p) cudaFree(p);
     for (auto &m : c->mats) if (m.tiles) cudaFree(m.tiles);
@@ -356,6 +378,133 @@ gx_result ensure_prefill(gx_context *c, const Layer &L, size_t slots) {
     return GX_OK;
 }
 
+// Work buffers of the shared expert for max_tokens tokens of shape (E, SF), grown only (any
+// captured stack is dropped, since it points at the old buffers).
+gx_result ensure_shared(gx_context *c, size_t E, size_t SF) {
+    auto &sh = c->sh;
+    if (sh.E >= E && sh.SF >= SF) return GX_OK;
+    E = std::max(E, sh.E);
+    SF = std::max(SF, sh.SF);
+    void *old[] = {sh.logit, sh.act, sh.y, sh.A, sh.A2, sh.pact, sh.Ysh, sh.ints};
+    for (void *q : old) if (q) cudaFree(q);
+    sh = gx_context::Shared{};
+    for (auto &kv : c->graphs) {
+        cudaGraphExecDestroy(kv.second.second);
+        cudaGraphDestroy(kv.second.first);
+    }
+    c->graphs.clear();
+    const size_t T = c->max_tokens, Td = std::min<size_t>(T, kPrefillMinTokens), tiles = (T + 127) / 128;
+    GX_CUDA(cudaMalloc(&sh.logit, T * sizeof(float)));
+    GX_CUDA(cudaMalloc(&sh.act, Td * SF * sizeof(float)));
+    GX_CUDA(cudaMalloc(&sh.y, Td * E * sizeof(float)));
+    if (T >= kPrefillMinTokens || c->world > 1) {
+        GX_CUDA(cudaMalloc(&sh.A, tiles * (E / 64) * 16384));
+        GX_CUDA(cudaMalloc(&sh.A2, tiles * (SF / 64) * 16384));
+        GX_CUDA(cudaMalloc(&sh.pact, tiles * 128 * SF * sizeof(float)));
+        GX_CUDA(cudaMalloc(&sh.Ysh, tiles * 128 * E * sizeof(__half)));
+        GX_CUDA(cudaMalloc(&sh.ints, (2 * tiles + 1) * sizeof(int)));
+    }
+    sh.E = E;
+    sh.SF = SF;
+    return GX_OK;
+}
+
+gx::SharedArgs shared_args(gx_context *c, const Layer &L, const void *x, int xb, uint32_t n_tok) {
+    gx::SharedArgs a{};
+    a.wt = L.sh_wt;
+    a.gate = L.sh_gate;
+    a.up = L.sh_up;
+    a.down = L.sh_down;
+    a.gate_inp = L.sh_gate_inp;
+    a.x = x;
+    a.x_bf16 = xb;
+    a.n_tok = (int)n_tok;
+    a.E = (int)L.E;
+    a.SF = (int)L.SF;
+    a.act = c->sh.act;
+    a.logit = c->sh.logit;
+    a.y = c->sh.y;
+    return a;
+}
+
+// Shared expert of a few-token call on the CUDA cores: act and gate logits, then the gated down
+// product into c->sh.y, which the routed down kernel adds. The token scale comes from the
+// router's sums of squares.
+gx_result enqueue_shared_decode(gx_context *c, const Layer &L, const void *x, int xb, uint32_t n_tok, float norm_eps,
+                                bool pdl) {
+    gx::SharedArgs a = shared_args(c, L, x, xb, n_tok);
+    a.ss = c->ss;
+    a.norm_eps = norm_eps;
+    GX_CUDA(gx::launch_shared_gate_up(a, c->stream, pdl));
+    GX_CUDA(gx::launch_shared_down(a, c->stream, pdl));
+    return GX_OK;
+}
+
+// Shared expert of a many-token call on the tensor cores: every token is a row of one "expert"
+// (tiles of 128 tokens in order), through the same grouped GEMM as the routed experts with the
+// Q8_0 / fp16 decoders, into f16 rows c->sh.Ysh; the gate logits into c->sh.logit. xscale: the
+// per-token scale the selection wrote.
+gx_result enqueue_shared_gemm(gx_context *c, const Layer &L, const void *x, int xb, uint32_t n_tok,
+                              const float *xscale) {
+    auto &sh = c->sh;
+    if (n_tok == 0) return GX_OK;
+    const int tiles = (int)((c->max_tokens + 127) / 128);
+    int *tile_expert = sh.ints, *tile_rows = sh.ints + tiles, *n_mtiles = sh.ints + 2 * tiles;
+    GX_CUDA(gx::launch_shared_tiles((int)n_tok, tile_expert, tile_rows, n_mtiles, c->stream));
+    gx::PackArgs pa{};
+    pa.src = x;
+    pa.src_bf16 = xb;
+    pa.by_token = 0;
+    pa.U = 1;
+    pa.K = (int)L.E;
+    pa.xscale = xscale;
+    pa.tile_rows = tile_rows;
+    pa.n_mtiles = n_mtiles;
+    pa.dst = sh.A;
+    GX_CUDA(gx::launch_pack_rows(pa, tiles, c->stream));
+    gx::GemmArgs gm{};
+    gm.type = L.sh_wt;
+    gm.w0 = L.sh_gate.w;
+    gm.w1 = L.sh_up.w;
+    gm.d0 = L.sh_gate.d;
+    gm.d1 = L.sh_up.d;
+    gm.K = (int)L.E;
+    gm.n_ntiles = (int)(L.SF / 128);
+    gm.n_expert = 1;
+    gm.A = sh.A;
+    gm.tile_expert = tile_expert;
+    gm.tile_rows = tile_rows;
+    gm.n_mtiles = n_mtiles;
+    gm.act = sh.pact;
+    gm.F = (int)L.SF;
+    gm.Y = sh.Ysh;
+    gm.E = (int)L.E;
+    gm.codebook = c->codebook;
+    gm.err = c->err;
+    GX_CUDA(gx::launch_moe_gemm(gm, 0, c->sm_count, c->stream));
+    gx::PackArgs pd{};
+    pd.src = sh.pact;
+    pd.by_token = 0;
+    pd.U = 1;
+    pd.K = (int)L.SF;
+    pd.tile_rows = tile_rows;
+    pd.n_mtiles = n_mtiles;
+    pd.dst = sh.A2;
+    GX_CUDA(gx::launch_pack_rows(pd, tiles, c->stream));
+    gm.w0 = L.sh_down.w;
+    gm.w1 = nullptr;
+    gm.d0 = L.sh_down.d;
+    gm.d1 = nullptr;
+    gm.K = (int)L.SF;
+    gm.n_ntiles = (int)(L.E / 256);
+    gm.A = sh.A2;
+    GX_CUDA(gx::launch_moe_gemm(gm, 1, c->sm_count, c->stream));
+    gx::SharedArgs a = shared_args(c, L, x, xb, n_tok);
+    a.xscale = xscale;
+    GX_CUDA(gx::launch_shared_logits(a, c->stream));
+    return GX_OK;
+}
+
 // Raw router logits of n_tok tokens into c->logits as *splits partial sums: on the tensor cores
 // when the layer carries its bf16 router parts, else the fp32 CUDA-core GEMM.
 cudaError_t launch_router_logits(gx_context *c, const Layer &L, const void *x, int xb, uint32_t n_tok, int *splits) {
@@ -402,6 +551,10 @@ gx_result enqueue_layer_prefill(gx_context *c, const Layer &L, const void *x, ui
     ra.weights = c->weights;
     ra.err = c->err;
     GX_CUDA(gx::launch_topk(ra, c->stream));
+    if (L.sh_wt) {
+        r = enqueue_shared_gemm(c, L, x, xb, n_tok, c->xscale);
+        if (r != GX_OK) return r;
+    }
     gx::GroupArgs ga{};
     ga.ids = c->ids;
     ga.n_slots = (int)(n_tok * L.U);
@@ -473,6 +626,8 @@ gx_result enqueue_layer_prefill(gx_context *c, const Layer &L, const void *x, ui
     ca.Y = p.Y;
     ca.slot_row = p.slot_row;
     ca.weights = c->weights;
+    ca.Ysh = L.sh_wt ? c->sh.Ysh : nullptr;
+    ca.sh_logit = c->sh.logit;
     ca.resid = resid;
     ca.resid_bf16 = resid_dtype == GX_BF16;
     ca.out = out;
@@ -843,6 +998,8 @@ gx_result enqueue_layer_ep_peer(gx_context *c, const Layer &L, const void *x, in
     ec.ret = reinterpret_cast<const __half *>(e.block + e.off.ret_rows);
     ec.pos_of = e.pos_of;
     ec.W = W;
+    ec.Ysh = L.sh_wt && n_tok ? c->sh.Ysh : nullptr;
+    ec.sh_logit = c->sh.logit;
     ec.resid = resid;
     ec.resid_bf16 = resid_dtype == GX_BF16;
     ec.out = out;
@@ -907,6 +1064,11 @@ gx_result enqueue_layer_ep(gx_context *c, const Layer &L, const void *x, uint32_
         ra.weights = c->weights;
         ra.err = c->err;
         GX_CUDA(gx::launch_topk(ra, c->stream));
+        if (L.sh_wt) {
+            // the shared expert is replicated: every rank computes it for its own tokens
+            r = enqueue_shared_gemm(c, L, x, xb, n_tok, c->xscale);
+            if (r != GX_OK) return r;
+        }
     }
     gx::EpPlanArgs pa{};
     pa.ids = c->ids;
@@ -1052,6 +1214,8 @@ gx_result enqueue_layer_ep(gx_context *c, const Layer &L, const void *x, uint32_
     ec.ret = e.ret_rows;
     ec.pos_of = e.pos_of;
     ec.W = W;
+    ec.Ysh = L.sh_wt && n_tok ? c->sh.Ysh : nullptr;
+    ec.sh_logit = c->sh.logit;
     ec.resid = resid;
     ec.resid_bf16 = resid_dtype == GX_BF16;
     ec.out = out;
@@ -1107,6 +1271,10 @@ gx_result enqueue_layer(gx_context *c, const Layer &L, const void *x, uint32_t x
     const bool pdl = ev == nullptr && chained;
     GX_CUDA(gx::launch_router(ra, c->stream, pdl, !fused && !sel_router));
     if (ev) GX_CUDA(record_phase(ev[1], c->stream));
+    if (L.sh_wt) {
+        gx_result r = enqueue_shared_decode(c, L, x, x_dtype == GX_BF16, n_tok, norm_eps, ev == nullptr);
+        if (r != GX_OK) return r;
+    }
 
     gx::GateUpArgs ga{};
     ga.type = L.type;
@@ -1149,6 +1317,7 @@ gx_result enqueue_layer(gx_context *c, const Layer &L, const void *x, uint32_t x
     da.weights = c->weights;
     da.resid = resid;
     da.resid_bf16 = resid_dtype == GX_BF16;
+    da.extra = L.sh_wt ? c->sh.y : nullptr;
     da.out = out;
     da.out_bf16 = out_dtype == GX_BF16;
     da.codebook = c->codebook;
@@ -1208,6 +1377,7 @@ bool stack_kernel_fits(gx_context *c, uint32_t first, uint32_t n_layers, uint32_
     for (uint32_t i = 0; i < n_layers; ++i) {
         const Layer &L = c->layers[first + i];
         if (L.type != L0.type || L.E != L0.E || L.F != L0.F || L.U != L0.U || L.n_expert != L0.n_expert) return false;
+        if (L.sh_wt) return false;  // the persistent kernel has no shared-expert phase
     }
     return L0.n_expert <= 4u * (uint32_t)c->sm_count &&
            gx::decode_stack_supported(L0.type, (int)L0.E, (int)L0.F, (int)L0.U, (int)L0.n_expert, (int)n_tok);
@@ -1371,7 +1541,7 @@ GX_API gx_result gx_get_caps(gx_context *c, gx_caps *caps) {
     caps->hbm_bytes = total_b;
     caps->free_bytes = free_b;
     caps->l2_bytes = (uint64_t)prop.l2CacheSize;
-    for (auto &l : c->layers) caps->arena_bytes += l.bytes;
+    for (auto &l : c->layers) caps->arena_bytes += l.bytes + l.sh_bytes;
     for (auto &m : c->mats) caps->arena_bytes += (uint64_t)m.rows / 8 * (m.cols / 128) * gx::tile_bytes(m.type);
     std::strncpy(caps->device_name, prop.name, sizeof(caps->device_name) - 1);
     caps->ep_exchange = c->ep.peer_state == 1 ? GX_EP_PEER : c->ep.peer_state == -1 ? GX_EP_NCCL : GX_EP_NONE;
@@ -1411,6 +1581,7 @@ GX_API gx_result gx_upload_layer(gx_context *c, uint32_t layer, const gx_layer_d
         gx_result r = sync_all(c, timeout_ms);
         if (r != GX_OK) return r;
         cudaFree(L.arena);
+        if (L.sh_arena) cudaFree(L.sh_arena);
         L = Layer{};
     }
     const uint64_t NEl = NE / c->world, first = c->rank * NEl;
@@ -1520,6 +1691,117 @@ GX_API gx_result gx_upload_layer(gx_context *c, uint32_t layer, const gx_layer_d
         cudaGraphDestroy(kv.second.first);
     }
     c->graphs.clear();
+    return GX_OK;
+}
+
+GX_API gx_result gx_upload_shared(gx_context *c, uint32_t layer, const gx_shared_desc *d, uint32_t timeout_ms) {
+    if (!c) return GX_E_INVALIDARG;
+    if (c->broken) return GX_E_DEVICE;
+    if (layer >= c->layers.size() || !c->layers[layer].ready) return GX_E_STATE;
+    Layer &L = c->layers[layer];
+    const uint64_t E = L.E;
+    uint64_t row_in = 0, row_sf = 0, SF = 0;
+    if (d) {
+        SF = d->n_ff;
+        if (SF == 0 || SF % 128 || SF > 4096 || !d->gate || !d->up || !d->down || !d->gate_inp) return GX_E_INVALIDARG;
+        if (d->type_id == GX_Q8_0) {
+            row_in = E / 32 * 34;
+            row_sf = SF / 32 * 34;
+        } else if (d->type_id == GX_BF16) {
+            row_in = E * 2;
+            row_sf = SF * 2;
+        } else if (d->type_id == GX_F32) {
+            row_in = E * 4;
+            row_sf = SF * 4;
+        } else {
+            return GX_E_INVALIDARG;
+        }
+        if (d->gate_bytes != SF * row_in || d->up_bytes != SF * row_in || d->down_bytes != E * row_sf)
+            return GX_E_INVALIDARG;
+        if (E % 256) return GX_E_UNSUPPORTED;
+    }
+    GX_CUDA(cudaSetDevice(c->device));
+    if (L.sh_arena) {
+        gx_result r = sync_all(c, timeout_ms);  // queued calls may still read the old matrices
+        if (r != GX_OK) return r;
+        cudaFree(L.sh_arena);
+    }
+    L.sh_arena = nullptr;
+    L.sh_wt = 0;
+    L.SF = 0;
+    L.sh_bytes = 0;
+    L.sh_gate = L.sh_up = L.sh_down = gx::SharedMat{};
+    L.sh_gate_inp = nullptr;
+    for (auto &kv : c->graphs) {  // captured stacks of this layer ran without (or with the old) shared expert
+        cudaGraphExecDestroy(kv.second.second);
+        cudaGraphDestroy(kv.second.first);
+    }
+    c->graphs.clear();
+    if (!d) return GX_OK;
+
+    // Device encodings: Q8_0 split into int8 weights and fp16 block scales; bf16 and f32 as fp16.
+    const bool q8 = d->type_id == GX_Q8_0;
+    struct Mat { const uint8_t *src; uint64_t rows, cols, row_bytes; };
+    const Mat mats[3] = {{static_cast<const uint8_t *>(d->gate), SF, E, row_in},
+                         {static_cast<const uint8_t *>(d->up), SF, E, row_in},
+                         {static_cast<const uint8_t *>(d->down), E, SF, row_sf}};
+    uint64_t off = 0, o_w[3], o_d[3];
+    for (int m = 0; m < 3; ++m) {
+        o_w[m] = off;
+        off = align256(off + mats[m].rows * mats[m].cols * (q8 ? 1 : 2));
+        o_d[m] = off;
+        off = align256(off + (q8 ? mats[m].rows * (mats[m].cols / 32) * 2 : 0));
+    }
+    const uint64_t o_gi = off;
+    off = align256(off + E * 4);
+    std::vector<uint8_t> host(off, 0);
+    for (int m = 0; m < 3; ++m) {
+        const Mat &M = mats[m];
+        for (uint64_t r = 0; r < M.rows; ++r) {
+            const uint8_t *row = M.src + r * M.row_bytes;
+            if (q8) {
+                int8_t *w = reinterpret_cast<int8_t *>(host.data() + o_w[m]) + r * M.cols;
+                uint16_t *sc = reinterpret_cast<uint16_t *>(host.data() + o_d[m]) + r * (M.cols / 32);
+                for (uint64_t b = 0; b < M.cols / 32; ++b) {
+                    std::memcpy(&sc[b], row + 34 * b, 2);
+                    std::memcpy(&w[32 * b], row + 34 * b + 2, 32);
+                }
+            } else {
+                __half *w = reinterpret_cast<__half *>(host.data() + o_w[m]) + r * M.cols;
+                for (uint64_t i = 0; i < M.cols; ++i) {
+                    float v;
+                    if (d->type_id == GX_BF16) {
+                        uint32_t bits = (uint32_t)row[2 * i] | ((uint32_t)row[2 * i + 1] << 8);
+                        bits <<= 16;
+                        std::memcpy(&v, &bits, 4);
+                    } else {
+                        std::memcpy(&v, row + 4 * i, 4);
+                    }
+                    w[i] = __float2half_rn(v);
+                }
+            }
+        }
+    }
+    std::memcpy(host.data() + o_gi, d->gate_inp, E * 4);
+    gx_result r = ensure_shared(c, E, SF);
+    if (r != GX_OK) return r;
+    uint8_t *arena = nullptr;
+    GX_CUDA(cudaMalloc(&arena, off));
+    cudaError_t e = cudaMemcpy(arena, host.data(), off, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(arena);
+        return fail_cuda(c, e);
+    }
+    L.sh_arena = arena;
+    L.sh_bytes = off;
+    L.sh_wt = q8 ? gx::W_Q8 : gx::W_F16;
+    L.SF = (uint32_t)SF;
+    gx::SharedMat *dst[3] = {&L.sh_gate, &L.sh_up, &L.sh_down};
+    for (int m = 0; m < 3; ++m) {
+        dst[m]->w = arena + o_w[m];
+        dst[m]->d = q8 ? reinterpret_cast<const __half *>(arena + o_d[m]) : nullptr;
+    }
+    L.sh_gate_inp = reinterpret_cast<float *>(arena + o_gi);
     return GX_OK;
 }
 
@@ -1766,9 +2048,12 @@ GX_API gx_result gx_upload_matrix(gx_context *c, uint32_t type_id, uint32_t rows
     if (packed_bytes != row_bytes * rows) return GX_E_INVALIDARG;
     if (c->broken) return GX_E_DEVICE;
     GX_CUDA(cudaSetDevice(c->device));
+    // the GEMV takes rows 16 at a time: an odd count of 8-row groups gets a zero group after it
+    const uint64_t pad = rows % 16 ? (uint64_t)gx::tile_bytes(type_id) * (cols / 128) : 0;
     uint8_t *raw = nullptr, *tiles = nullptr;
-    GX_CUDA(cudaMalloc(&tiles, packed_bytes));
+    GX_CUDA(cudaMalloc(&tiles, packed_bytes + pad));
     cudaError_t e = cudaMalloc(&raw, packed_bytes);
+    if (e == cudaSuccess && pad) e = cudaMemsetAsync(tiles + packed_bytes, 0, pad, c->stream);
     if (e == cudaSuccess) e = cudaMemcpyAsync(raw, packed, packed_bytes, cudaMemcpyHostToDevice, c->stream);
     if (e == cudaSuccess) e = gx::launch_repack(type_id, raw, row_bytes, rows, cols, tiles, c->stream);
     gx_result r = e == cudaSuccess ? sync_all(c, timeout_ms) : fail_cuda(c, e);
@@ -1927,6 +2212,7 @@ GX_API gx_result gx_moe_forward_noalloc(gx_context *c, uint32_t layer, const voi
         return GX_E_INVALIDARG;
     const Layer &L = c->layers[layer];
     if (L.n_expert > 512 || L.U > 16 || (uint64_t)L.U * L.F > 64 * 128) return GX_E_INVALIDARG;
+    if (L.sh_wt) return GX_E_UNSUPPORTED;  // its scratch holds no shared-expert buffers
     GX_CUDA(cudaSetDevice(c->device));
     uint8_t *base = nullptr;
     gx_result r = noalloc_scratch(c, &base);

@@ -138,7 +138,8 @@ __global__ void __launch_bounds__(kPlanTok) ep_plan_place_kernel(EpPlanArgs a) {
         }
 }
 
-// out[t] = resid[t] + sum over destinations of the returned partial row of (t, d).
+// out[t] = resid[t] + sum over destinations of the returned partial row of (t, d) (+ the gated
+// shared-expert row of t).
 __global__ void __launch_bounds__(256) ep_combine_kernel(EpCombineArgs a) {
     const long long i = (long long)blockIdx.x * 256 + threadIdx.x;
     const int per_row = a.E / 4;
@@ -155,6 +156,17 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(EpCombineArgs a) {
         v[1] += f0.y;
         v[2] += f1.x;
         v[3] += f1.y;
+    }
+    if (a.Ysh) {
+        // this rank's shared expert for its own token, with its sigmoid gate (src/engine.zig:649-652)
+        const float g = 1.0f / (1.0f + expf(-a.sh_logit[t]));
+        const uint2 q = *reinterpret_cast<const uint2 *>(a.Ysh + (size_t)t * a.E + c);
+        const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&q.x));
+        const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(&q.y));
+        v[0] += f0.x * g;
+        v[1] += f0.y * g;
+        v[2] += f1.x * g;
+        v[3] += f1.y * g;
     }
     const size_t o = (size_t)t * a.E + c;
 #pragma unroll

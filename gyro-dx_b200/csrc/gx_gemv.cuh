@@ -8,6 +8,59 @@
 
 namespace gx {
 
+// ---- codebook lookups by byte offset -------------------------------------------------------
+// prmt.b32 in its default mode: a selector nibble with bit 3 set replicates the sign bit of the
+// chosen byte, which yields a zero byte from a byte below 0x80.
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+
+// Byte offsets into a Codebook<NC> array of the two codebook pairs of each of the 8 chunks of a
+// lane's quarter (the values quarter_indices computes, as offsets): o0[c] for weights
+// 32q + 4c + {0,1}, o1[c] for 32q + 4c + {2,3}. lane_off = 4 * (the lane's copy). The index of a
+// pair times 4 * NC is taken straight from the hash by one shift and one masked OR (the copy
+// offset lies below the index bits), so a lookup costs two integer operations and the load.
+// TQ2_T builds each 15-bit state with one prmt from the run and a copy whose bytes have bit 7
+// cleared (the previous byte's high bit is not part of the state, the sign bytes are zero).
+template <uint32_t T, int NC>
+__device__ __forceinline__ void quarter_offsets(const uint32_t own[4], uint32_t nb, uint32_t lane_off, uint32_t (&o0)[8],
+                                                uint32_t (&o1)[8]) {
+    constexpr int SH = NC == 16 ? 6 : NC == 8 ? 5 : NC == 4 ? 4 : -1;
+    static_assert(SH > 0, "codebook copies: 4, 8 or 16");
+    constexpr uint32_t M = 2047u << SH;
+    auto offsets = [&](uint32_t s15, uint32_t &a, uint32_t &b) {
+        const uint32_t h = s15 * 0x9e3779b1u;
+        a = ((h >> (21 - SH)) & M) | lane_off;
+        b = ((h >> (10 - SH)) & M) | lane_off;
+    };
+    if constexpr (T == T_TQ2_T) {
+        const uint32_t m0 = own[0] & 0x7f7f7f7fu, m1 = own[1] & 0x7f7f7f7fu, mn = nb & 0x7fu;
+        // step c: this byte (low) and the byte before it (high, bit 7 cleared), upper bytes zero
+        offsets(prmt(own[0], mn, 0x5540u), o0[0], o1[0]);
+        offsets(prmt(own[0], m0, 0xcc41u), o0[1], o1[1]);
+        offsets(prmt(own[0], m0, 0xdd52u), o0[2], o1[2]);
+        offsets(prmt(own[0], m0, 0xee63u), o0[3], o1[3]);
+        offsets(prmt(own[1], m0, 0xff70u), o0[4], o1[4]);
+        offsets(prmt(own[1], m1, 0xcc41u), o0[5], o1[5]);
+        offsets(prmt(own[1], m1, 0xdd52u), o0[6], o1[6]);
+        offsets(prmt(own[1], m1, 0xee63u), o0[7], o1[7]);
+    } else {
+        uint32_t i0[8], i1[8];
+        quarter_indices<T>(own, nb, i0, i1);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            o0[c] = (i0[c] << SH) | lane_off;
+            o1[c] = (i1[c] << SH) | lane_off;
+        }
+    }
+}
+
+__device__ __forceinline__ uint32_t lds_u32(const uint8_t *base, uint32_t off) {
+    return *reinterpret_cast<const uint32_t *>(base + off);
+}
+
 // One 8-row x 128-column tile against NG groups of 8 tokens. acc[g][0..1] accumulates, for
 // token (8g + lane/4), rows 2*(lane%4) and 2*(lane%4)+1 of the tile (scaled by d).
 template <uint32_t T, int NG, int NC>

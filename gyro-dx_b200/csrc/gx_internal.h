@@ -69,6 +69,43 @@ struct GateUpArgs {
 // Whether gate_up_kernel can select experts itself for n_tok tokens (at most 8 tokens per CTA).
 bool gate_up_fuses_topk(int E, int F, int U, int n_tok, int sm_count);
 
+// ---- the shared expert of a layer (src/engine.zig:644-653) -----------------------------------
+// Device encodings of its three plain row-major matrices: Q8_0 split into int8 weights
+// [rows][cols] and fp16 block scales [rows][cols/32] (one per 32 weights), or fp16 weights
+// [rows][cols] (bf16 and f32 matrices are converted at upload). The values double as the
+// weight "type" of moe_gemm_kernel's shared-expert decoders; they are not Gyro type ids.
+enum : uint32_t { W_F16 = 1, W_Q8 = 8 };
+
+struct SharedMat {
+    const uint8_t *w;        // int8 (W_Q8) or fp16 (W_F16) weights [rows][cols]
+    const __half *d;         // W_Q8: fp16 scales [rows][cols/32]; nullptr for W_F16
+};
+
+// Decode path (few tokens, CUDA cores): act = silu(Gate x) * Up x and the gate logits, then
+// y = sigmoid(logit) * Down act, an f32 [n_tok][E] term the routed down kernel adds.
+struct SharedArgs {
+    uint32_t wt;             // W_Q8 or W_F16
+    SharedMat gate, up, down;
+    const float *gate_inp;   // [E] f32
+    const void *x;           // [n_tok][E] layer input (unrotated)
+    int x_bf16;
+    // RMSNorm scale of token t: xscale[t] when given, else 1/sqrt(ss[t]/E + norm_eps) when
+    // norm_eps > 0 (ss from the router), else 1
+    const float *xscale;
+    const float *ss;
+    float norm_eps;
+    int n_tok, E, SF;
+    float *act;              // [n_tok][SF]
+    float *logit;            // [n_tok] gate_inp . (x * xscale)
+    float *y;                // [n_tok][E]
+};
+cudaError_t launch_shared_gate_up(const SharedArgs &a, cudaStream_t s, bool pdl);
+cudaError_t launch_shared_down(const SharedArgs &a, cudaStream_t s, bool pdl);
+// Only the gate logits (the tensor-core path computes the rest with moe_gemm_kernel).
+cudaError_t launch_shared_logits(const SharedArgs &a, cudaStream_t s);
+// Tile list of the shared expert on the tensor-core path: every token in order, 128 per tile.
+cudaError_t launch_shared_tiles(int n_tok, int *tile_expert, int *tile_rows, int *n_mtiles, cudaStream_t s);
+
 struct DownArgs {
     uint32_t type;
     const uint8_t *down;     // tiles of local expert 0
@@ -79,6 +116,7 @@ struct DownArgs {
     const float *weights;    // [n_tok][U]
     const void *resid;       // [n_tok][E] or nullptr (residual added to the output)
     int resid_bf16;
+    const float *extra;      // [n_tok][E] or nullptr: the gated shared-expert term, added too
     void *out;               // [n_tok][E]
     int out_bf16;
     const uint32_t *codebook;
@@ -105,7 +143,7 @@ struct PackArgs {
     const void *src;         // by_token: x [n_tok][K]; else act [padded rows][K]
     int src_bf16;
     int by_token, U, K;
-    const float *xscale;     // [n_tok] or nullptr (transform mode only)
+    const float *xscale;     // by_token: [n_tok] per-token scale; else [padded rows] row scale, or nullptr
     const __half *xh;        // by_token: rotated f16 token rows [n_tok][K] (rotate_tokens)
     const float *signs;      // [K] or nullptr (then no Hadamard transform)
     const int *row_slot, *tile_rows, *n_mtiles;
@@ -113,8 +151,9 @@ struct PackArgs {
 };
 
 struct GemmArgs {
-    uint32_t type;
+    uint32_t type;           // Gyro type id, or W_Q8 / W_F16 for the shared expert's matrices
     const uint8_t *w0, *w1;  // gate + up (mode 0) or down (mode 1) tiles of local expert 0
+    const __half *d0, *d1;   // W_Q8: block scales of w0 / w1
     uint64_t expert_bytes;   // tiles of one projection of one expert
     int K, n_ntiles, n_expert;
     const uint8_t *A;        // packed operand tiles [tile][K/64][16384]
@@ -131,6 +170,8 @@ struct CombineArgs {
     const __half *Y;
     const int *slot_row;
     const float *weights;
+    const __half *Ysh;       // [n_tok][E] shared-expert rows, or nullptr
+    const float *sh_logit;   // [n_tok] their gate logits (added as sigmoid(logit) * Ysh)
     const void *resid;
     int resid_bf16;
     void *out;
@@ -213,6 +254,8 @@ struct EpCombineArgs {
     const __half *ret;       // returned partial rows, laid out as the send buffer
     const int *pos_of;       // [n_tok][W]
     int W;
+    const __half *Ysh;       // [n_tok][E] this rank's shared-expert rows, or nullptr
+    const float *sh_logit;   // [n_tok]
     const void *resid;       // [n_tok][E] or nullptr
     int resid_bf16;
     void *out;               // [n_tok][E]

@@ -10,7 +10,7 @@
 //   down_kernel        per token: down-input signs + FWHT prologue (:606), fused decode + down
 //                      GEMV for all U slots, weighted combine (+ residual) epilogue
 //                      (:608-641; moe.hlsl proj 2 + moe_combine:292-305)
-//   matvec_kernel      standalone decode GEMV of one matrix for up to 16 tokens
+//   matvec_kernel      standalone decode GEMV of one matrix, a warp per 16-row unit, up to 16 tokens
 //   decode_blocks_kernel  strict per-weight decode, bit-exact conformance (gyro_decode.hlsl)
 //   repack_kernel      reference block layout -> HBM tile layout (gx_tile.h)
 //
@@ -22,6 +22,8 @@
 // about 22 bits of the fp32 activation while the weights are exact.
 #include <cuda_runtime.h>
 #include <math.h>
+
+#include <algorithm>
 
 #define GX_TRACE_OWNER
 #include "gx_device.cuh"
@@ -765,6 +767,7 @@ __global__ void __launch_bounds__(512, 1) down_kernel(DownArgs a, int P) {
                 v += wsm[j * 16 + k] * dk;
             }
             const size_t o = (size_t)t * a.E + row;
+            if (a.extra) v += a.extra[o];
             if (a.resid) v = load_act(a.resid, a.resid_bf16, o) + v;
             if (a.out_bf16)
                 reinterpret_cast<__nv_bfloat16 *>(a.out)[o] = __float2bfloat16_rn(v);
@@ -776,126 +779,135 @@ __global__ void __launch_bounds__(512, 1) down_kernel(DownArgs a, int P) {
     GX_TRACE_POINT(6);
 }
 
-// ---- standalone matvec: unit = RG row groups; up to 16 tokens (2 groups of 8) -----------
-template <uint32_t T, int KBW, int NG, int NC>
-__global__ void __launch_bounds__(512, 1) matvec_kernel(MatvecArgs a, int t0, int P) {
+// ---- standalone matvec: one warp per 16-row unit across all column blocks -----------------
+// The weights are the MMA's A operand (m16n8k16: rows g and g+8 of a lane are the same row of
+// two consecutive 8-row tiles, so a lane decodes one quarter of two rows) and the activations
+// the B operand: the token dimension n holds (token, hi/lo part) pairs, four tokens per MMA
+// group. Every warp streams its own units with the next blocks' codes loaded into registers two
+// blocks ahead (no shared-memory staging, no barriers, no cross-warp reduction); shared memory
+// holds the codebook copies and the activations in B-fragment order.
+template <uint32_t T>
+struct TileCodes {
+    uint32_t own0[4], own1[4];   // the lane's run in the unit's two tiles
+    uint32_t sc;                 // scales of row g in the two tiles (low / high half)
+};
+
+template <uint32_t T>
+__device__ __forceinline__ void load_codes(const uint8_t *t0, const uint8_t *t1, int lane, TileCodes<T> &c) {
+    load_run<T>(t0, lane, c.own0);
+    load_run<T>(t1, lane, c.own1);
+    const int g = lane >> 2;
+    const uint32_t s0 = *reinterpret_cast<const uint16_t *>(t0 + tile_code_bytes(T) + 2 * g);
+    const uint32_t s1 = *reinterpret_cast<const uint16_t *>(t1 + tile_code_bytes(T) + 2 * g);
+    c.sc = s0 | (s1 << 16);
+}
+
+template <uint32_t T, int NG, int NC, int THREADS>
+__global__ void __launch_bounds__(THREADS, 1) matvec_kernel(MatvecArgs a, int t0) {
     using CB = Codebook<NC>;
-    GX_TRACE_START(3);
     constexpr int TB = tile_bytes(T);
     extern __shared__ __align__(128) uint8_t smem[];
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int NB = a.cols >> 7;
-    const int WB = NB < 16 ? NB : 16;
-    const int RG = 16 / WB;
-    const int NT = a.rows >> 3;
-    const int n_units = (NT + RG - 1) / RG;
-    const int unit_bytes = RG * NB * TB;
-    const int stage_bytes = P * unit_bytes;
-    const int ntok = min(16, a.n_tok - t0);
-
     uint32_t *cb = reinterpret_cast<uint32_t *>(smem);
-    uint8_t *stage = smem + CB::BYTES;
-    float *part = reinterpret_cast<float *>(stage + 2 * stage_bytes);  // [P][16 warps][16 tok][8]
-    uint64_t *bar = reinterpret_cast<uint64_t *>(part + P * 16 * 16 * 8);
+    uint2 *xf = reinterpret_cast<uint2 *>(smem + CB::BYTES);   // [block][chunk][group][lane]
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, q = lane & 3;
+    const int NB = a.cols >> 7;
+    const int ntok = min(4 * NG, a.n_tok - t0);
+    GX_TRACE_START(3);
 
-    StageCtl ctl;
-    ctl.bar = bar;
-    ctl.P = P;
-    ctl.u0 = (int)((long long)blockIdx.x * n_units / gridDim.x);
-    ctl.u1 = (int)((long long)(blockIdx.x + 1) * n_units / gridDim.x);
-    ctl.n_stages = (ctl.u1 - ctl.u0 + P - 1) / P;
-    if (tid == 0) {
-        mbar_init(&bar[0], 1);
-        mbar_init(&bar[1], 1);
-        fence_barrier_init();
-    }
-    __syncthreads();
-    auto issue = [&](int s) {
-        uint8_t *buf = stage + (s & 1) * stage_bytes;
-        const int ua = ctl.u0 + s * P, ub = min(ua + P, ctl.u1);
-        if (lane == 0) {
-            uint32_t total = 0;
-            for (int u = ua; u < ub; ++u) total += (uint32_t)(min(RG, NT - u * RG) * NB * TB);
-            mbar_expect_tx(&bar[s & 1], total);
-        }
-        __syncwarp();
-        for (int u = ua + lane; u < ub; u += 32)
-            bulk_g2s(buf + (u - ua) * unit_bytes, a.tiles + (uint64_t)u * unit_bytes,
-                     (uint32_t)(min(RG, NT - u * RG) * NB * TB), &bar[s & 1]);
-    };
-    if (warp == 0) {
-        if (ctl.n_stages > 0) issue(0);
-        if (ctl.n_stages > 1) issue(1);
-    }
     CB::stage(cb, a.codebook, tid, blockDim.x);
-
-    const bool active = warp < WB * RG;
-    const int kcol = warp % WB, rg = warp / WB;
-    const uint32_t copy_off = CB::copy_off(lane);
-    // A fragments straight from global x: lane (g, q) holds token 8*grp + g.
-    uint32_t A[KBW][NG][8][4];
-#pragma unroll
-    for (int j = 0; j < KBW; ++j)
-#pragma unroll
-        for (int grp = 0; grp < NG; ++grp) {
-            const int b = kcol + WB * j;
-            const int tok = 8 * grp + (lane >> 2), q = lane & 3;
-#pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                if (active && b < NB && tok < ntok) {
-                    const float4 xv = *reinterpret_cast<const float4 *>(a.x + (size_t)(t0 + tok) * a.cols + b * 128 +
-                                                                        32 * q + 4 * c);
-                    float h0, l0, h1, l1, h2, l2, h3, l3;
-                    split_hilo(xv.x, h0, l0);
-                    split_hilo(xv.y, h1, l1);
-                    split_hilo(xv.z, h2, l2);
-                    split_hilo(xv.w, h3, l3);
-                    A[j][grp][c][0] = pack_half2(h0, h1);
-                    A[j][grp][c][1] = pack_half2(l0, l1);
-                    A[j][grp][c][2] = pack_half2(h2, h3);
-                    A[j][grp][c][3] = pack_half2(l2, l3);
-                } else {
-                    A[j][grp][c][0] = A[j][grp][c][1] = A[j][grp][c][2] = A[j][grp][c][3] = 0u;
-                }
-            }
+    // Activation fragments: lane (g, q) of group ng carries token 4ng + g/2, part g%2 (hi or lo
+    // fp16 half of the f32 value) at columns 32q + 4c + {0,1} (b0) and {2,3} (b1).
+    for (int i = tid; i < NB * 8 * NG * 32; i += blockDim.x) {
+        const int ln = i & 31, ng = (i >> 5) % NG, c = (i / (32 * NG)) & 7, b = i / (256 * NG);
+        const int tok = 4 * ng + ((ln >> 2) >> 1), part = (ln >> 2) & 1, qq = ln & 3;
+        uint2 v = make_uint2(0u, 0u);
+        if (tok < ntok) {
+            const float4 x4 = *reinterpret_cast<const float4 *>(a.x + (size_t)(t0 + tok) * a.cols + b * 128 + 32 * qq + 4 * c);
+            float h0, l0, h1, l1, h2, l2, h3, l3;
+            split_hilo(x4.x, h0, l0);
+            split_hilo(x4.y, h1, l1);
+            split_hilo(x4.z, h2, l2);
+            split_hilo(x4.w, h3, l3);
+            v.x = part ? pack_half2(l0, l1) : pack_half2(h0, h1);
+            v.y = part ? pack_half2(l2, l3) : pack_half2(h2, h3);
         }
+        xf[i] = v;
+    }
     __syncthreads();
 
-    for (int s = 0; s < ctl.n_stages; ++s) {
-        if (!stage_wait(ctl, s, a.err)) return;
-        const int ua = ctl.u0 + s * P, ub = min(ua + P, ctl.u1);
-        const uint8_t *buf = stage + (s & 1) * stage_bytes;
-        for (int u = ua; u < ub; ++u) {
-            const int nt = min(RG, NT - u * RG);
-            if (active && rg < nt) {
-                float acc[NG][2];
+    const int n_units = (a.rows + 15) >> 4;     // the tiles hold a zero row group past an odd count
+    const int wid = blockIdx.x * (blockDim.x >> 5) + warp, nw = gridDim.x * (blockDim.x >> 5);
+    const int n_mine = wid < n_units ? (n_units - 1 - wid) / nw + 1 : 0;
+    const int steps = n_mine * NB;            // (unit, block) pairs of this warp, in order
+    const uint32_t lane_off = 4u * CB::copy_off(lane);
+    const uint8_t *cbb = smem;
+    const int nbr = (lane & ~3) | ((lane + 3) & 3);
+    // (unit, block) positions advance by counting, no division in the loop: the prefetch runs two
+    // steps ahead of the step being decoded
+    const size_t unit_stride = (size_t)2 * NB * TB;      // bytes of one 16-row unit
+    const uint8_t *pf_unit = a.tiles + (size_t)wid * unit_stride;
+    int pf_b = 0;
+    auto prefetch = [&](TileCodes<T> &dst) {
+        load_codes<T>(pf_unit + (size_t)pf_b * TB, pf_unit + (size_t)(NB + pf_b) * TB, lane, dst);
+        if (++pf_b == NB) {
+            pf_b = 0;
+            pf_unit += (size_t)nw * unit_stride;
+        }
+    };
+    TileCodes<T> nx0, nx1;
+    if (steps > 0) prefetch(nx0);
+    if (steps > 1) prefetch(nx1);
+    float acc[NG][2];
 #pragma unroll
-                for (int grp = 0; grp < NG; ++grp) acc[grp][0] = acc[grp][1] = 0.f;
+    for (int ng = 0; ng < NG; ++ng) acc[ng][0] = acc[ng][1] = 0.f;
+    bool xon[NG];                             // lanes whose (token, part) is live load activations
 #pragma unroll
-                for (int j = 0; j < KBW; ++j) {
-                    const int b = kcol + WB * j;
-                    if (b < NB) tile_mma<T, NG, NC>(buf + (u - ua) * unit_bytes + (rg * NB + b) * TB, cb, copy_off, lane, A[j], acc);
-                }
+    for (int ng = 0; ng < NG; ++ng) xon[ng] = 4 * ng + (g >> 1) < ntok;
+    int b = 0, u = wid;
+    for (int step = 0; step < steps; ++step) {
+        const TileCodes<T> cur = nx0;
+        nx0 = nx1;
+        if (step + 2 < steps) prefetch(nx1);
+        const uint32_t v0 = __shfl_sync(0xffffffffu, (T == T_TQ2_T) ? cur.own0[1] : cur.own0[0], nbr);
+        const uint32_t v1 = __shfl_sync(0xffffffffu, (T == T_TQ2_T) ? cur.own1[1] : cur.own1[0], nbr);
+        uint32_t o0a[8], o1a[8], o0b[8], o1b[8];
+        quarter_offsets<T, NC>(cur.own0, (T == T_TQ2_T) ? (v0 >> 24) : (v0 & 0xffffu), lane_off, o0a, o1a);
+        quarter_offsets<T, NC>(cur.own1, (T == T_TQ2_T) ? (v1 >> 24) : (v1 & 0xffffu), lane_off, o0b, o1b);
+        float d[NG][4];
 #pragma unroll
-                for (int grp = 0; grp < NG; ++grp) {
-                    float *p = part + (((u - ua) * 16 + warp) * 16 + 8 * grp + (lane >> 2)) * 8 + 2 * (lane & 3);
-                    p[0] = acc[grp][0];
-                    p[1] = acc[grp][1];
-                }
+        for (int ng = 0; ng < NG; ++ng) d[ng][0] = d[ng][1] = d[ng][2] = d[ng][3] = 0.f;
+        const uint2 *xb = xf + (size_t)b * 8 * NG * 32 + lane;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            const uint32_t w[4] = {lds_u32(cbb, o0a[c]), lds_u32(cbb, o0b[c]), lds_u32(cbb, o1a[c]),
+                                   lds_u32(cbb, o1b[c])};
+#pragma unroll
+            for (int ng = 0; ng < NG; ++ng) {
+                const uint2 xv = xon[ng] ? xb[(c * NG + ng) * 32] : make_uint2(0u, 0u);
+                mma16816(d[ng], w, xv.x, xv.y);
             }
         }
-        if (s == 0) GX_TRACE_POINT(5);
-        __syncthreads();
-        if (warp == 0 && s + 2 < ctl.n_stages) issue(s + 2);
-        for (int r = tid; r < (ub - ua) * RG * 16 * 8; r += blockDim.x) {
-            const int j = r / (RG * 128), rgi = (r / 128) % RG, tok = (r >> 3) & 15, n = r & 7;
-            const int u = ua + j;
-            if (rgi >= min(RG, NT - u * RG) || tok >= ntok) continue;
-            float v = 0.f;
-            for (int kc = 0; kc < WB; ++kc) v += part[(((j * 16) + rgi * WB + kc) * 16 + tok) * 8 + n];
-            a.y[(size_t)(t0 + tok) * a.rows + (u * RG + rgi) * 8 + n] = v;
+        const float2 s = __half22float2(*reinterpret_cast<const __half2 *>(&cur.sc));
+#pragma unroll
+        for (int ng = 0; ng < NG; ++ng) {
+            acc[ng][0] = fmaf(s.x, d[ng][0] + d[ng][1], acc[ng][0]);
+            acc[ng][1] = fmaf(s.y, d[ng][2] + d[ng][3], acc[ng][1]);
         }
-        __syncthreads();
+        if (++b == NB) {
+#pragma unroll
+            for (int ng = 0; ng < NG; ++ng) {
+                const int tok = 4 * ng + q;
+                if (tok < ntok) {
+                    float *y = a.y + (size_t)(t0 + tok) * a.rows + 16 * u + g;
+                    y[0] = acc[ng][0];
+                    if (16 * u + 8 < a.rows) y[8] = acc[ng][1];
+                }
+                acc[ng][0] = acc[ng][1] = 0.f;
+            }
+            b = 0;
+            u += nw;
+        }
     }
 }
 
@@ -1023,21 +1035,17 @@ cudaError_t down_t(const DownArgs &a, int sm_count, cudaStream_t s, bool pdl) {
     return launch(down_kernel<T, KBW, NC>, grid, 512, smem, s, pdl, a, P);
 }
 
-template <uint32_t T, int KBW, int NG>
+template <uint32_t T, int NG, int NC, int THREADS>
 cudaError_t matvec_t(const MatvecArgs &a, int sm_count, cudaStream_t s) {
-    constexpr int NC = kCodebookCopies;
-    const int NB = a.cols / 128, WB = NB < 16 ? NB : 16, RG = 16 / WB;
-    const int unit_bytes = RG * NB * tile_bytes(T);
-    const int fixed = Codebook<NC>::BYTES + 64;
-    int P = pick_stages(fixed, unit_bytes + 16 * 16 * 8 * 4 / 2, kSmemLimit);
-    if (P == 0) return cudaErrorInvalidValue;
-    const int smem = fixed + 2 * P * unit_bytes + P * 16 * 16 * 8 * 4;
-    const int NT = a.rows / 8, n_units = (NT + RG - 1) / RG;
-    const int grid = n_units < sm_count ? n_units : sm_count;
-    cudaError_t e = set_smem<matvec_kernel<T, KBW, NG, NC>>();
+    const int NB = a.cols / 128;
+    const int smem = Codebook<NC>::BYTES + NB * 8 * NG * 32 * 8;
+    if (smem > kSmemLimit) return cudaErrorInvalidValue;
+    const int n_units = (a.rows + 15) / 16;
+    const int grid = std::max(1, std::min(sm_count, (n_units + THREADS / 32 - 1) / (THREADS / 32)));
+    cudaError_t e = set_smem<matvec_kernel<T, NG, NC, THREADS>>();
     if (e != cudaSuccess) return e;
-    for (int t0 = 0; t0 < a.n_tok; t0 += 16) {
-        e = launch(matvec_kernel<T, KBW, NG, NC>, grid, 512, smem, s, false, a, t0, P);
+    for (int t0 = 0; t0 < a.n_tok; t0 += 4 * NG) {
+        e = launch(matvec_kernel<T, NG, NC, THREADS>, grid, THREADS, smem, s, false, a, t0);
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;
@@ -1109,9 +1117,14 @@ cudaError_t launch_down(const DownArgs &a, int sm_count, cudaStream_t s, bool pd
 
 cudaError_t launch_matvec(const MatvecArgs &a, int sm_count, cudaStream_t s) {
     const int NB = a.cols / 128;
-    if (NB > 16) return cudaErrorInvalidValue;
-    if (a.n_tok <= 8) { GX_TYPE_SWITCH(a.type, return (matvec_t<T, 1, 1>(a, sm_count, s))) }
-    GX_TYPE_SWITCH(a.type, return (matvec_t<T, 1, 2>(a, sm_count, s)))
+    if (NB > 16 || a.rows % 8) return cudaErrorInvalidValue;
+    // Up to 4 tokens: one MMA group; up to 8: two; beyond, four groups per launch with half the
+    // codebook copies (the activation fragments take the room).
+    // 32 warps per SM hide the code loads for one and two groups (64 registers a thread); four
+    // groups need more registers and run 16 warps.
+    if (a.n_tok <= 4) { GX_TYPE_SWITCH(a.type, return (matvec_t<T, 1, kCodebookCopies, 1024>(a, sm_count, s))) }
+    if (a.n_tok <= 8) { GX_TYPE_SWITCH(a.type, return (matvec_t<T, 2, kCodebookCopies, 1024>(a, sm_count, s))) }
+    GX_TYPE_SWITCH(a.type, return (matvec_t<T, 4, kCodebookCopies / 2, 512>(a, sm_count, s)))
 }
 
 cudaError_t launch_repack(uint32_t type, const uint8_t *raw, uint64_t row_bytes, uint32_t rows, uint32_t cols,

@@ -213,6 +213,8 @@ __global__ void __launch_bounds__(256) pack_rows_kernel(PackArgs a) {
         const int tok = a.row_slot[row] / a.U;
         src_row = (size_t)tok;
         if (a.xscale) sc = a.xscale[tok];
+    } else if (valid && a.xscale) {
+        sc = a.xscale[row];
     }
     const int ks_lo = lane >> 4, col = 4 * (lane & 15);
     if (a.by_token) {
@@ -386,6 +388,58 @@ __global__ void __launch_bounds__(kGemmThreads, 1) moe_gemm_kernel(GemmArgs a) {
             mbar_wait(done, 0, nullptr);
         }
     } else if (warp < 10) {
+      if constexpr (T == W_Q8 || T == W_F16) {
+        // ---- B from a plain matrix (the shared expert): thread d writes row d of the B tile,
+        // Q8_0 as fp16(d * q) (one rounding, as d * CB for the Gyro types), fp16 as stored. The
+        // row's 64 weights are loaded before the stage is free, hiding part of their latency.
+        const int d = tid - 64;
+        int n = 0;
+        for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
+            const int nt = it % a.n_ntiles;
+            const bool second = MODE == 0 && d >= 128;
+            const uint8_t *mat = second ? a.w1 : a.w0;
+            const __half *dsc = second ? a.d1 : a.d0;
+            const int row = MODE == 0 ? nt * 128 + (d & 127) : nt * 256 + d;
+            bool ok = true;
+            for (int ks = 0; ks < KS; ++ks, ++n) {
+                const int s = n % kGemmStages, round = n / kGemmStages;
+                uint4 v[8];
+                if constexpr (T == W_Q8) {
+                    const uint4 *q = reinterpret_cast<const uint4 *>(mat + (size_t)row * a.K + 64 * ks);
+                    const uint4 q4[4] = {q[0], q[1], q[2], q[3]};
+                    const float dd[2] = {__half2float(dsc[(size_t)row * (a.K / 32) + 2 * ks]),
+                                         __half2float(dsc[(size_t)row * (a.K / 32) + 2 * ks + 1])};
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {       // weights 8j .. 8j+7
+                        const uint32_t lo = (&q4[j >> 1].x)[(j & 1) * 2], hi = (&q4[j >> 1].x)[(j & 1) * 2 + 1];
+                        const float sc = dd[j >> 2];
+                        uint32_t h[4];
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) {
+                            const uint32_t word = k < 2 ? lo : hi;
+                            const int sh = 16 * (k & 1);
+                            const float a0 = sc * (float)(int8_t)((word >> sh) & 0xffu);
+                            const float a1 = sc * (float)(int8_t)((word >> (sh + 8)) & 0xffu);
+                            h[k] = pack_half2(a0, a1);
+                        }
+                        v[j] = make_uint4(h[0], h[1], h[2], h[3]);
+                    }
+                } else {
+                    const uint4 *w = reinterpret_cast<const uint4 *>(mat + ((size_t)row * a.K + 64 * ks) * 2);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) v[j] = w[j];
+                }
+                if (!wait(&empty[s], (round & 1) ^ 1)) { ok = false; break; }
+                uint8_t *bt = sm + s * kStageBytes + GemmSmem::B;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) *reinterpret_cast<uint4 *>(bt + sw128_offset((uint32_t)d, (uint32_t)(8 * j))) = v[j];
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&full_b[s]);
+            }
+            if (!ok) break;
+        }
+      } else {
         // ---- B decoders: thread d builds row d of the 256-row B tile -----------------------
         const int d = tid - 64;
         const uint32_t copy_off = CBk::copy_off(lane);
@@ -460,6 +514,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) moe_gemm_kernel(GemmArgs a) {
             }
             if (!ok) break;
         }
+      }
     } else {
         // ---- epilogue: warp (10..13) reads TMEM lanes 32*(warp%4) .. +31 -------------------
         const int lg = warp & 3;
@@ -550,6 +605,17 @@ __global__ void __launch_bounds__(256) combine_kernel(CombineArgs a) {
         v[2] += w * f1.x;
         v[3] += w * f1.y;
     }
+    if (a.Ysh) {
+        // the shared expert with its sigmoid gate (src/engine.zig:649-652)
+        const float g = 1.0f / (1.0f + expf(-a.sh_logit[t]));
+        const uint2 q = *reinterpret_cast<const uint2 *>(a.Ysh + (size_t)t * a.E + c);
+        const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&q.x));
+        const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(&q.y));
+        v[0] += f0.x * g;
+        v[1] += f0.y * g;
+        v[2] += f1.x * g;
+        v[3] += f1.y * g;
+    }
     const size_t o = (size_t)t * a.E + c;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -616,6 +682,8 @@ cudaError_t launch_moe_gemm(const GemmArgs &a, int mode, int sm_count, cudaStrea
         GX_GEMM_CASE(149)
         GX_GEMM_CASE(150)
         GX_GEMM_CASE(151)
+        GX_GEMM_CASE(W_Q8)
+        GX_GEMM_CASE(W_F16)
         default:
             return cudaErrorInvalidValue;
     }

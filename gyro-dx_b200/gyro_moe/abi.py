@@ -19,7 +19,7 @@ CODEBOOK_PATH = PKG / "data" / "gyro_codebook.f16"
 GX_OK = 0
 ERRORS = {-1: "GX_E_INVALIDARG", -2: "GX_E_OUTOFMEMORY", -3: "GX_E_TIMEOUT", -4: "GX_E_DEVICE",
           -5: "GX_E_UNSUPPORTED", -6: "GX_E_STATE", -7: "GX_E_MISMATCH", -8: "GX_E_COMM", -9: "GX_E_KERNEL"}
-GX_F32, GX_BF16 = 0, 30
+GX_F32, GX_Q8_0, GX_BF16 = 0, 8, 30
 GX_FLAG_PROFILE = 1
 GX_EP_NONE, GX_EP_NCCL, GX_EP_PEER = 0, 1, 2     # gx_caps.ep_exchange
 
@@ -54,12 +54,19 @@ class LayerDesc(ctypes.Structure):
                 ("down_signs", ctypes.c_void_p), ("router_bias", ctypes.c_void_p)]
 
 
+class SharedDesc(ctypes.Structure):
+    _fields_ = [("type_id", ctypes.c_uint32), ("n_ff", ctypes.c_uint32), ("gate", ctypes.c_void_p),
+                ("up", ctypes.c_void_p), ("down", ctypes.c_void_p), ("gate_bytes", ctypes.c_uint64),
+                ("up_bytes", ctypes.c_uint64), ("down_bytes", ctypes.c_uint64), ("gate_inp", ctypes.c_void_p)]
+
+
 class Timings(ctypes.Structure):
     _fields_ = [("router_ns", ctypes.c_uint64), ("gate_up_ns", ctypes.c_uint64), ("down_ns", ctypes.c_uint64),
                 ("experts_ns", ctypes.c_uint64), ("total_ns", ctypes.c_uint64), ("layers", ctypes.c_uint64)]
 
 
 assert ctypes.sizeof(Options) == 168 and ctypes.sizeof(Caps) == 192 and ctypes.sizeof(LayerDesc) == 112
+assert ctypes.sizeof(SharedDesc) == 64
 
 # (name, argtypes) of every exported entry point; include/gyro_moe.h declares exactly these.
 _P, _U32, _U64, _F = ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_float
@@ -68,6 +75,7 @@ SIGNATURES = {
     "gx_comm_unique_id": [ctypes.c_char_p, _U64],
     "gx_get_caps": [_P, ctypes.POINTER(Caps)],
     "gx_upload_layer": [_P, _U32, ctypes.POINTER(LayerDesc), _U32],
+    "gx_upload_shared": [_P, _U32, ctypes.POINTER(SharedDesc), _U32],
     "gx_moe_forward": [_P, _U32, _P, _U32, _U32, _P, _U32, _P, _P, ctypes.POINTER(_U64)],
     "gx_moe_forward_host": [_P, _U32, _P, _U32, _U32, _P, _U32, _P, _P, _U32],
     "gx_stack_forward": [_P, _U32, _U32, _P, _U32, _U32, _P, _U32, ctypes.POINTER(_U64)],
@@ -203,6 +211,19 @@ class Context:
                          arr(layer.get("down_signs"), np.float32), arr(layer.get("router_bias"), np.float32))
         _check(self.lib.gx_upload_layer(self.handle, index, ctypes.byref(desc), timeout_ms), "gx_upload_layer")
         self.layers[index] = {k: layer[k] for k in ("n_embd", "n_used", "n_expert")}
+        if layer.get("shared") is not None:
+            self.upload_shared(index, layer["shared"], timeout_ms)
+
+    def upload_shared(self, index: int, shared: dict | None, timeout_ms: int = 600000) -> None:
+        """gx_upload_shared: the layer's shared expert (synth.make_shared layout), or None to drop it."""
+        if shared is None:
+            _check(self.lib.gx_upload_shared(self.handle, index, None, timeout_ms), "gx_upload_shared")
+            return
+        mats = [np.ascontiguousarray(shared[k], dtype=np.uint8) for k in ("gate", "up", "down")]
+        gi = np.ascontiguousarray(shared["gate_inp"], dtype=np.float32)
+        desc = SharedDesc(shared["type_id"], shared["n_ff"], mats[0].ctypes.data, mats[1].ctypes.data,
+                          mats[2].ctypes.data, mats[0].nbytes, mats[1].nbytes, mats[2].nbytes, gi.ctypes.data)
+        _check(self.lib.gx_upload_shared(self.handle, index, ctypes.byref(desc), timeout_ms), "gx_upload_shared")
 
     # --- forward ---------------------------------------------------------------------------
     def forward(self, layer: int, x, y, ids=None, weights=None) -> int:

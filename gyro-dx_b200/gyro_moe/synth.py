@@ -71,6 +71,32 @@ def make_layer(seed: int, n_expert: int = 256, E: int = 2048, F: int = 512, U: i
     return layer
 
 
+SHARED_TYPES = {"f32": 0, "q8_0": 8, "bf16": 30}
+
+
+def make_shared(seed: int, E: int = 2048, SF: int = 512, type_id: int = 8) -> dict:
+    """A shared expert (src/model.zig:418-421) in one of the non-expert encodings the reference GPU
+    engine multiplies (src/gpu_engine.zig:846-850): Q8_0 (blocks of an fp16 scale and 32 int8, with
+    d = fp16(1 / (73 sqrt(cols))) so the weights come out with a standard deviation near
+    1 / sqrt(cols)), bf16 or f32 (~N(0, 1/cols)). Its sigmoid gate is f32 ~N(0, 0.02)."""
+    rng = np.random.default_rng(seed)
+
+    def mat(rows: int, cols: int) -> np.ndarray:
+        if type_id == 8:
+            q = rng.integers(-127, 128, (rows, cols // 32, 32), dtype=np.int8)
+            d = np.full((rows, cols // 32, 1), fp16_bits(1.0 / (73.0 * np.sqrt(cols))), np.uint16)
+            return np.concatenate([d.view(np.uint8), q.view(np.uint8)], axis=2).reshape(rows, cols // 32 * 34)
+        w = rng.normal(0.0, 1.0 / np.sqrt(cols), size=(rows, cols)).astype(np.float32)
+        if type_id == 30:
+            return bf16_bits(w).view(np.uint8).reshape(rows, cols * 2)
+        if type_id == 0:
+            return w.view(np.uint8).reshape(rows, cols * 4)
+        raise ValueError(f"unsupported shared-expert type {type_id}")
+
+    return {"type_id": type_id, "n_ff": SF, "gate": mat(SF, E), "up": mat(SF, E), "down": mat(E, SF),
+            "gate_inp": rng.normal(0.0, 0.02, size=E).astype(np.float32)}
+
+
 def tokens(seed: int, n: int, E: int = 2048, dtype=np.float32) -> np.ndarray:
     """x ~ N(0, 1); bf16 inputs are produced by rounding (returned as float32 values that are
     exactly representable in bf16 when dtype is 'bf16')."""

@@ -18,6 +18,7 @@ pub const e_comm: gx_result = -8;
 pub const e_kernel: gx_result = -9;
 
 pub const dtype_f32: u32 = 0;
+pub const dtype_q8_0: u32 = 8;
 pub const dtype_bf16: u32 = 30;
 pub const flag_profile: u32 = 1;
 pub const ep_none: u32 = 0;
@@ -74,6 +75,18 @@ pub const gx_layer_desc = extern struct {
     router_bias: ?[*]const f32,
 };
 
+pub const gx_shared_desc = extern struct {
+    type_id: u32,
+    n_ff: u32,
+    gate: ?*const anyopaque,
+    up: ?*const anyopaque,
+    down: ?*const anyopaque,
+    gate_bytes: u64,
+    up_bytes: u64,
+    down_bytes: u64,
+    gate_inp: ?[*]const f32,
+};
+
 pub const gx_timings = extern struct {
     router_ns: u64,
     gate_up_ns: u64,
@@ -86,6 +99,7 @@ pub const gx_timings = extern struct {
 pub extern fn gx_create(options: *const gx_options, context: *?*gx_context) gx_result;
 pub extern fn gx_get_caps(context: *gx_context, caps: *gx_caps) gx_result;
 pub extern fn gx_upload_layer(context: *gx_context, layer: u32, desc: *const gx_layer_desc, timeout_ms: u32) gx_result;
+pub extern fn gx_upload_shared(context: *gx_context, layer: u32, desc: ?*const gx_shared_desc, timeout_ms: u32) gx_result;
 pub extern fn gx_moe_forward(context: *gx_context, layer: u32, x: ?*const anyopaque, x_dtype: u32, n_tok: u32,
     y: ?*anyopaque, y_dtype: u32, ids: ?[*]u32, weights: ?[*]f32, ticket: ?*u64) gx_result;
 pub extern fn gx_moe_forward_host(context: *gx_context, layer: u32, x: ?*const anyopaque, x_dtype: u32, n_tok: u32,
@@ -124,4 +138,6 @@ comptime {
     assert(@sizeOf(gx_layer_desc) == 112);
     assert(@offsetOf(gx_layer_desc, "router") == 72);
     assert(@sizeOf(gx_timings) == 48);
+    assert(@sizeOf(gx_shared_desc) == 64);
+    assert(@offsetOf(gx_shared_desc, "gate_inp") == 56);
 }

@@ -54,8 +54,9 @@ enum {
     GX_E_KERNEL = -9        /* a kernel's bounded wait expired; its outputs are invalid */
 };
 
-/* Activation encodings (the type ids of src/kernels.zig:7-10). */
-enum { GX_F32 = 0, GX_BF16 = 30 };
+/* Activation encodings, and the weight encodings of a shared expert (the type ids of
+ * src/kernels.zig:7-10). */
+enum { GX_F32 = 0, GX_Q8_0 = 8, GX_BF16 = 30 };
 
 /* Options: mirrors the role of gd_options (native/include/gyro_native.h:25-31). */
 enum {
@@ -115,6 +116,22 @@ typedef struct gx_layer_desc {
                                      skewed expert popularity; no reference counterpart) */
 } gx_layer_desc;
 
+/* The shared expert of a routed layer and its sigmoid gate, as the Zig host binds them
+ * (ffn_{gate,up,down}_shexp and ffn_gate_inp_shexp, src/model.zig:418-421). Plain row-major
+ * matrices in one of the encodings the reference GPU engine multiplies them in
+ * (src/gpu_engine.zig:846-850): GX_Q8_0 (blocks of an fp16 scale and 32 int8), GX_BF16 or GX_F32.
+ * On the device Q8_0 stays Q8_0; bf16 and f32 matrices are stored as fp16 (bf16 values convert
+ * exactly within the fp16 range, f32 values are rounded once). */
+typedef struct gx_shared_desc {
+    uint32_t type_id;             /* GX_Q8_0, GX_BF16 or GX_F32 */
+    uint32_t n_ff;                /* SF = n_ff_shexp: multiple of 128, at most 4096 */
+    const void *gate;             /* [SF rows][n_embd], host memory */
+    const void *up;               /* [SF][n_embd] */
+    const void *down;             /* [n_embd rows][SF] */
+    uint64_t gate_bytes, up_bytes, down_bytes;
+    const float *gate_inp;        /* [n_embd] f32 weights of the sigmoid gate */
+} gx_shared_desc;
+
 /* Per-phase device times, in nanoseconds, of the most recent forward call (gx_moe_forward*, or
  * all layers of the most recent gx_stack_forward*) on a context created with GX_FLAG_PROFILE.
  * Measured with CUDA events recorded on the context's stream between the kernels (inside the
@@ -152,6 +169,17 @@ GX_API gx_result gx_get_caps(gx_context *context, gx_caps *out_caps);
  * (src/gpu_engine.zig:447-458, :593-668). Blocking. */
 GX_API gx_result gx_upload_layer(gx_context *context, uint32_t layer, const gx_layer_desc *desc,
                                  uint32_t timeout_ms);
+
+/* Adds the shared expert to an uploaded layer (desc NULL removes it). From then on every forward
+ * call of the layer returns ffn_out instead of ffn_moe_out (src/engine.zig:642-653):
+ *   y[t] = routed[t] + sigmoid(gate_inp . x[t]) * Down(silu(Gate x[t]) * Up x[t])
+ * with x the layer input (unrotated). gx_upload_layer of the same index removes it again. With
+ * world > 1 every rank holds the whole shared expert and computes it for its own tokens (it is
+ * not exchanged). Needs n_embd to be a multiple of 256. Blocking. No counterpart function in the
+ * reference bridge: its host binds these tensors next to the routed ones (src/gpu_engine.zig:
+ * 397-401) and multiplies them with its generic mv (:1061-1063, :1074). */
+GX_API gx_result gx_upload_shared(gx_context *context, uint32_t layer, const gx_shared_desc *desc,
+                                  uint32_t timeout_ms);
 
 /* Routed-expert layer on device-resident activations, enqueued on the context's stream
  * (replaces the dispatch chain of Engine.ffn, src/gpu_engine.zig:1059-1116, through

@@ -278,6 +278,8 @@ void gxo_rotate_f32(float *x, size_t n, size_t block, const float *signs) {
 /* src/kernels.zig:56-67 (f32 and Gyro types only: the non-expert types are out of scope). */
 size_t gxo_row_bytes(uint32_t type_id, size_t cols) {
     if (type_id == 0) return cols * 4;
+    if (type_id == 1 || type_id == 30) return cols * 2;
+    if (type_id == 8) return cols % 32 ? 0 : cols / 32 * 34;
     int bb;
     if (gxo_type_info(type_id, NULL, NULL, &bb) || cols % 128) return 0;
     return cols / 128 * (size_t)bb;
@@ -378,8 +380,34 @@ static float dot_gyro_generic(uint32_t type_id, const uint8_t *row, const float 
 }
 
 /* src/kernels.zig:201-210 */
+/* src/kernels.zig:86-105 (dotHalf): bf16 widened by a 16-bit shift, f16 converted exactly. */
+static float dot_half(int bf, const uint8_t *row, const float *x, size_t n) {
+    float sum = 0;
+    for (size_t i = 0; i < n; ++i) {
+        uint16_t bits = (uint16_t)(row[2 * i] | (row[2 * i + 1] << 8));
+        float w = bf ? bits_to_f32((uint32_t)bits << 16) : gxo_fp16_to_fp32(bits);
+        sum += w * x[i];
+    }
+    return sum;
+}
+
+/* src/kernels.zig:107-120 (dotQ8): per 32-weight block, d * sum(q * x). */
+static float dot_q8(const uint8_t *row, const float *x, size_t n) {
+    float total = 0;
+    for (size_t b = 0; b < n / 32; ++b) {
+        const uint8_t *block = row + b * 34;
+        float d = gxo_fp16_to_fp32((uint16_t)(block[0] | (block[1] << 8)));
+        float acc = 0;
+        for (int j = 0; j < 32; ++j) acc += (float)(int8_t)block[2 + j] * x[b * 32 + j];
+        total += d * acc;
+    }
+    return total;
+}
+
 float gxo_dot_row(uint32_t type_id, const uint8_t *row, const float *x, size_t cols) {
     if (type_id == 0) return dot_f32(row, x, cols);
+    if (type_id == 1 || type_id == 30) return dot_half(type_id == 30, row, x, cols);
+    if (type_id == 8) return dot_q8(row, x, cols);
     if (type_id == 144) return dot_tq2(row, x, cols);
     return dot_gyro_generic(type_id, row, x, cols);
 }
@@ -604,4 +632,54 @@ int gxo_moe_experts(const gxo_layer *l, const float *x, size_t n, const uint32_t
     if (!layer_ok(l) || !x || !out || !ids || !weights) return -1;
     if (n == 0) return 0;
     return experts_phase(l, x, n, ids, weights, out, threads);
+}
+
+/* ---- shared expert, src/engine.zig:644-653 ------------------------------------------------
+ * out[t] += sigmoid(gate_inp . x[t]) * Down(silu(Gate x[t]) * Up x[t]); the three matrices are
+ * plain row-major (kernels.matmul over dotRow, src/kernels.zig:239-268). */
+typedef struct shared_ctx {
+    const gxo_shared *s;
+    const float *x;
+    size_t n, E, SF, row_in, row_f;
+    float *g, *u, *d;
+} shared_ctx;
+
+static void shared_gate_up_range(void *p, size_t a, size_t b) {
+    shared_ctx *c = (shared_ctx *)p;
+    for (size_t r = a; r < b; ++r)
+        for (size_t t = 0; t < c->n; ++t) {
+            c->g[t * c->SF + r] = gxo_dot_row(c->s->type_id, c->s->gate + r * c->row_in, c->x + t * c->E, c->E);
+            c->u[t * c->SF + r] = gxo_dot_row(c->s->type_id, c->s->up + r * c->row_in, c->x + t * c->E, c->E);
+        }
+}
+
+static void shared_down_range(void *p, size_t a, size_t b) {
+    shared_ctx *c = (shared_ctx *)p;
+    for (size_t r = a; r < b; ++r)
+        for (size_t t = 0; t < c->n; ++t)
+            c->d[t * c->E + r] = gxo_dot_row(c->s->type_id, c->s->down + r * c->row_f, c->g + t * c->SF, c->SF);
+}
+
+/* src/kernels.zig:303-305 */
+static float sigmoid(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+int gxo_shared_expert(const gxo_shared *s, const float *x, size_t n, size_t E, float *out, int threads) {
+    if (!s || !x || !out || !s->gate || !s->up || !s->down || !s->gate_inp || s->n_ff == 0) return -1;
+    const size_t SF = s->n_ff;
+    const size_t row_in = gxo_row_bytes(s->type_id, E), row_f = gxo_row_bytes(s->type_id, SF);
+    if (!row_in || !row_f || (s->type_id != 0 && s->type_id != 1 && s->type_id != 8 && s->type_id != 30)) return -1;
+    float *g = malloc(sizeof(float) * n * SF), *u = malloc(sizeof(float) * n * SF), *d = malloc(sizeof(float) * n * E);
+    if (!g || !u || !d) { free(g); free(u); free(d); return -1; }
+    shared_ctx c = {s, x, n, E, SF, row_in, row_f, g, u, d};
+    pool_run(threads, SF, 8, shared_gate_up_range, &c);
+    for (size_t i = 0; i < n * SF; ++i) g[i] = silu(g[i]) * u[i];
+    pool_run(threads, E, 8, shared_down_range, &c);
+    for (size_t t = 0; t < n; ++t) {
+        const float gate = sigmoid(dot_f32((const uint8_t *)s->gate_inp, x + t * E, E));
+        float *o = out + t * E;
+        const float *v = d + t * E;
+        for (size_t i = 0; i < E; ++i) o[i] += v[i] * gate;
+    }
+    free(g); free(u); free(d);
+    return 0;
 }

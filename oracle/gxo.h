@@ -57,7 +57,7 @@ void gxo_rotate_f32(float *x, size_t n, size_t block, const float *signs);
 /* Row bytes of a matrix row, src/kernels.zig:56-67 (0 for f32 routers is cols*4). */
 size_t gxo_row_bytes(uint32_t type_id, size_t cols);
 
-/* dotRow for f32 and the eight Gyro types, src/kernels.zig:72-84, 161-210. */
+/* dotRow for f32, f16, bf16, Q8_0 and the eight Gyro types, src/kernels.zig:72-120, 161-210. */
 float gxo_dot_row(uint32_t type_id, const uint8_t *row, const float *x, size_t cols);
 
 /* decodeRow for Gyro types (fast path of the engine), src/kernels.zig:136-159, 213-235. */
@@ -96,6 +96,21 @@ int gxo_moe_ffn(const gxo_layer *layer, const float *x, size_t n, float *out,
  * rank serves in the expert-parallel model). The router fields of the layer are not used. */
 int gxo_moe_experts(const gxo_layer *layer, const float *x, size_t n, const uint32_t *ids,
                     const float *weights, float *out, int threads);
+
+/* The shared expert of a layer, src/engine.zig:644-653: three plain row-major matrices in a
+ * non-expert encoding (0 f32, 1 f16, 8 Q8_0, 30 bf16; src/kernels.zig:7-10, :56-67) and the f32
+ * vector of its sigmoid gate. Bindings of src/model.zig:418-421. */
+typedef struct gxo_shared {
+    uint32_t type_id;
+    uint32_t n_ff;                       /* n_ff_shexp */
+    const uint8_t *gate, *up;            /* [n_ff][n_embd] */
+    const uint8_t *down;                 /* [n_embd][n_ff] */
+    const float *gate_inp;               /* [n_embd] */
+} gxo_shared;
+
+/* out[t] += sigmoid(gate_inp . x[t]) * Down(silu(Gate x[t]) * Up x[t]) for n tokens x [n][E]
+ * (the unrotated layer input). Returns 0, or -1 on bad arguments. */
+int gxo_shared_expert(const gxo_shared *s, const float *x, size_t n, size_t E, float *out, int threads);
 
 /* Threads the library can use (1 when built without GXO_THREADS). */
 int gxo_max_threads(void);

@@ -82,6 +82,8 @@ def lib(fast: bool = False) -> ctypes.CDLL:
                               ctypes.c_int]
     L.gxo_moe_experts.argtypes = [ctypes.POINTER(_Layer), _F32P, ctypes.c_size_t, _U32P, _F32P, _F32P,
                                   ctypes.c_int]
+    L.gxo_shared_expert.argtypes = [ctypes.POINTER(_Shared), _F32P, ctypes.c_size_t, ctypes.c_size_t, _F32P,
+                                    ctypes.c_int]
     L.gxo_max_threads.restype = ctypes.c_int
     L.gxo_rms_norm.argtypes = [_F32P, _F32P, ctypes.c_size_t, ctypes.c_float]
     L.gxo_rms_norm.restype = None
@@ -90,6 +92,17 @@ def lib(fast: bool = False) -> ctypes.CDLL:
         raise RuntimeError("oracle rejected the codebook")
     _LIBS[name] = L
     return L
+
+
+class _Shared(ctypes.Structure):
+    _fields_ = [
+        ("type_id", ctypes.c_uint32),
+        ("n_ff", ctypes.c_uint32),
+        ("gate", ctypes.c_void_p),
+        ("up", ctypes.c_void_p),
+        ("down", ctypes.c_void_p),
+        ("gate_inp", ctypes.c_void_p),
+    ]
 
 
 def _f32p(a: np.ndarray):
@@ -149,7 +162,25 @@ def moe_ffn(layer: dict, x: np.ndarray, threads: int = 1, fast: bool = False):
     rc = L.gxo_moe_ffn(ctypes.byref(desc), _f32p(x), n, _f32p(out), ids.ctypes.data_as(_U32P), _f32p(w), threads)
     if rc != 0:
         raise RuntimeError(f"gxo_moe_ffn failed ({rc})")
+    if layer.get("shared") is not None:
+        shared_expert(layer["shared"], x, out, threads=threads, fast=fast)
     return out, ids, w
+
+
+def shared_expert(shared: dict, x: np.ndarray, out: np.ndarray, threads: int = 1, fast: bool = False) -> None:
+    """src/engine.zig:644-653: adds sigmoid(gate_inp . x) * Down(silu(Gate x) * Up x) into out [n, E]."""
+    L = lib(fast)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    n, E = x.shape
+    keep = [np.ascontiguousarray(shared[k], dtype=np.uint8) for k in ("gate", "up", "down")]
+    gi = np.ascontiguousarray(shared["gate_inp"], dtype=np.float32)
+    desc = _Shared(shared["type_id"], shared["n_ff"], keep[0].ctypes.data, keep[1].ctypes.data, keep[2].ctypes.data,
+                   gi.ctypes.data)
+    if not (out.flags["C_CONTIGUOUS"] and out.dtype == np.float32 and out.shape == (n, E)):
+        raise ValueError("out must be a contiguous float32 [n, E] array")
+    rc = L.gxo_shared_expert(ctypes.byref(desc), _f32p(x), n, E, _f32p(out), threads)
+    if rc != 0:
+        raise RuntimeError(f"gxo_shared_expert failed ({rc})")
 
 
 def moe_experts(layer: dict, x: np.ndarray, ids: np.ndarray, weights: np.ndarray, threads: int = 1,

@@ -24,6 +24,8 @@ CASES = [
     ("small", dict(seed=31, n_expert=16, E=256, F=128, U=4), [37, 21]),
     ("zipf_empty_rank", dict(seed=32, n_expert=32, E=256, F=256, U=4, zipf=1.1), [70, 0]),
     ("config0_shape", dict(seed=33, zipf=1.1), [300, 180]),
+    # a Q8_0 shared expert: every rank computes it for its own tokens, beside the exchanged rows
+    ("shared_expert", dict(seed=35, n_expert=32, E=256, F=256, U=4, shared=256), [45, 20]),
 ]
 
 
@@ -35,7 +37,11 @@ def make(kw):
     from gyro_moe import synth
     kw = dict(kw)
     seed = kw.pop("seed")
-    return synth.make_layer(seed, **kw)
+    sf = kw.pop("shared", None)
+    layer = synth.make_layer(seed, **kw)
+    if sf:
+        layer["shared"] = synth.make_shared(seed + 500, E=layer["n_embd"], SF=sf, type_id=8)
+    return layer
 
 
 def tokens(case_i, rank, n, E):

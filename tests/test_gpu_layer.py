@@ -197,6 +197,26 @@ def test_matvec_type_sweep(ctx, type_id, shape):
         check(x.astype(np.float64) @ dense.T, yt.cpu().numpy())
 
 
+@pytest.mark.parametrize("type_id", [144, 147, 151])
+def test_matvec_odd_row_groups_and_token_groups(ctx, type_id):
+    """40 rows (an odd number of 8-row groups: the last 16-row unit is half padding) and 1, 5 and
+    13 tokens (one, two and four MMA token groups, the last partly empty)."""
+    rows, cols = 40, 384
+    rng = np.random.default_rng(type_id + 5)
+    W = synth.packed_matrix(rng, type_id, rows, cols)
+    h = ctx.upload_matrix(type_id, rows, cols, W)
+    dense = np.stack([oracle.decode_row(type_id, W[r].tobytes(), cols) for r in range(rows)]).astype(np.float64)
+    for n in (1, 5, 13):
+        x = rng.standard_normal((n, cols)).astype(np.float32)
+        xt = torch.from_numpy(x).cuda()
+        yt = torch.full((n, rows + 8), 7.0, dtype=torch.float32, device="cuda")   # guard columns
+        torch.cuda.synchronize()
+        ctx.wait(ctx.matvec(h, xt, yt.view(-1)[:n * rows].view(n, rows)))
+        got = yt.view(-1)[:n * rows].view(n, rows).cpu().numpy()
+        check(x.astype(np.float64) @ dense.T, got)
+        assert (yt.view(-1)[n * rows:].cpu().numpy() == 7.0).all()     # nothing written past the rows
+
+
 def test_profiled_stack_reports_times():
     """Per-phase kernels report router / gate-up / down times per layer; the persistent stack
     kernel (GX_STACK_KERNEL=1) reports its total."""

@@ -258,3 +258,30 @@ def test_layer_dense_definition():
             acc += w[t, k] * (D[e] @ a)
         rel = np.sqrt(((acc - out[t]) ** 2).sum() / (acc ** 2).sum())
         assert rel < 1e-5
+
+
+@pytest.mark.parametrize("type_id", [0, 8, 30])
+def test_shared_expert_matches_dense_definition(type_id):
+    """src/engine.zig:644-653 with the Q8_0 / bf16 / f32 dots of src/kernels.zig:72-120, against a
+    float64 numpy restatement of the same definition."""
+    layer = synth.make_layer(5, n_expert=16, E=256, F=128, U=4)
+    x = synth.tokens(6, 3, E=256)
+    sh = synth.make_shared(9, E=256, SF=128, type_id=type_id)
+    base, _, _ = oracle.moe_ffn(layer, x)
+    out, _, _ = oracle.moe_ffn(dict(layer, shared=sh), x)
+
+    def dense(m, rows, cols):
+        if type_id == 8:
+            b = m.reshape(rows, cols // 32, 34)
+            d = b[:, :, :2].copy().view(np.float16).astype(np.float64)
+            q = b[:, :, 2:].view(np.int8).astype(np.float64)
+            return (d * q).reshape(rows, cols)
+        if type_id == 30:
+            return (m.view(np.uint16).astype(np.uint32) << 16).view(np.float32).reshape(rows, cols).astype(np.float64)
+        return m.view(np.float32).reshape(rows, cols).astype(np.float64)
+
+    xd = x.astype(np.float64)
+    g, u = xd @ dense(sh["gate"], 128, 256).T, xd @ dense(sh["up"], 128, 256).T
+    y = (g / (1 + np.exp(-g)) * u) @ dense(sh["down"], 256, 128).T
+    gate = 1 / (1 + np.exp(-(xd @ sh["gate_inp"].astype(np.float64))))
+    np.testing.assert_allclose(out, base + y * gate[:, None], rtol=1e-5, atol=1e-5)
