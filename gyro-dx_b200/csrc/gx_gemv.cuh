@@ -71,13 +71,14 @@ __device__ __forceinline__ void tile_mma(const uint8_t *tile, const uint32_t *cb
     const int nbr = (lane & ~3) | ((lane + 3) & 3);
     const uint32_t nv = __shfl_sync(0xffffffffu, (T == T_TQ2_T) ? own[1] : own[0], nbr);
     const uint32_t nb = (T == T_TQ2_T) ? (nv >> 24) : (nv & 0xffffu);
-    uint32_t i0[8], i1[8];
-    quarter_indices<T>(own, nb, i0, i1);
+    uint32_t o0[8], o1[8];
+    quarter_offsets<T, NC>(own, nb, 4u * copy_off, o0, o1);
+    const uint8_t *cbb = reinterpret_cast<const uint8_t *>(cb);
     uint32_t b0[8], b1[8];
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
-        b0[c] = cb[Codebook<NC>::word(i0[c], copy_off)];
-        b1[c] = cb[Codebook<NC>::word(i1[c], copy_off)];
+        b0[c] = lds_u32(cbb, o0[c]);
+        b1[c] = lds_u32(cbb, o1[c]);
     }
     // Two independent accumulator chains (even / odd chunks) halve the mma dependency chain.
     float d[2][NG][4];

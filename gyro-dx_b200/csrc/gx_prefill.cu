@@ -19,6 +19,7 @@
 #include <cuda_runtime.h>
 
 #include "gx_device.cuh"
+#include "gx_gemv.cuh"
 #include "gx_internal.h"
 #include "gx_umma.cuh"
 
@@ -442,7 +443,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) moe_gemm_kernel(GemmArgs a) {
       } else {
         // ---- B decoders: thread d builds row d of the 256-row B tile -----------------------
         const int d = tid - 64;
-        const uint32_t copy_off = CBk::copy_off(lane);
+        const uint32_t lane_off = 4u * CBk::copy_off(lane);
+        const uint8_t *cbb = reinterpret_cast<const uint8_t *>(cb);
         int n = 0;
         for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
             const int t = it / a.n_ntiles, nt = it % a.n_ntiles;
@@ -484,9 +486,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) moe_gemm_kernel(GemmArgs a) {
                 const uint16_t dh = nxd;
                 if (ks + 1 < KS) fetch(ks + 1);
                 const __half2 d2 = __halves2half2(__ushort_as_half(dh), __ushort_as_half(dh));
-                uint32_t i0[2][8], i1[2][8];
-                quarter_indices<T>(own0, neighbour_bits<T>(nbr), i0[0], i1[0]);
-                quarter_indices<T>(own1, neighbour_bits<T>(own0), i0[1], i1[1]);
+                uint32_t o0[2][8], o1[2][8];
+                quarter_offsets<T, kGemmCopies>(own0, neighbour_bits<T>(nbr), lane_off, o0[0], o1[0]);
+                quarter_offsets<T, kGemmCopies>(own1, neighbour_bits<T>(own0), lane_off, o0[1], o1[1]);
                 if (!wait(&empty[s], (round & 1) ^ 1)) { ok = false; break; }
                 uint8_t *bt = sm + s * kStageBytes + GemmSmem::B;
 #pragma unroll
@@ -494,10 +496,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) moe_gemm_kernel(GemmArgs a) {
 #pragma unroll
                     for (int c = 0; c < 8; c += 2) {
                         uint32_t w[4];
-                        const uint32_t p0 = cb[CBk::word(i0[qq][c], copy_off)];
-                        const uint32_t p1 = cb[CBk::word(i1[qq][c], copy_off)];
-                        const uint32_t p2 = cb[CBk::word(i0[qq][c + 1], copy_off)];
-                        const uint32_t p3 = cb[CBk::word(i1[qq][c + 1], copy_off)];
+                        const uint32_t p0 = lds_u32(cbb, o0[qq][c]);
+                        const uint32_t p1 = lds_u32(cbb, o1[qq][c]);
+                        const uint32_t p2 = lds_u32(cbb, o0[qq][c + 1]);
+                        const uint32_t p3 = lds_u32(cbb, o1[qq][c + 1]);
                         const uint32_t pp[4] = {p0, p1, p2, p3};
 #pragma unroll
                         for (int j = 0; j < 4; ++j) {
