@@ -445,46 +445,59 @@ __global__ void __launch_bounds__(kGemmThreads, 1) moe_gemm_kernel(GemmArgs a) {
         const int d = tid - 64;
         const uint32_t lane_off = 4u * CBk::copy_off(lane);
         const uint8_t *cbb = reinterpret_cast<const uint8_t *>(cb);
-        int n = 0;
-        for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
+        const int r8 = d & 7;                  // row within its 8-row tile (the same in every item)
+        // The thread's row of an item's B tile: its 8-row tiles, one per 128-column block.
+        auto rowtiles_of = [&](int it) -> const uint8_t * {
             const int t = it / a.n_ntiles, nt = it % a.n_ntiles;
             uint32_t e = (uint32_t)a.tile_expert[t];
             if (e >= (uint32_t)a.n_expert) {
                 atomicExch(a.err, KERR_BOUNDS);
                 e = 0;
             }
-            const uint8_t *mat;
-            int row;
-            if (MODE == 0) {
-                mat = (d < 128 ? a.w0 : a.w1) + (uint64_t)e * a.expert_bytes;
-                row = nt * 128 + (d & 127);
-            } else {
-                mat = a.w0 + (uint64_t)e * a.expert_bytes;
-                row = nt * 256 + d;
+            const uint8_t *mat = (MODE == 0 ? (d < 128 ? a.w0 : a.w1) : a.w0) + (uint64_t)e * a.expert_bytes;
+            const int row = MODE == 0 ? nt * 128 + (d & 127) : nt * 256 + d;
+            return mat + (size_t)(row >> 3) * NB * TB;
+        };
+        // Codes of one k-step: the two own quarters (2h, 2h+1), the neighbour run of quarter
+        // (2h+3)%4 and the row's block scale. They are fetched kPrefetch k-steps ahead, across
+        // item boundaries, so the global-load latency hides behind the decoding of the steps
+        // between.
+        struct Codes {
+            uint32_t own0[4], own1[4], nbr[4];
+            uint16_t d;
+        };
+        constexpr int kPrefetch = 3;
+        int pf_it = blockIdx.x, pf_ks = 0;
+        const uint8_t *pf_rt = pf_it < n_items ? rowtiles_of(pf_it) : nullptr;
+        auto fetch_next = [&](Codes &cd) {
+            if (pf_it >= n_items) return;
+            const int h = pf_ks & 1;
+            const uint8_t *tile = pf_rt + (size_t)(pf_ks >> 1) * TB;
+            load_run<T>(tile, 4 * r8 + 2 * h, cd.own0);
+            load_run<T>(tile, 4 * r8 + 2 * h + 1, cd.own1);
+            load_run<T>(tile, 4 * r8 + ((2 * h + 3) & 3), cd.nbr);
+            cd.d = *reinterpret_cast<const uint16_t *>(tile + tile_code_bytes(T) + 2 * r8);
+            if (++pf_ks == KS) {
+                pf_ks = 0;
+                pf_it += gridDim.x;
+                if (pf_it < n_items) pf_rt = rowtiles_of(pf_it);
             }
-            const uint8_t *rowtiles = mat + (size_t)(row >> 3) * NB * TB;
-            const int r8 = row & 7;
+        };
+        Codes cq[kPrefetch];
+#pragma unroll
+        for (int i = 0; i < kPrefetch; ++i) fetch_next(cq[i]);
+        int n = 0;
+        for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
             bool ok = true;
-            // codes of one k-step: the two own quarters (2h, 2h+1), the neighbour run of quarter
-            // (2h+3)%4 and the row's block scale; step ks+1 is fetched while ks is decoded
-            uint32_t nx0[4], nx1[4], nxn[4];
-            uint16_t nxd;
-            auto fetch = [&](int ks) {
-                const int h = ks & 1;
-                const uint8_t *tile = rowtiles + (size_t)(ks >> 1) * TB;
-                load_run<T>(tile, 4 * r8 + 2 * h, nx0);
-                load_run<T>(tile, 4 * r8 + 2 * h + 1, nx1);
-                load_run<T>(tile, 4 * r8 + ((2 * h + 3) & 3), nxn);
-                nxd = *reinterpret_cast<const uint16_t *>(tile + tile_code_bytes(T) + 2 * r8);
-            };
-            fetch(0);
             for (int ks = 0; ks < KS; ++ks, ++n) {
                 const int s = n % kGemmStages, round = n / kGemmStages;
                 uint32_t own0[4], own1[4], nbr[4];
 #pragma unroll
-                for (int j = 0; j < 4; ++j) { own0[j] = nx0[j]; own1[j] = nx1[j]; nbr[j] = nxn[j]; }
-                const uint16_t dh = nxd;
-                if (ks + 1 < KS) fetch(ks + 1);
+                for (int j = 0; j < 4; ++j) { own0[j] = cq[0].own0[j]; own1[j] = cq[0].own1[j]; nbr[j] = cq[0].nbr[j]; }
+                const uint16_t dh = cq[0].d;
+#pragma unroll
+                for (int i = 0; i + 1 < kPrefetch; ++i) cq[i] = cq[i + 1];
+                fetch_next(cq[kPrefetch - 1]);
                 const __half2 d2 = __halves2half2(__ushort_as_half(dh), __ushort_as_half(dh));
                 uint32_t o0[2][8], o1[2][8];
                 quarter_offsets<T, kGemmCopies>(own0, neighbour_bits<T>(nbr), lane_off, o0[0], o1[0]);
