@@ -60,13 +60,23 @@ class SharedDesc(ctypes.Structure):
                 ("up_bytes", ctypes.c_uint64), ("down_bytes", ctypes.c_uint64), ("gate_inp", ctypes.c_void_p)]
 
 
+class GgufLayerInfo(ctypes.Structure):
+    _fields_ = [("type_id", ctypes.c_uint32), ("n_expert", ctypes.c_uint32), ("n_embd", ctypes.c_uint32),
+                ("n_ff", ctypes.c_uint32), ("n_used", ctypes.c_uint32), ("expert_weights_scale", ctypes.c_float),
+                ("shared_type", ctypes.c_uint32), ("shared_ff", ctypes.c_uint32), ("rotated", ctypes.c_uint32),
+                ("reserved", ctypes.c_uint32)]
+
+
+GX_SHARED_NONE = 0xFFFFFFFF
+
+
 class Timings(ctypes.Structure):
     _fields_ = [("router_ns", ctypes.c_uint64), ("gate_up_ns", ctypes.c_uint64), ("down_ns", ctypes.c_uint64),
                 ("experts_ns", ctypes.c_uint64), ("total_ns", ctypes.c_uint64), ("layers", ctypes.c_uint64)]
 
 
 assert ctypes.sizeof(Options) == 168 and ctypes.sizeof(Caps) == 192 and ctypes.sizeof(LayerDesc) == 112
-assert ctypes.sizeof(SharedDesc) == 64
+assert ctypes.sizeof(SharedDesc) == 64 and ctypes.sizeof(GgufLayerInfo) == 40
 
 # (name, argtypes) of every exported entry point; include/gyro_moe.h declares exactly these.
 _P, _U32, _U64, _F = ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_float
@@ -76,6 +86,8 @@ SIGNATURES = {
     "gx_get_caps": [_P, ctypes.POINTER(Caps)],
     "gx_upload_layer": [_P, _U32, ctypes.POINTER(LayerDesc), _U32],
     "gx_upload_shared": [_P, _U32, ctypes.POINTER(SharedDesc), _U32],
+    "gx_gguf_inspect_layer": [ctypes.c_char_p, _U32, ctypes.POINTER(GgufLayerInfo)],
+    "gx_upload_layer_gguf": [_P, _U32, ctypes.c_char_p, _U32, _U32],
     "gx_moe_forward": [_P, _U32, _P, _U32, _U32, _P, _U32, _P, _P, ctypes.POINTER(_U64)],
     "gx_moe_forward_host": [_P, _U32, _P, _U32, _U32, _P, _U32, _P, _P, _U32],
     "gx_stack_forward": [_P, _U32, _U32, _P, _U32, _U32, _P, _U32, ctypes.POINTER(_U64)],
@@ -141,6 +153,13 @@ def _dtype_code(a) -> int:
     if name == "uint16":  # numpy bf16 bit patterns
         return GX_BF16
     raise ValueError(f"unsupported activation dtype {name}")
+
+
+def gguf_layer_info(path, gguf_layer: int) -> GgufLayerInfo:
+    """gx_gguf_inspect_layer: shapes and types of one layer of a GGUF file (no device needed)."""
+    info = GgufLayerInfo()
+    _check(load().gx_gguf_inspect_layer(str(path).encode(), gguf_layer, ctypes.byref(info)), "gx_gguf_inspect_layer")
+    return info
 
 
 def unique_id() -> bytes:
@@ -224,6 +243,13 @@ class Context:
         desc = SharedDesc(shared["type_id"], shared["n_ff"], mats[0].ctypes.data, mats[1].ctypes.data,
                           mats[2].ctypes.data, mats[0].nbytes, mats[1].nbytes, mats[2].nbytes, gi.ctypes.data)
         _check(self.lib.gx_upload_shared(self.handle, index, ctypes.byref(desc), timeout_ms), "gx_upload_shared")
+
+    def upload_layer_gguf(self, index: int, path, gguf_layer: int, timeout_ms: int = 600000) -> None:
+        """gx_upload_layer_gguf: layer gguf_layer of a GGUF file into slot index."""
+        _check(self.lib.gx_upload_layer_gguf(self.handle, index, str(path).encode(), gguf_layer, timeout_ms),
+               "gx_upload_layer_gguf")
+        info = gguf_layer_info(path, gguf_layer)
+        self.layers[index] = {"n_embd": info.n_embd, "n_used": info.n_used, "n_expert": info.n_expert}
 
     # --- forward ---------------------------------------------------------------------------
     def forward(self, layer: int, x, y, ids=None, weights=None) -> int:

@@ -87,6 +87,21 @@ pub const gx_shared_desc = extern struct {
     gate_inp: ?[*]const f32,
 };
 
+pub const shared_none: u32 = 0xffffffff;
+
+pub const gx_gguf_layer_info = extern struct {
+    type_id: u32,
+    n_expert: u32,
+    n_embd: u32,
+    n_ff: u32,
+    n_used: u32,
+    expert_weights_scale: f32,
+    shared_type: u32,
+    shared_ff: u32,
+    rotated: u32,
+    reserved: u32,
+};
+
 pub const gx_timings = extern struct {
     router_ns: u64,
     gate_up_ns: u64,
@@ -100,6 +115,9 @@ pub extern fn gx_create(options: *const gx_options, context: *?*gx_context) gx_r
 pub extern fn gx_get_caps(context: *gx_context, caps: *gx_caps) gx_result;
 pub extern fn gx_upload_layer(context: *gx_context, layer: u32, desc: *const gx_layer_desc, timeout_ms: u32) gx_result;
 pub extern fn gx_upload_shared(context: *gx_context, layer: u32, desc: ?*const gx_shared_desc, timeout_ms: u32) gx_result;
+pub extern fn gx_gguf_inspect_layer(path: [*:0]const u8, gguf_layer: u32, info: *gx_gguf_layer_info) gx_result;
+pub extern fn gx_upload_layer_gguf(context: *gx_context, layer: u32, path: [*:0]const u8, gguf_layer: u32,
+    timeout_ms: u32) gx_result;
 pub extern fn gx_moe_forward(context: *gx_context, layer: u32, x: ?*const anyopaque, x_dtype: u32, n_tok: u32,
     y: ?*anyopaque, y_dtype: u32, ids: ?[*]u32, weights: ?[*]f32, ticket: ?*u64) gx_result;
 pub extern fn gx_moe_forward_host(context: *gx_context, layer: u32, x: ?*const anyopaque, x_dtype: u32, n_tok: u32,
@@ -140,4 +158,5 @@ comptime {
     assert(@sizeOf(gx_timings) == 48);
     assert(@sizeOf(gx_shared_desc) == 64);
     assert(@offsetOf(gx_shared_desc, "gate_inp") == 56);
+    assert(@sizeOf(gx_gguf_layer_info) == 40);
 }

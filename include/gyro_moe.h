@@ -181,6 +181,37 @@ GX_API gx_result gx_upload_layer(gx_context *context, uint32_t layer, const gx_l
 GX_API gx_result gx_upload_shared(gx_context *context, uint32_t layer, const gx_shared_desc *desc,
                                   uint32_t timeout_ms);
 
+/* ---- layers from a GGUF model file ---------------------------------------------------------
+ * Replaces, for this path, the Zig host's GGUF reader and tensor binding (src/gguf.zig:263-334,
+ * src/model.zig:395-421) and its expert-arena setup (src/gpu_engine.zig:593-668). Layer L of the
+ * file is blk.L.ffn_{gate,up,down}_exps.weight (one Gyro type, stacked experts [E,F,NE] / [F,E,NE]),
+ * blk.L.ffn_gate_inp.weight (router [E,NE], f32, f16 or bf16), optionally the shared expert
+ * blk.L.ffn_{gate,up,down}_shexp.weight and blk.L.ffn_gate_inp_shexp.weight, with U from
+ * <general.architecture>.expert_used_count, expert_weights_scale when present, and the Hadamard
+ * signs the prism.hadamard.* metadata assigns to the expert tensors (by input width). The header
+ * is validated as src/gguf.zig does; a malformed file gives GX_E_INVALIDARG, a well-formed one this
+ * path cannot take (other tensor types, other prism.hadamard versions) GX_E_UNSUPPORTED; with
+ * GX_DEBUG=1 in the environment the reason is printed. */
+#define GX_SHARED_NONE 0xffffffffu
+typedef struct gx_gguf_layer_info {
+    uint32_t type_id;             /* Gyro type of the expert tensors */
+    uint32_t n_expert, n_embd, n_ff, n_used;
+    float expert_weights_scale;
+    uint32_t shared_type;         /* GX_Q8_0 / GX_BF16 / GX_F32, or GX_SHARED_NONE */
+    uint32_t shared_ff;           /* n_ff_shexp (0 without a shared expert) */
+    uint32_t rotated;             /* bit 0: gate/up carry signs, bit 1: down carries signs */
+    uint32_t reserved;
+} gx_gguf_layer_info;             /* 40 bytes */
+
+/* Shapes and types of layer gguf_layer of a file (no device needed), so the host can size its
+ * context before creating it. */
+GX_API gx_result gx_gguf_inspect_layer(const char *path, uint32_t gguf_layer, gx_gguf_layer_info *out_info);
+
+/* gx_upload_layer (and gx_upload_shared when the layer has a shared expert) of layer gguf_layer
+ * of the file into slot layer of the context, reading only the tensors it needs. Blocking. */
+GX_API gx_result gx_upload_layer_gguf(gx_context *context, uint32_t layer, const char *path, uint32_t gguf_layer,
+                                      uint32_t timeout_ms);
+
 /* Routed-expert layer on device-resident activations, enqueued on the context's stream
  * (replaces the dispatch chain of Engine.ffn, src/gpu_engine.zig:1059-1116, through
  * gd_dispatch, native/gyro_native.cpp:891-900):
