@@ -50,6 +50,15 @@ struct Layer {
     uint64_t sh_bytes = 0;
     gx::SharedMat sh_gate{}, sh_up{}, sh_down{};
     float *sh_gate_inp = nullptr;
+    // hyper-connection mixer of the FFN block (gx_upload_hc), in an arena of its own: H streams,
+    // rank padded with zeros to R (a multiple of 128), Down padded with zero rows to Rp (a
+    // multiple of 256) for the tensor-core path
+    uint32_t hc_wt = 0, H = 0, R = 0, Rp = 0;
+    float hc_eps = 0.f;
+    uint8_t *hc_arena = nullptr;
+    uint64_t hc_bytes = 0;
+    gx::SharedMat hc_down{}, hc_up{}, hc_inject{};
+    float *hc_norm = nullptr;
 };
 
 // Copies of hot experts one expert-parallel rank can hold per layer, beside its own shard.
@@ -100,6 +109,16 @@ struct gx_context {
         __half *Ysh = nullptr;
         int *ints = nullptr;  // tile_expert | tile_rows | n_mtiles
     } sh;
+    // FFN-block mixer work buffers for max_tokens tokens of the widest mixer uploaded: normed
+    // streams, low-rank activations, injection logits, the layer's input and output; tensor-core
+    // path: operand tiles of xn and lo, f16 rows of Down xn and Up lo, tile list
+    struct Hc {
+        size_t HD = 0, Rp = 0, E = 0;
+        float *xn = nullptr, *lo = nullptr, *inj = nullptr, *cur = nullptr, *y = nullptr;
+        uint8_t *A = nullptr, *A2 = nullptr;
+        __half *Ylo = nullptr, *gate = nullptr;
+        int *ints = nullptr;  // tile_expert | tile_rows | n_mtiles
+    } hc;
     uint32_t *ids = nullptr;
     int *err = nullptr;
     void *x_stage = nullptr, *y_stage = nullptr;     // device staging (graphs, host calls)
@@ -296,8 +315,11 @@ void release_all(gx_context *c) {
     for (auto &l : c->layers) {
         if (l.arena) cudaFree(l.arena);
         if (l.sh_arena) cudaFree(l.sh_arena);
+        if (l.hc_arena) cudaFree(l.hc_arena);
     }
-    void *sh[] = {c->sh.logit, c->sh.act, c->sh.y, c->sh.A, c->sh.A2, c->sh.pact, c->sh.Ysh, c->sh.ints};
+    void *sh[] = {c->sh.logit, c->sh.act, c->sh.y, c->sh.A, c->sh.A2, c->sh.pact, c->sh.Ysh, c->sh.ints,
+                  c->hc.xn, c->hc.lo, c->hc.inj, c->hc.cur, c->hc.y, c->hc.A, c->hc.A2, c->hc.Ylo, c->hc.gate,
+                  c->hc.ints};
     for (void *p : sh) if (p) cudaFree(p);
     void *pf[] = {c->pf.A, c->pf.A2, c->pf.act, c->pf.Y, c->pf.ints, c->pf.xh};
     for (void *p : pf) if (p) cudaFree(p);
@@ -406,6 +428,120 @@ gx_result ensure_shared(gx_context *c, size_t E, size_t SF) {
     }
     sh.E = E;
     sh.SF = SF;
+    return GX_OK;
+}
+
+// Work buffers of the FFN-block mixer for max_tokens tokens (E, HD = H * E, Rp), grown only.
+gx_result ensure_hc(gx_context *c, size_t E, size_t HD, size_t Rp) {
+    auto &h = c->hc;
+    if (h.E >= E && h.HD >= HD && h.Rp >= Rp) return GX_OK;
+    E = std::max(E, h.E);
+    HD = std::max(HD, h.HD);
+    Rp = std::max(Rp, h.Rp);
+    void *old[] = {h.xn, h.lo, h.inj, h.cur, h.y, h.A, h.A2, h.Ylo, h.gate, h.ints};
+    for (void *q : old) if (q) cudaFree(q);
+    h = gx_context::Hc{};
+    const size_t T = c->max_tokens, tiles = (T + 127) / 128;
+    GX_CUDA(cudaMalloc(&h.xn, T * HD * sizeof(float)));
+    GX_CUDA(cudaMalloc(&h.lo, T * Rp * sizeof(float)));
+    GX_CUDA(cudaMalloc(&h.inj, T * 8 * sizeof(float)));
+    GX_CUDA(cudaMalloc(&h.cur, T * E * sizeof(float)));
+    GX_CUDA(cudaMalloc(&h.y, T * E * sizeof(float)));
+    if (T >= kPrefillMinTokens) {
+        GX_CUDA(cudaMalloc(&h.A, tiles * (HD / 64) * 16384));
+        GX_CUDA(cudaMalloc(&h.A2, tiles * (Rp / 64) * 16384));
+        GX_CUDA(cudaMalloc(&h.Ylo, tiles * 128 * Rp * sizeof(__half)));
+        GX_CUDA(cudaMalloc(&h.gate, tiles * 128 * HD * sizeof(__half)));
+        GX_CUDA(cudaMalloc(&h.ints, (2 * tiles + 1) * sizeof(int)));
+    }
+    h.E = E;
+    h.HD = HD;
+    h.Rp = Rp;
+    return GX_OK;
+}
+
+gx::HcArgs hc_args(gx_context *c, const Layer &L, float *res, uint32_t n_tok) {
+    gx::HcArgs a{};
+    a.wt = L.hc_wt;
+    a.down = L.hc_down;
+    a.up = L.hc_up;
+    a.inject = L.hc_inject;
+    a.norm = L.hc_norm;
+    a.eps = L.hc_eps;
+    a.n_tok = (int)n_tok;
+    a.H = (int)L.H;
+    a.E = (int)L.E;
+    a.R = (int)L.R;
+    a.res = res;
+    a.res_out = res;
+    a.xn = c->hc.xn;
+    a.lo = c->hc.lo;
+    a.inj = c->hc.inj;
+    a.cur = c->hc.cur;
+    return a;
+}
+
+// The mixer in front of the routed layer (src/engine.zig:184-215): per-stream norm, then the two
+// low-rank products and the gated mean into c->hc.cur, and the injection logits into c->hc.inj.
+// Few tokens on the CUDA cores; many tokens through the grouped GEMM with the plain-matrix
+// decoders (one "expert", 128 tokens per row tile), as the reference switches to its tiled
+// products above gemm_min_tok (src/gpu_engine.zig:896, :909-922).
+gx_result enqueue_hc_mix(gx_context *c, const Layer &L, const gx::HcArgs &a) {
+    const uint32_t n_tok = (uint32_t)a.n_tok;
+    GX_CUDA(gx::launch_hc_norm(a, c->stream, false));
+    if (n_tok < kPrefillMinTokens) {
+        GX_CUDA(gx::launch_hc_down(a, 0, c->stream, true));
+        GX_CUDA(gx::launch_hc_up_mix(a, c->stream, true));
+        return GX_OK;
+    }
+    auto &h = c->hc;
+    const int tiles = (int)((c->max_tokens + 127) / 128);
+    const int HD = (int)(L.H * L.E);
+    int *tile_expert = h.ints, *tile_rows = h.ints + tiles, *n_mtiles = h.ints + 2 * tiles;
+    GX_CUDA(gx::launch_shared_tiles((int)n_tok, tile_expert, tile_rows, n_mtiles, c->stream));
+    gx::PackArgs pa{};
+    pa.src = h.xn;
+    pa.U = 1;
+    pa.K = HD;
+    pa.tile_rows = tile_rows;
+    pa.n_mtiles = n_mtiles;
+    pa.dst = h.A;
+    GX_CUDA(gx::launch_pack_rows(pa, tiles, c->stream));
+    gx::GemmArgs gm{};
+    gm.type = L.hc_wt;
+    gm.w0 = L.hc_down.w;
+    gm.d0 = L.hc_down.d;
+    gm.K = HD;
+    gm.n_ntiles = (int)(L.Rp / 256);
+    gm.n_expert = 1;
+    gm.A = h.A;
+    gm.tile_expert = tile_expert;
+    gm.tile_rows = tile_rows;
+    gm.n_mtiles = n_mtiles;
+    gm.Y = h.Ylo;
+    gm.E = (int)L.Rp;
+    gm.codebook = c->codebook;
+    gm.err = c->err;
+    GX_CUDA(gx::launch_moe_gemm(gm, 1, c->sm_count, c->stream));
+    GX_CUDA(gx::launch_hc_down(a, (int)L.R, c->stream, false));   // the injection rows
+    GX_CUDA(gx::launch_hc_lo(a, h.Ylo, (int)L.Rp, c->stream));
+    gx::PackArgs pl{};
+    pl.src = h.lo;
+    pl.U = 1;
+    pl.K = (int)L.R;
+    pl.tile_rows = tile_rows;
+    pl.n_mtiles = n_mtiles;
+    pl.dst = h.A2;
+    GX_CUDA(gx::launch_pack_rows(pl, tiles, c->stream));
+    gm.w0 = L.hc_up.w;
+    gm.d0 = L.hc_up.d;
+    gm.K = (int)L.R;
+    gm.n_ntiles = HD / 256;
+    gm.A = h.A2;
+    gm.Y = h.gate;
+    gm.E = HD;
+    GX_CUDA(gx::launch_moe_gemm(gm, 1, c->sm_count, c->stream));
+    GX_CUDA(gx::launch_hc_mix(a, h.gate, c->stream));
     return GX_OK;
 }
 
@@ -1541,7 +1677,7 @@ GX_API gx_result gx_get_caps(gx_context *c, gx_caps *caps) {
     caps->hbm_bytes = total_b;
     caps->free_bytes = free_b;
     caps->l2_bytes = (uint64_t)prop.l2CacheSize;
-    for (auto &l : c->layers) caps->arena_bytes += l.bytes + l.sh_bytes;
+    for (auto &l : c->layers) caps->arena_bytes += l.bytes + l.sh_bytes + l.hc_bytes;
     for (auto &m : c->mats) caps->arena_bytes += (uint64_t)m.rows / 8 * (m.cols / 128) * gx::tile_bytes(m.type);
     std::strncpy(caps->device_name, prop.name, sizeof(caps->device_name) - 1);
     caps->ep_exchange = c->ep.peer_state == 1 ? GX_EP_PEER : c->ep.peer_state == -1 ? GX_EP_NCCL : GX_EP_NONE;
@@ -1582,6 +1718,7 @@ GX_API gx_result gx_upload_layer(gx_context *c, uint32_t layer, const gx_layer_d
         if (r != GX_OK) return r;
         cudaFree(L.arena);
         if (L.sh_arena) cudaFree(L.sh_arena);
+        if (L.hc_arena) cudaFree(L.hc_arena);
         L = Layer{};
     }
     const uint64_t NEl = NE / c->world, first = c->rank * NEl;
@@ -1694,6 +1831,72 @@ GX_API gx_result gx_upload_layer(gx_context *c, uint32_t layer, const gx_layer_d
     return GX_OK;
 }
 
+namespace {
+
+// Bytes of one source row of cols values in a non-expert encoding (0: not one of them).
+uint64_t dense_row_bytes(uint32_t type, uint64_t cols) {
+    if (type == GX_Q8_0) return cols % 32 ? 0 : cols / 32 * 34;
+    if (type == GX_BF16) return cols * 2;
+    if (type == GX_F32) return cols * 4;
+    return 0;
+}
+
+// A plain row-major matrix in host memory (src/gguf.zig's row layout of Q8_0, bf16 and f32).
+struct DenseMat {
+    const uint8_t *src;
+    uint64_t rows, cols, row_bytes;
+};
+
+// Arena offsets of a matrix's device encoding: weights at *o_w, Q8_0 block scales at *o_d.
+void dense_place(uint32_t type, const DenseMat &m, uint64_t *off, uint64_t *o_w, uint64_t *o_d) {
+    const bool q8 = type == GX_Q8_0;
+    *o_w = *off;
+    *off = align256(*off + m.rows * m.cols * (q8 ? 1 : 2));
+    *o_d = *off;
+    *off = align256(*off + (q8 ? m.rows * (m.cols / 32) * 2 : 0));
+}
+
+// Device encoding into zeroed host memory: Q8_0 split into int8 weights w [rows][ld] and fp16
+// block scales d [rows][ld/32]; bf16 and f32 as fp16 w [rows][ld] (bf16 values convert exactly
+// within the fp16 range, f32 values are rounded once). ld >= cols (0: cols); columns past cols
+// stay zero.
+void dense_encode(uint32_t type, const DenseMat &M, uint8_t *w_out, uint8_t *d_out, uint64_t ld = 0) {
+    if (ld == 0) ld = M.cols;
+    for (uint64_t r = 0; r < M.rows; ++r) {
+        const uint8_t *row = M.src + r * M.row_bytes;
+        if (type == GX_Q8_0) {
+            int8_t *w = reinterpret_cast<int8_t *>(w_out) + r * ld;
+            uint16_t *sc = reinterpret_cast<uint16_t *>(d_out) + r * (ld / 32);
+            for (uint64_t b = 0; b < M.cols / 32; ++b) {
+                std::memcpy(&sc[b], row + 34 * b, 2);
+                std::memcpy(&w[32 * b], row + 34 * b + 2, 32);
+            }
+        } else {
+            __half *w = reinterpret_cast<__half *>(w_out) + r * ld;
+            for (uint64_t i = 0; i < M.cols; ++i) {
+                float v;
+                if (type == GX_BF16) {
+                    const uint32_t bits = ((uint32_t)row[2 * i] | ((uint32_t)row[2 * i + 1] << 8)) << 16;
+                    std::memcpy(&v, &bits, 4);
+                } else {
+                    std::memcpy(&v, row + 4 * i, 4);
+                }
+                w[i] = __float2half_rn(v);
+            }
+        }
+    }
+}
+
+void drop_graphs(gx_context *c) {
+    for (auto &kv : c->graphs) {
+        cudaGraphExecDestroy(kv.second.second);
+        cudaGraphDestroy(kv.second.first);
+    }
+    c->graphs.clear();
+}
+
+}  // namespace
+
 GX_API gx_result gx_upload_shared(gx_context *c, uint32_t layer, const gx_shared_desc *d, uint32_t timeout_ms) {
     if (!c) return GX_E_INVALIDARG;
     if (c->broken) return GX_E_DEVICE;
@@ -1704,18 +1907,9 @@ GX_API gx_result gx_upload_shared(gx_context *c, uint32_t layer, const gx_shared
     if (d) {
         SF = d->n_ff;
         if (SF == 0 || SF % 128 || SF > 4096 || !d->gate || !d->up || !d->down || !d->gate_inp) return GX_E_INVALIDARG;
-        if (d->type_id == GX_Q8_0) {
-            row_in = E / 32 * 34;
-            row_sf = SF / 32 * 34;
-        } else if (d->type_id == GX_BF16) {
-            row_in = E * 2;
-            row_sf = SF * 2;
-        } else if (d->type_id == GX_F32) {
-            row_in = E * 4;
-            row_sf = SF * 4;
-        } else {
-            return GX_E_INVALIDARG;
-        }
+        row_in = dense_row_bytes(d->type_id, E);
+        row_sf = dense_row_bytes(d->type_id, SF);
+        if (!row_in || !row_sf) return GX_E_INVALIDARG;
         if (d->gate_bytes != SF * row_in || d->up_bytes != SF * row_in || d->down_bytes != E * row_sf)
             return GX_E_INVALIDARG;
         if (E % 256) return GX_E_UNSUPPORTED;
@@ -1739,49 +1933,16 @@ GX_API gx_result gx_upload_shared(gx_context *c, uint32_t layer, const gx_shared
     c->graphs.clear();
     if (!d) return GX_OK;
 
-    // Device encodings: Q8_0 split into int8 weights and fp16 block scales; bf16 and f32 as fp16.
     const bool q8 = d->type_id == GX_Q8_0;
-    struct Mat { const uint8_t *src; uint64_t rows, cols, row_bytes; };
-    const Mat mats[3] = {{static_cast<const uint8_t *>(d->gate), SF, E, row_in},
-                         {static_cast<const uint8_t *>(d->up), SF, E, row_in},
-                         {static_cast<const uint8_t *>(d->down), E, SF, row_sf}};
+    const DenseMat mats[3] = {{static_cast<const uint8_t *>(d->gate), SF, E, row_in},
+                              {static_cast<const uint8_t *>(d->up), SF, E, row_in},
+                              {static_cast<const uint8_t *>(d->down), E, SF, row_sf}};
     uint64_t off = 0, o_w[3], o_d[3];
-    for (int m = 0; m < 3; ++m) {
-        o_w[m] = off;
-        off = align256(off + mats[m].rows * mats[m].cols * (q8 ? 1 : 2));
-        o_d[m] = off;
-        off = align256(off + (q8 ? mats[m].rows * (mats[m].cols / 32) * 2 : 0));
-    }
+    for (int m = 0; m < 3; ++m) dense_place(d->type_id, mats[m], &off, &o_w[m], &o_d[m]);
     const uint64_t o_gi = off;
     off = align256(off + E * 4);
     std::vector<uint8_t> host(off, 0);
-    for (int m = 0; m < 3; ++m) {
-        const Mat &M = mats[m];
-        for (uint64_t r = 0; r < M.rows; ++r) {
-            const uint8_t *row = M.src + r * M.row_bytes;
-            if (q8) {
-                int8_t *w = reinterpret_cast<int8_t *>(host.data() + o_w[m]) + r * M.cols;
-                uint16_t *sc = reinterpret_cast<uint16_t *>(host.data() + o_d[m]) + r * (M.cols / 32);
-                for (uint64_t b = 0; b < M.cols / 32; ++b) {
-                    std::memcpy(&sc[b], row + 34 * b, 2);
-                    std::memcpy(&w[32 * b], row + 34 * b + 2, 32);
-                }
-            } else {
-                __half *w = reinterpret_cast<__half *>(host.data() + o_w[m]) + r * M.cols;
-                for (uint64_t i = 0; i < M.cols; ++i) {
-                    float v;
-                    if (d->type_id == GX_BF16) {
-                        uint32_t bits = (uint32_t)row[2 * i] | ((uint32_t)row[2 * i + 1] << 8);
-                        bits <<= 16;
-                        std::memcpy(&v, &bits, 4);
-                    } else {
-                        std::memcpy(&v, row + 4 * i, 4);
-                    }
-                    w[i] = __float2half_rn(v);
-                }
-            }
-        }
-    }
+    for (int m = 0; m < 3; ++m) dense_encode(d->type_id, mats[m], host.data() + o_w[m], host.data() + o_d[m]);
     std::memcpy(host.data() + o_gi, d->gate_inp, E * 4);
     gx_result r = ensure_shared(c, E, SF);
     if (r != GX_OK) return r;
@@ -1802,6 +1963,82 @@ GX_API gx_result gx_upload_shared(gx_context *c, uint32_t layer, const gx_shared
         dst[m]->d = q8 ? reinterpret_cast<const __half *>(arena + o_d[m]) : nullptr;
     }
     L.sh_gate_inp = reinterpret_cast<float *>(arena + o_gi);
+    return GX_OK;
+}
+
+GX_API gx_result gx_upload_hc(gx_context *c, uint32_t layer, const gx_hc_desc *d, uint32_t timeout_ms) {
+    if (!c) return GX_E_INVALIDARG;
+    if (c->broken) return GX_E_DEVICE;
+    if (layer >= c->layers.size() || !c->layers[layer].ready) return GX_E_STATE;
+    Layer &L = c->layers[layer];
+    const uint64_t E = L.E;
+    uint64_t H = 0, R = 0, HD = 0, row_hd = 0, row_r = 0;
+    if (d) {
+        H = d->n_streams;
+        R = d->rank;
+        HD = H * E;
+        if (H == 0 || H > 8 || R == 0 || R % 64 || R > 4096 || !d->norm || !d->down || !d->up || !d->inject ||
+            !(d->eps > 0.f))
+            return GX_E_INVALIDARG;
+        row_hd = dense_row_bytes(d->type_id, HD);
+        row_r = dense_row_bytes(d->type_id, R);
+        if (!row_hd || !row_r) return GX_E_INVALIDARG;
+        if (d->down_bytes != R * row_hd || d->up_bytes != HD * row_r || d->inject_bytes != H * row_hd)
+            return GX_E_INVALIDARG;
+        if (E % 256) return GX_E_UNSUPPORTED;
+    }
+    GX_CUDA(cudaSetDevice(c->device));
+    if (L.hc_arena) {
+        gx_result r = sync_all(c, timeout_ms);  // queued blocks may still read the old weights
+        if (r != GX_OK) return r;
+        cudaFree(L.hc_arena);
+    }
+    L.hc_arena = nullptr;
+    L.hc_bytes = 0;
+    L.hc_wt = L.H = L.R = L.Rp = 0;
+    L.hc_down = L.hc_up = L.hc_inject = gx::SharedMat{};
+    L.hc_norm = nullptr;
+    if (!d) return GX_OK;
+
+    // The rank is padded with zeros to Rk (a multiple of 128, the operand packing's block): Up gets
+    // zero columns, Down zero rows, and lo = silu(0) = 0 there, so every sum is unchanged. Down has
+    // Rp >= Rk rows (a multiple of 256) for the tensor-core path's column tiles of Down xn.
+    const uint64_t Rk = (R + 127) / 128 * 128, Rp = (R + 255) / 256 * 256;
+    const DenseMat mats[3] = {{static_cast<const uint8_t *>(d->down), R, HD, row_hd},
+                              {static_cast<const uint8_t *>(d->up), HD, R, row_r},
+                              {static_cast<const uint8_t *>(d->inject), H, HD, row_hd}};
+    const DenseMat shapes[3] = {{nullptr, Rp, HD, 0}, {nullptr, HD, Rk, 0}, mats[2]};
+    uint64_t off = 0, o_w[3], o_d[3];
+    for (int m = 0; m < 3; ++m) dense_place(d->type_id, shapes[m], &off, &o_w[m], &o_d[m]);
+    const uint64_t o_norm = off;
+    off = align256(off + HD * 4);
+    std::vector<uint8_t> host(off, 0);
+    for (int m = 0; m < 3; ++m)
+        dense_encode(d->type_id, mats[m], host.data() + o_w[m], host.data() + o_d[m], shapes[m].cols);
+    std::memcpy(host.data() + o_norm, d->norm, HD * 4);
+    gx_result r = ensure_hc(c, E, HD, Rp);
+    if (r != GX_OK) return r;
+    uint8_t *arena = nullptr;
+    GX_CUDA(cudaMalloc(&arena, off));
+    cudaError_t e = cudaMemcpy(arena, host.data(), off, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(arena);
+        return fail_cuda(c, e);
+    }
+    const bool q8 = d->type_id == GX_Q8_0;
+    L.hc_arena = arena;
+    L.hc_bytes = off;
+    L.hc_wt = q8 ? gx::W_Q8 : gx::W_F16;
+    L.H = (uint32_t)H;
+    L.R = (uint32_t)Rk;
+    L.Rp = (uint32_t)Rp;
+    L.hc_eps = d->eps;
+    gx::SharedMat *dst[3] = {&L.hc_down, &L.hc_up, &L.hc_inject};
+    for (int m = 0; m < 3; ++m) {
+        dst[m]->w = arena + o_w[m];
+        dst[m]->d = q8 ? reinterpret_cast<const __half *>(arena + o_d[m]) : nullptr;
+    }
+    L.hc_norm = reinterpret_cast<float *>(arena + o_norm);
     return GX_OK;
 }
 
@@ -1833,6 +2070,34 @@ GX_API gx_result gx_moe_forward(gx_context *c, uint32_t layer, const void *x, ui
         if (weights)
             GX_CUDA(cudaMemcpyAsync(weights, c->weights, (size_t)n_tok * L.U * 4, cudaMemcpyDeviceToDevice, c->stream));
     }
+    return record_ticket(c, out_ticket);
+}
+
+GX_API gx_result gx_ffn_block(gx_context *c, uint32_t layer, float *res, uint32_t n_tok, float *mixed,
+                              uint64_t *out_ticket) {
+    gx_result r = check_forward(c, layer, GX_F32, n_tok, GX_F32);
+    if (r != GX_OK) return r;
+    const Layer &L = c->layers[layer];
+    if (!L.hc_wt) return GX_E_STATE;
+    if (n_tok > 0 && (!res || ((uintptr_t)res & 15) || ((uintptr_t)mixed & 3))) return GX_E_INVALIDARG;
+    GX_CUDA(cudaSetDevice(c->device));
+    if (c->world > 1) {  // every rank takes part in the layer's exchange, also with no tokens
+        r = ep_sync_ntok(c, n_tok);
+        if (r != GX_OK) return r;
+    } else if (n_tok == 0) {
+        return record_ticket(c, out_ticket);
+    }
+    const gx::HcArgs a = hc_args(c, L, res, n_tok);
+    if (n_tok > 0) {
+        r = enqueue_hc_mix(c, L, a);
+        if (r != GX_OK) return r;
+        if (mixed)
+            GX_CUDA(cudaMemcpyAsync(mixed, c->hc.cur, (size_t)n_tok * L.E * sizeof(float), cudaMemcpyDeviceToDevice,
+                                    c->stream));
+    }
+    r = enqueue_layer(c, L, c->hc.cur, GX_F32, n_tok, nullptr, GX_F32, c->hc.y, GX_F32, -1, 0.f, false);
+    if (r != GX_OK) return r;
+    if (n_tok > 0) GX_CUDA(gx::launch_hc_combine(a, c->hc.y, c->stream, false));
     return record_ticket(c, out_ticket);
 }
 

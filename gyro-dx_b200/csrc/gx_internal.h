@@ -106,6 +106,31 @@ cudaError_t launch_shared_logits(const SharedArgs &a, cudaStream_t s);
 // Tile list of the shared expert on the tensor-core path: every token in order, 128 per tile.
 cudaError_t launch_shared_tiles(int n_tok, int *tile_expert, int *tile_rows, int *n_mtiles, cudaStream_t s);
 
+// Hyper-connection mixer of the FFN block (H residual streams of E, low rank R).
+struct HcArgs {
+    uint32_t wt;             // W_Q8 or W_F16
+    SharedMat down;          // [R][H*E]
+    SharedMat up;            // [H*E][R]
+    SharedMat inject;        // [H][H*E]
+    const float *norm;       // [H*E] per-stream RMSNorm weights
+    float eps;
+    int n_tok, H, E, R;
+    const float *res;        // [n_tok][H*E] residual streams (read by the norm)
+    float *res_out;          // the same streams, updated by the combine
+    float *xn;               // [n_tok][H*E] normed streams
+    float *lo;               // [n_tok][R]
+    float *inj;              // [n_tok][H]
+    float *cur;              // [n_tok][E] the routed layer's input
+};
+cudaError_t launch_hc_norm(const HcArgs &a, cudaStream_t s, bool pdl);
+// Rows [row0, R + H) of Down | Inject on the CUDA cores (row0 = R: the injection rows alone).
+cudaError_t launch_hc_down(const HcArgs &a, int row0, cudaStream_t s, bool pdl);
+cudaError_t launch_hc_up_mix(const HcArgs &a, cudaStream_t s, bool pdl);
+// Tensor-core path: lo from the Down GEMM's f16 rows (stride Rp), cur from the Up GEMM's f16 rows.
+cudaError_t launch_hc_lo(const HcArgs &a, const __half *Ylo, int Rp, cudaStream_t s);
+cudaError_t launch_hc_mix(const HcArgs &a, const __half *gate, cudaStream_t s);
+cudaError_t launch_hc_combine(const HcArgs &a, const float *y, cudaStream_t s, bool pdl);
+
 struct DownArgs {
     uint32_t type;
     const uint8_t *down;     // tiles of local expert 0

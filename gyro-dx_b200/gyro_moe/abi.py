@@ -60,6 +60,13 @@ class SharedDesc(ctypes.Structure):
                 ("up_bytes", ctypes.c_uint64), ("down_bytes", ctypes.c_uint64), ("gate_inp", ctypes.c_void_p)]
 
 
+class HcDesc(ctypes.Structure):
+    _fields_ = [("n_streams", ctypes.c_uint32), ("rank", ctypes.c_uint32), ("type_id", ctypes.c_uint32),
+                ("eps", ctypes.c_float), ("norm", ctypes.c_void_p), ("down", ctypes.c_void_p),
+                ("up", ctypes.c_void_p), ("inject", ctypes.c_void_p), ("down_bytes", ctypes.c_uint64),
+                ("up_bytes", ctypes.c_uint64), ("inject_bytes", ctypes.c_uint64)]
+
+
 class GgufLayerInfo(ctypes.Structure):
     _fields_ = [("type_id", ctypes.c_uint32), ("n_expert", ctypes.c_uint32), ("n_embd", ctypes.c_uint32),
                 ("n_ff", ctypes.c_uint32), ("n_used", ctypes.c_uint32), ("expert_weights_scale", ctypes.c_float),
@@ -76,7 +83,7 @@ class Timings(ctypes.Structure):
 
 
 assert ctypes.sizeof(Options) == 168 and ctypes.sizeof(Caps) == 192 and ctypes.sizeof(LayerDesc) == 112
-assert ctypes.sizeof(SharedDesc) == 64 and ctypes.sizeof(GgufLayerInfo) == 40
+assert ctypes.sizeof(SharedDesc) == 64 and ctypes.sizeof(GgufLayerInfo) == 40 and ctypes.sizeof(HcDesc) == 72
 
 # (name, argtypes) of every exported entry point; include/gyro_moe.h declares exactly these.
 _P, _U32, _U64, _F = ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_float
@@ -86,6 +93,8 @@ SIGNATURES = {
     "gx_get_caps": [_P, ctypes.POINTER(Caps)],
     "gx_upload_layer": [_P, _U32, ctypes.POINTER(LayerDesc), _U32],
     "gx_upload_shared": [_P, _U32, ctypes.POINTER(SharedDesc), _U32],
+    "gx_upload_hc": [_P, _U32, ctypes.POINTER(HcDesc), _U32],
+    "gx_ffn_block": [_P, _U32, _P, _U32, _P, ctypes.POINTER(_U64)],
     "gx_gguf_inspect_layer": [ctypes.c_char_p, _U32, ctypes.POINTER(GgufLayerInfo)],
     "gx_upload_layer_gguf": [_P, _U32, ctypes.c_char_p, _U32, _U32],
     "gx_moe_forward": [_P, _U32, _P, _U32, _U32, _P, _U32, _P, _P, ctypes.POINTER(_U64)],
@@ -244,6 +253,17 @@ class Context:
                           mats[2].ctypes.data, mats[0].nbytes, mats[1].nbytes, mats[2].nbytes, gi.ctypes.data)
         _check(self.lib.gx_upload_shared(self.handle, index, ctypes.byref(desc), timeout_ms), "gx_upload_shared")
 
+    def upload_hc(self, index: int, hc: dict | None, timeout_ms: int = 600000) -> None:
+        """gx_upload_hc: the FFN block's hyper-connection mixer (synth.make_hc layout), or None."""
+        if hc is None:
+            _check(self.lib.gx_upload_hc(self.handle, index, None, timeout_ms), "gx_upload_hc")
+            return
+        mats = [np.ascontiguousarray(hc[k], dtype=np.uint8) for k in ("down", "up", "inject")]
+        norm = np.ascontiguousarray(hc["norm"], dtype=np.float32)
+        desc = HcDesc(hc["n_streams"], hc["rank"], hc["type_id"], hc["eps"], norm.ctypes.data, mats[0].ctypes.data,
+                      mats[1].ctypes.data, mats[2].ctypes.data, mats[0].nbytes, mats[1].nbytes, mats[2].nbytes)
+        _check(self.lib.gx_upload_hc(self.handle, index, ctypes.byref(desc), timeout_ms), "gx_upload_hc")
+
     def upload_layer_gguf(self, index: int, path, gguf_layer: int, timeout_ms: int = 600000) -> None:
         """gx_upload_layer_gguf: layer gguf_layer of a GGUF file into slot index."""
         _check(self.lib.gx_upload_layer_gguf(self.handle, index, str(path).encode(), gguf_layer, timeout_ms),
@@ -258,6 +278,14 @@ class Context:
         n_tok = x.shape[0]
         _check(self.lib.gx_moe_forward(self.handle, layer, _ptr(x), _dtype_code(x), n_tok, _ptr(y), _dtype_code(y),
                                        _ptr(ids), _ptr(weights), ctypes.byref(t)), "gx_moe_forward")
+        return t.value
+
+    def ffn_block(self, layer: int, res, n_tok: int | None = None, mixed=None) -> int:
+        """gx_ffn_block on a device f32 tensor res [n_tok, hc * n_embd], updated in place; mixed
+        (optional device f32 [n_tok, n_embd]) receives the mixer's output. Returns the ticket."""
+        t = ctypes.c_uint64()
+        n = res.shape[0] if n_tok is None else n_tok
+        _check(self.lib.gx_ffn_block(self.handle, layer, _ptr(res), n, _ptr(mixed), ctypes.byref(t)), "gx_ffn_block")
         return t.value
 
     def expert_counts(self, layer: int, reset: bool = False, timeout_ms: int = 60000) -> np.ndarray:

@@ -16,9 +16,9 @@ PKG = Path(__file__).resolve().parent
 CSRC = PKG.parent / "csrc"
 ROOT = PKG.parents[1]
 LIB = PKG / "libgyromoe.so"
-SOURCES = ["gx_kernels.cu", "gx_decode_stack.cu", "gx_prefill.cu", "gx_router_tc.cu", "gx_ep.cu", "gx_shared.cu",
+SOURCES = ["gx_kernels.cu", "gx_decode_stack.cu", "gx_prefill.cu", "gx_router_tc.cu", "gx_ep.cu", "gx_shared.cu", "gx_hc.cu",
            "gx_comm.cu", "gx_abi.cu", "gx_gguf.cpp"]
-HEADERS = ["gx_tile.h", "gx_device.cuh", "gx_gemv.cuh", "gx_internal.h", "gx_umma.cuh", "gx_comm.h"]
+HEADERS = ["gx_tile.h", "gx_device.cuh", "gx_gemv.cuh", "gx_internal.h", "gx_umma.cuh", "gx_comm.h", "gx_dense.cuh"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-fvisibility=hidden", "--expt-relaxed-constexpr",

@@ -82,19 +82,39 @@ def make_shared(seed: int, E: int = 2048, SF: int = 512, type_id: int = 8) -> di
     rng = np.random.default_rng(seed)
 
     def mat(rows: int, cols: int) -> np.ndarray:
-        if type_id == 8:
-            q = rng.integers(-127, 128, (rows, cols // 32, 32), dtype=np.int8)
-            d = np.full((rows, cols // 32, 1), fp16_bits(1.0 / (73.0 * np.sqrt(cols))), np.uint16)
-            return np.concatenate([d.view(np.uint8), q.view(np.uint8)], axis=2).reshape(rows, cols // 32 * 34)
-        w = rng.normal(0.0, 1.0 / np.sqrt(cols), size=(rows, cols)).astype(np.float32)
-        if type_id == 30:
-            return bf16_bits(w).view(np.uint8).reshape(rows, cols * 2)
-        if type_id == 0:
-            return w.view(np.uint8).reshape(rows, cols * 4)
-        raise ValueError(f"unsupported shared-expert type {type_id}")
+        return dense_matrix(rng, type_id, rows, cols, 1.0 / np.sqrt(cols))
 
     return {"type_id": type_id, "n_ff": SF, "gate": mat(SF, E), "up": mat(SF, E), "down": mat(E, SF),
             "gate_inp": rng.normal(0.0, 0.02, size=E).astype(np.float32)}
+
+
+def dense_matrix(rng: np.random.Generator, type_id: int, rows: int, cols: int, std: float) -> np.ndarray:
+    """Row-major bytes of a plain matrix with weights of about the given deviation: Q8_0 (blocks of
+    an fp16 scale d = fp16(std / 73) and 32 int8 ~U[-127, 127]), bf16 or f32 (~N(0, std^2))."""
+    if type_id == 8:
+        q = rng.integers(-127, 128, (rows, cols // 32, 32), dtype=np.int8)
+        d = np.full((rows, cols // 32, 1), fp16_bits(std / 73.0), np.uint16)
+        return np.concatenate([d.view(np.uint8), q.view(np.uint8)], axis=2).reshape(rows, cols // 32 * 34)
+    w = rng.normal(0.0, std, size=(rows, cols)).astype(np.float32)
+    if type_id == 30:
+        return bf16_bits(w).view(np.uint8).reshape(rows, cols * 2)
+    if type_id == 0:
+        return w.view(np.uint8).reshape(rows, cols * 4)
+    raise ValueError(f"unsupported non-expert type {type_id}")
+
+
+def make_hc(seed: int, E: int = 2048, n_streams: int = 4, rank: int = 256, eps: float = 1e-6,
+            type_id: int = 8) -> dict:
+    """Hyper-connection mixer weights of the FFN block (src/model.zig:361-366: hc_ffn_norm, down,
+    up, inject) in one non-expert encoding (Q8_0 by default); norm weights ~1 + N(0, 0.1).
+    HD = n_streams * E. The reference model has 4 streams of rank 320."""
+    rng = np.random.default_rng(seed)
+    HD = n_streams * E
+    return {"n_streams": n_streams, "rank": rank, "n_embd": E, "type_id": type_id, "eps": eps,
+            "norm": (1.0 + 0.1 * rng.standard_normal(HD)).astype(np.float32),
+            "down": dense_matrix(rng, type_id, rank, HD, 1.0 / np.sqrt(HD)),
+            "up": dense_matrix(rng, type_id, HD, rank, 1.0 / np.sqrt(rank)),
+            "inject": dense_matrix(rng, type_id, n_streams, HD, 1.0 / np.sqrt(HD))}
 
 
 def tokens(seed: int, n: int, E: int = 2048, dtype=np.float32) -> np.ndarray:

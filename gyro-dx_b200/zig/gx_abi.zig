@@ -89,6 +89,20 @@ pub const gx_shared_desc = extern struct {
 
 pub const shared_none: u32 = 0xffffffff;
 
+pub const gx_hc_desc = extern struct {
+    n_streams: u32,
+    rank: u32,
+    type_id: u32,
+    eps: f32,
+    norm: ?[*]const f32,
+    down: ?*const anyopaque,
+    up: ?*const anyopaque,
+    inject: ?*const anyopaque,
+    down_bytes: u64,
+    up_bytes: u64,
+    inject_bytes: u64,
+};
+
 pub const gx_gguf_layer_info = extern struct {
     type_id: u32,
     n_expert: u32,
@@ -115,6 +129,9 @@ pub extern fn gx_create(options: *const gx_options, context: *?*gx_context) gx_r
 pub extern fn gx_get_caps(context: *gx_context, caps: *gx_caps) gx_result;
 pub extern fn gx_upload_layer(context: *gx_context, layer: u32, desc: *const gx_layer_desc, timeout_ms: u32) gx_result;
 pub extern fn gx_upload_shared(context: *gx_context, layer: u32, desc: ?*const gx_shared_desc, timeout_ms: u32) gx_result;
+pub extern fn gx_upload_hc(context: *gx_context, layer: u32, desc: ?*const gx_hc_desc, timeout_ms: u32) gx_result;
+pub extern fn gx_ffn_block(context: *gx_context, layer: u32, res: ?[*]f32, n_tok: u32, mixed: ?[*]f32,
+    ticket: ?*u64) gx_result;
 pub extern fn gx_gguf_inspect_layer(path: [*:0]const u8, gguf_layer: u32, info: *gx_gguf_layer_info) gx_result;
 pub extern fn gx_upload_layer_gguf(context: *gx_context, layer: u32, path: [*:0]const u8, gguf_layer: u32,
     timeout_ms: u32) gx_result;
@@ -159,4 +176,6 @@ comptime {
     assert(@sizeOf(gx_shared_desc) == 64);
     assert(@offsetOf(gx_shared_desc, "gate_inp") == 56);
     assert(@sizeOf(gx_gguf_layer_info) == 40);
+    assert(@sizeOf(gx_hc_desc) == 72);
+    assert(@offsetOf(gx_hc_desc, "down_bytes") == 48);
 }

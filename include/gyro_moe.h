@@ -181,6 +181,41 @@ GX_API gx_result gx_upload_layer(gx_context *context, uint32_t layer, const gx_l
 GX_API gx_result gx_upload_shared(gx_context *context, uint32_t layer, const gx_shared_desc *desc,
                                   uint32_t timeout_ms);
 
+/* ---- the FFN block with its hyper-connection mixer -----------------------------------------
+ * The reference model keeps hc residual streams per token and reaches each routed layer through a
+ * low-rank mixer (src/engine.zig:162-165, :184-228; src/gpu_engine.zig:891-928 with the hc_pre /
+ * hc_post / hc_mix / hc_combine kernels of its engine shaders). The mixer weights of one layer's
+ * FFN block are blk.L.hc_ffn_{norm,down,up,inject}.weight (src/model.zig:361-366) in one
+ * non-expert encoding: GX_Q8_0, GX_BF16 or GX_F32 (stored on the device as for the shared expert). */
+typedef struct gx_hc_desc {
+    uint32_t n_streams;           /* hc: 1..8 residual streams of n_embd each (HD = hc * n_embd) */
+    uint32_t rank;                /* hc_rank: multiple of 64, at most 4096 (320 in the reference model) */
+    uint32_t type_id;             /* GX_Q8_0, GX_BF16 or GX_F32 of down / up / inject */
+    float eps;                    /* RMSNorm epsilon of the per-stream norm */
+    const float *norm;            /* [HD] f32 per-stream norm weights, host memory */
+    const void *down;             /* [rank rows][HD], host memory */
+    const void *up;               /* [HD rows][rank] */
+    const void *inject;           /* [hc rows][HD] */
+    uint64_t down_bytes, up_bytes, inject_bytes;
+} gx_hc_desc;
+
+/* Attaches the FFN block's mixer to an uploaded layer (desc NULL removes it). Needs n_embd to be a
+ * multiple of 256. Blocking. No counterpart function in the reference bridge: its host binds these
+ * tensors with the rest of the layer (src/gpu_engine.zig:351-354). */
+GX_API gx_result gx_upload_hc(gx_context *context, uint32_t layer, const gx_hc_desc *desc, uint32_t timeout_ms);
+
+/* One FFN block on device-resident residual streams, enqueued on the context's stream:
+ *   cur, inj = hcMix(res)        xn_c = RMSNorm(res_c) * norm_c, lo = silu(Down xn / hc),
+ *                                cur = mean_c xn_c * sigmoid((Up lo)_c), inj = Inject xn
+ *   y = the layer on cur         routed experts (+ shared expert), as gx_moe_forward
+ *   res_c += y * 2 sigmoid(inj_c / hc)
+ * res: [n_tok][hc * n_embd] f32 device, updated in place. mixed: optional device [n_tok][n_embd]
+ * f32 output of cur (the hc_mixed observation, src/engine.zig:210), or NULL. The layer needs
+ * gx_upload_hc. With world > 1 it is a collective like gx_moe_forward (the mixer itself runs on
+ * each rank's own tokens). out_ticket: optional; completes when res is written. */
+GX_API gx_result gx_ffn_block(gx_context *context, uint32_t layer, float *res, uint32_t n_tok, float *mixed,
+                              uint64_t *out_ticket);
+
 /* ---- layers from a GGUF model file ---------------------------------------------------------
  * Replaces, for this path, the Zig host's GGUF reader and tensor binding (src/gguf.zig:263-334,
  * src/model.zig:395-421) and its expert-arena setup (src/gpu_engine.zig:593-668). Layer L of the

@@ -683,3 +683,81 @@ int gxo_shared_expert(const gxo_shared *s, const float *x, size_t n, size_t E, f
     free(g); free(u); free(d);
     return 0;
 }
+
+/* ---- hyper-connection mixer around the FFN block, src/engine.zig:184-228 ------------------
+ * res [n][hc*E] holds hc residual streams per token. hc_mix: per stream RMSNorm with its weight,
+ * lo = silu((Down xn) / hc), gate = Up lo, out = mean over streams of xn * sigmoid(gate), and the
+ * injection weights Inject xn; hc_combine: res[c] += block_out * 2 sigmoid(inject[c] / hc). */
+typedef struct hc_ctx {
+    const gxo_hc *w;
+    size_t n, HD, R, rb_hd, rb_r;
+    const float *xn, *lo;
+    float *lo_out, *gate, *inj;
+} hc_ctx;
+
+static void hc_down_range(void *p, size_t a, size_t b) {
+    hc_ctx *c = (hc_ctx *)p;
+    for (size_t r = a; r < b; ++r)
+        for (size_t t = 0; t < c->n; ++t)
+            c->lo_out[t * c->R + r] = gxo_dot_row(c->w->type_id, c->w->down + r * c->rb_hd, c->xn + t * c->HD, c->HD);
+}
+
+static void hc_up_range(void *p, size_t a, size_t b) {
+    hc_ctx *c = (hc_ctx *)p;
+    for (size_t r = a; r < b; ++r)
+        for (size_t t = 0; t < c->n; ++t)
+            c->gate[t * c->HD + r] = gxo_dot_row(c->w->type_id, c->w->up + r * c->rb_r, c->lo + t * c->R, c->R);
+}
+
+int gxo_hc_mix(const gxo_hc *w, const float *res, size_t n, float *out, float *inject, int threads) {
+    if (!w || !res || !out || !w->norm || !w->down || !w->up || w->n_streams == 0 || w->rank == 0) return -1;
+    const size_t E = w->n_embd, H = w->n_streams, HD = H * E, R = w->rank;
+    const size_t rb_hd = gxo_row_bytes(w->type_id, HD), rb_r = gxo_row_bytes(w->type_id, R);
+    if (!rb_hd || !rb_r) return -1;
+    float *xn = malloc(sizeof(float) * n * HD), *lo = malloc(sizeof(float) * n * R), *gate = malloc(sizeof(float) * n * HD);
+    if (!xn || !lo || !gate) { free(xn); free(lo); free(gate); return -1; }
+    const float hcf = (float)H;
+    for (size_t t = 0; t < n; ++t)
+        for (size_t c = 0; c < H; ++c) {
+            const size_t o = t * HD + c * E;
+            /* src/kernels.zig:281-291 with the stream's weight */
+            float ss = 0;
+            for (size_t i = 0; i < E; ++i) ss += res[o + i] * res[o + i];
+            const float scale = 1.0f / sqrtf(ss / (float)E + w->eps);
+            for (size_t i = 0; i < E; ++i) xn[o + i] = res[o + i] * scale * w->norm[c * E + i];
+        }
+    hc_ctx c = {w, n, HD, R, rb_hd, rb_r, xn, lo, lo, gate, NULL};
+    pool_run(threads, R, 8, hc_down_range, &c);
+    for (size_t i = 0; i < n * R; ++i) lo[i] = silu(lo[i] / hcf);
+    pool_run(threads, HD, 64, hc_up_range, &c);
+    for (size_t t = 0; t < n; ++t) {
+        float *dst = out + t * E;
+        memset(dst, 0, sizeof(float) * E);
+        for (size_t ci = 0; ci < H; ++ci) {
+            const size_t o = t * HD + ci * E;
+            for (size_t i = 0; i < E; ++i) dst[i] += xn[o + i] * sigmoid(gate[o + i]);
+        }
+        for (size_t i = 0; i < E; ++i) dst[i] /= hcf;
+    }
+    if (inject) {
+        if (!w->inject) { free(xn); free(lo); free(gate); return -1; }
+        for (size_t t = 0; t < n; ++t)
+            for (size_t ci = 0; ci < H; ++ci)
+                inject[t * H + ci] = gxo_dot_row(w->type_id, w->inject + ci * rb_hd, xn + t * HD, HD);
+    }
+    free(xn); free(lo); free(gate);
+    return 0;
+}
+
+int gxo_hc_combine(const gxo_hc *w, float *res, size_t n, const float *block_out, const float *inject) {
+    if (!w || !res || !block_out || !inject) return -1;
+    const size_t E = w->n_embd, H = w->n_streams, HD = H * E;
+    const float hcf = (float)H;
+    for (size_t t = 0; t < n; ++t)
+        for (size_t c = 0; c < H; ++c) {
+            const float wgt = 2.0f * sigmoid(inject[t * H + c] / hcf);
+            float *dst = res + t * HD + c * E;
+            for (size_t i = 0; i < E; ++i) dst[i] += block_out[t * E + i] * wgt;
+        }
+    return 0;
+}

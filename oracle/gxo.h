@@ -112,6 +112,24 @@ typedef struct gxo_shared {
  * (the unrotated layer input). Returns 0, or -1 on bad arguments. */
 int gxo_shared_expert(const gxo_shared *s, const float *x, size_t n, size_t E, float *out, int threads);
 
+/* Hyper-connection mixer weights around the FFN block (src/model.zig:55-60, :362-367): n_streams
+ * residual streams of n_embd, a per-stream RMSNorm weight, the low-rank down [rank][hc*E], up
+ * [hc*E][rank] and inject [hc][hc*E] matrices in one non-expert encoding (8 Q8_0, 0 f32, 30 bf16,
+ * 1 f16), the norm epsilon. */
+typedef struct gxo_hc {
+    uint32_t n_streams, rank, n_embd, type_id;
+    float eps;
+    const float *norm;                   /* [hc*E] */
+    const uint8_t *down, *up, *inject;
+} gxo_hc;
+
+/* src/engine.zig:184-215 (hcMix): res [n][hc*E] -> out [n][E] and, if inject is not NULL,
+ * inject [n][hc]. Returns 0, or -1 on bad arguments. */
+int gxo_hc_mix(const gxo_hc *w, const float *res, size_t n, float *out, float *inject, int threads);
+
+/* src/engine.zig:217-228 (hcCombine): res[t][c] += block_out[t] * 2 sigmoid(inject[t][c] / hc). */
+int gxo_hc_combine(const gxo_hc *w, float *res, size_t n, const float *block_out, const float *inject);
+
 /* Threads the library can use (1 when built without GXO_THREADS). */
 int gxo_max_threads(void);
 

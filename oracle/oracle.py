@@ -84,6 +84,8 @@ def lib(fast: bool = False) -> ctypes.CDLL:
                                   ctypes.c_int]
     L.gxo_shared_expert.argtypes = [ctypes.POINTER(_Shared), _F32P, ctypes.c_size_t, ctypes.c_size_t, _F32P,
                                     ctypes.c_int]
+    L.gxo_hc_mix.argtypes = [ctypes.POINTER(_Hc), _F32P, ctypes.c_size_t, _F32P, ctypes.c_void_p, ctypes.c_int]
+    L.gxo_hc_combine.argtypes = [ctypes.POINTER(_Hc), _F32P, ctypes.c_size_t, _F32P, _F32P]
     L.gxo_max_threads.restype = ctypes.c_int
     L.gxo_rms_norm.argtypes = [_F32P, _F32P, ctypes.c_size_t, ctypes.c_float]
     L.gxo_rms_norm.restype = None
@@ -103,6 +105,12 @@ class _Shared(ctypes.Structure):
         ("down", ctypes.c_void_p),
         ("gate_inp", ctypes.c_void_p),
     ]
+
+
+class _Hc(ctypes.Structure):
+    _fields_ = [("n_streams", ctypes.c_uint32), ("rank", ctypes.c_uint32), ("n_embd", ctypes.c_uint32),
+                ("type_id", ctypes.c_uint32), ("eps", ctypes.c_float), ("norm", ctypes.c_void_p),
+                ("down", ctypes.c_void_p), ("up", ctypes.c_void_p), ("inject", ctypes.c_void_p)]
 
 
 def _f32p(a: np.ndarray):
@@ -255,3 +263,46 @@ def ref_lib() -> ctypes.CDLL | None:
 if __name__ == "__main__":
     build(force=bool(os.environ.get("FORCE")))
     print("oracle built; threads:", max_threads())
+
+
+def _hc_desc(hc: dict, keep: list):
+    arrs = [np.ascontiguousarray(hc[k], dtype=np.uint8) for k in ("down", "up", "inject")]
+    norm = np.ascontiguousarray(hc["norm"], dtype=np.float32)
+    keep += arrs + [norm]
+    return _Hc(hc["n_streams"], hc["rank"], hc["n_embd"], hc["type_id"], hc["eps"], norm.ctypes.data,
+               arrs[0].ctypes.data, arrs[1].ctypes.data, arrs[2].ctypes.data)
+
+
+def hc_mix(hc: dict, res: np.ndarray, threads: int = 1, fast: bool = False):
+    """src/engine.zig:184-215: res [n, hc*E] -> (cur [n, E], inject [n, hc])."""
+    L = lib(fast)
+    res = np.ascontiguousarray(res, dtype=np.float32)
+    n = res.shape[0]
+    keep = []
+    desc = _hc_desc(hc, keep)
+    out = np.empty((n, hc["n_embd"]), np.float32)
+    inj = np.empty((n, hc["n_streams"]), np.float32)
+    if L.gxo_hc_mix(ctypes.byref(desc), _f32p(res), n, _f32p(out), inj.ctypes.data, threads) != 0:
+        raise RuntimeError("gxo_hc_mix failed")
+    return out, inj
+
+
+def hc_combine(hc: dict, res: np.ndarray, block_out: np.ndarray, inject: np.ndarray) -> np.ndarray:
+    """src/engine.zig:217-228: a new res with the block output added to every stream."""
+    L = lib()
+    res = np.ascontiguousarray(res, dtype=np.float32).copy()
+    block_out = np.ascontiguousarray(block_out, dtype=np.float32)
+    inject = np.ascontiguousarray(inject, dtype=np.float32)
+    keep = []
+    desc = _hc_desc(hc, keep)
+    if L.gxo_hc_combine(ctypes.byref(desc), _f32p(res), res.shape[0], _f32p(block_out), _f32p(inject)) != 0:
+        raise RuntimeError("gxo_hc_combine failed")
+    return res
+
+
+def ffn_block(layer: dict, hc: dict, res: np.ndarray, threads: int = 1, fast: bool = False) -> np.ndarray:
+    """The reference's FFN block (src/engine.zig:162-165): hc mixer, routed + shared experts,
+    hc combine. res [n, hc*E] -> res'."""
+    cur, inj = hc_mix(hc, res, threads=threads, fast=fast)
+    out, _, _ = moe_ffn(layer, cur, threads=threads, fast=fast)
+    return hc_combine(hc, res, out, inj)

@@ -41,14 +41,16 @@ def test_struct_layouts_match_c(tmp_path):
                    'int main(void){printf("%zu %zu %zu %zu %zu %zu %zu %zu\\n", sizeof(gx_options), sizeof(gx_caps),'
                    ' sizeof(gx_layer_desc), sizeof(gx_timings), offsetof(gx_options, nccl_id),'
                    ' offsetof(gx_layer_desc, router), sizeof(gx_shared_desc), offsetof(gx_shared_desc, gate_inp));'
-                   'printf("%zu\\n", sizeof(gx_gguf_layer_info));return 0;}\n')
+                   'printf("%zu %zu %zu\\n", sizeof(gx_gguf_layer_info), sizeof(gx_hc_desc),'
+                   ' offsetof(gx_hc_desc, down_bytes));return 0;}\n')
     exe = tmp_path / "sz"
     subprocess.run(["gcc", "-I", str(ROOT / "include"), str(src), "-o", str(exe)], check=True)
     sizes = [int(v) for v in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
     import ctypes
     assert sizes == [ctypes.sizeof(abi.Options), ctypes.sizeof(abi.Caps), ctypes.sizeof(abi.LayerDesc),
                      ctypes.sizeof(abi.Timings), abi.Options.nccl_id.offset, abi.LayerDesc.router.offset,
-                     ctypes.sizeof(abi.SharedDesc), abi.SharedDesc.gate_inp.offset, ctypes.sizeof(abi.GgufLayerInfo)]
+                     ctypes.sizeof(abi.SharedDesc), abi.SharedDesc.gate_inp.offset, ctypes.sizeof(abi.GgufLayerInfo),
+                     ctypes.sizeof(abi.HcDesc), abi.HcDesc.down_bytes.offset]
 
 
 def test_create_rejects_bad_options_without_touching_a_device(lib):

@@ -285,3 +285,53 @@ def test_shared_expert_matches_dense_definition(type_id):
     y = (g / (1 + np.exp(-g)) * u) @ dense(sh["down"], 256, 128).T
     gate = 1 / (1 + np.exp(-(xd @ sh["gate_inp"].astype(np.float64))))
     np.testing.assert_allclose(out, base + y * gate[:, None], rtol=1e-5, atol=1e-5)
+
+
+def dense_f64(m: np.ndarray, type_id: int, rows: int, cols: int) -> np.ndarray:
+    """Plain matrix bytes (Q8_0 / bf16 / f32 rows) as float64 values."""
+    if type_id == 8:
+        b = m.reshape(rows, cols // 32, 34)
+        d = b[:, :, :2].copy().view(np.float16).astype(np.float64)
+        q = b[:, :, 2:].view(np.int8).astype(np.float64)
+        return (d * q).reshape(rows, cols)
+    if type_id == 30:
+        return (m.view(np.uint16).astype(np.uint32) << 16).view(np.float32).reshape(rows, cols).astype(np.float64)
+    return m.view(np.float32).reshape(rows, cols).astype(np.float64)
+
+
+@pytest.mark.parametrize("type_id", [0, 8, 30])
+def test_hc_mixer_matches_dense_definition(type_id):
+    """hcMix and hcCombine (src/engine.zig:184-228) against a float64 numpy restatement: per-stream
+    RMSNorm with the stream's weight, lo = silu(Down xn / hc), cur = mean_c xn_c sigmoid((Up lo)_c),
+    inject = Inject xn, res_c += y 2 sigmoid(inject_c / hc). Rank 320 as in the reference model."""
+    E, H, R = 256, 4, 320
+    hc = synth.make_hc(11, E=E, n_streams=H, rank=R, type_id=type_id)
+    res = np.random.default_rng(12).standard_normal((5, H * E)).astype(np.float32) * 3.0
+    cur, inj = oracle.hc_mix(hc, res)
+    r = res.astype(np.float64).reshape(5, H, E)
+    xn = r / np.sqrt((r ** 2).mean(axis=2, keepdims=True) + hc["eps"]) * hc["norm"].reshape(H, E)
+    xn = xn.reshape(5, H * E)
+    lo = xn @ dense_f64(hc["down"], type_id, R, H * E).T / H
+    lo = lo / (1 + np.exp(-lo))
+    gate = lo @ dense_f64(hc["up"], type_id, H * E, R).T
+    want = (xn * (1 / (1 + np.exp(-gate)))).reshape(5, H, E).mean(axis=1)
+    np.testing.assert_allclose(cur, want, rtol=2e-5, atol=2e-5)
+    want_inj = xn @ dense_f64(hc["inject"], type_id, H, H * E).T
+    np.testing.assert_allclose(inj, want_inj, rtol=2e-5, atol=2e-5)
+    y = np.random.default_rng(13).standard_normal((5, E)).astype(np.float32)
+    got = oracle.hc_combine(hc, res, y, inj)
+    w = 2 / (1 + np.exp(-inj.astype(np.float64) / H))
+    want_res = r + y.astype(np.float64)[:, None, :] * w[:, :, None]
+    np.testing.assert_allclose(got, want_res.reshape(5, H * E), rtol=1e-6, atol=1e-6)
+
+
+def test_ffn_block_is_mix_layer_combine():
+    layer = synth.make_layer(14, n_expert=16, E=256, F=128, U=4)
+    layer["shared"] = synth.make_shared(15, E=256, SF=128)
+    hc = synth.make_hc(16, E=256, n_streams=4, rank=128)
+    res = np.random.default_rng(17).standard_normal((3, 1024)).astype(np.float32)
+    cur, inj = oracle.hc_mix(hc, res)
+    y, _, _ = oracle.moe_ffn(layer, cur)
+    np.testing.assert_array_equal(oracle.ffn_block(layer, hc, res), oracle.hc_combine(hc, res, y, inj))
+    with pytest.raises(RuntimeError):
+        oracle.hc_mix(dict(hc, rank=0), res)
