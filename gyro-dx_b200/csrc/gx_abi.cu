@@ -717,6 +717,7 @@ gx_result enqueue_layer_prefill(gx_context *c, const Layer &L, const void *x, ui
     pa.tile_rows = p.tile_rows;
     pa.n_mtiles = p.n_mtiles;
     pa.dst = p.A;
+    pa.compact = gx::gemm_ts_routed(L.type);
     GX_CUDA(gx::launch_pack_rows(pa, (int)p.max_tiles, c->stream));
     if (ev) GX_CUDA(record_phase(ev[1], c->stream));
     gx::GemmArgs gm{};
@@ -750,6 +751,7 @@ gx_result enqueue_layer_prefill(gx_context *c, const Layer &L, const void *x, ui
     pd.tile_rows = p.tile_rows;
     pd.n_mtiles = p.n_mtiles;
     pd.dst = p.A2;
+    pd.compact = gx::gemm_ts_routed(L.type);
     GX_CUDA(gx::launch_pack_rows(pd, (int)p.max_tiles, c->stream));
     gm.w0 = L.down;
     gm.w1 = nullptr;
@@ -1089,6 +1091,7 @@ gx_result enqueue_layer_ep_peer(gx_context *c, const Layer &L, const void *x, in
     pk.tile_rows = p.tile_rows;
     pk.n_mtiles = p.n_mtiles;
     pk.dst = p.A;
+    pk.compact = gx::gemm_ts_routed(L.type);
     GX_CUDA(gx::launch_pack_rows(pk, (int)p.max_tiles, c->stream));
     gx::GemmArgs gm{};
     gm.type = L.type;
@@ -1120,6 +1123,7 @@ gx_result enqueue_layer_ep_peer(gx_context *c, const Layer &L, const void *x, in
     pd.tile_rows = p.tile_rows;
     pd.n_mtiles = p.n_mtiles;
     pd.dst = p.A2;
+    pd.compact = gx::gemm_ts_routed(L.type);
     GX_CUDA(gx::launch_pack_rows(pd, (int)p.max_tiles, c->stream));
     gm.w0 = L.down;
     gm.w1 = nullptr;
@@ -1286,6 +1290,7 @@ gx_result enqueue_layer_ep(gx_context *c, const Layer &L, const void *x, uint32_
         pk.tile_rows = p.tile_rows;
         pk.n_mtiles = p.n_mtiles;
         pk.dst = p.A;
+        pk.compact = gx::gemm_ts_routed(L.type);
         GX_CUDA(gx::launch_pack_rows(pk, (int)p.max_tiles, c->stream));
         gx::GemmArgs gm{};
         gm.type = L.type;
@@ -1317,6 +1322,7 @@ gx_result enqueue_layer_ep(gx_context *c, const Layer &L, const void *x, uint32_
         pd.tile_rows = p.tile_rows;
         pd.n_mtiles = p.n_mtiles;
         pd.dst = p.A2;
+        pd.compact = gx::gemm_ts_routed(L.type);
         GX_CUDA(gx::launch_pack_rows(pd, (int)p.max_tiles, c->stream));
         gm.w0 = L.down;
         gm.w1 = nullptr;

@@ -173,6 +173,8 @@ struct PackArgs {
     const float *signs;      // [K] or nullptr (then no Hadamard transform)
     const int *row_slot, *tile_rows, *n_mtiles;
     uint8_t *dst;            // [tiles][K/64][16384] f16 swizzled
+    int compact;             // k-step blocks of rows16(tile rows) x 128 B each, back to back
+                             // (moe_gemm_ts_kernel), instead of 16384 B each
 };
 
 struct GemmArgs {
@@ -349,6 +351,12 @@ cudaError_t launch_ep_combine(const EpCombineArgs &a, cudaStream_t s);
 cudaError_t launch_group(const GroupArgs &a, cudaStream_t s);
 cudaError_t launch_pack_rows(const PackArgs &a, int max_tiles, cudaStream_t s);
 cudaError_t launch_moe_gemm(const GemmArgs &a, int mode, int sm_count, cudaStream_t s);
+// The routed experts' grouped GEMM with the decoded weights in tensor memory (gx_gemm_ts.cu):
+// launch_moe_gemm uses it for the Gyro types (gemm_ts_routed) unless GX_GEMM_SMEM=1 selects
+// moe_gemm_kernel; its token tiles are packed compact (PackArgs::compact).
+bool gemm_ts_routed(uint32_t type);
+bool gemm_ts_supports(const GemmArgs &a, int mode);
+cudaError_t launch_moe_gemm_ts(const GemmArgs &a, int mode, int sm_count, cudaStream_t s);
 cudaError_t launch_combine(const CombineArgs &a, cudaStream_t s);
 
 struct MatvecArgs {

@@ -207,7 +207,13 @@ __global__ void __launch_bounds__(256) pack_rows_kernel(PackArgs a) {
     const int nb = a.K / 128;
     if (row >= (long long)*a.n_mtiles * 128) return;
     const int t = (int)(row >> 7), i = (int)(row & 127);
-    const bool valid = i < a.tile_rows[t];
+    const int rows_t = a.tile_rows[t];
+    const bool valid = i < rows_t;
+    // compact tiles keep rows16(rows) rows per k-step block; the rows past that are not stored
+    const int np = a.compact ? (rows_t <= 16 ? 16 : (rows_t + 15) & ~15) : 128;
+    if (i >= np) return;
+    uint8_t *tile_base = a.dst + (size_t)t * (a.K / 64) * 16384u;
+    const size_t kblock = (size_t)np * 128u;
     size_t src_row = (size_t)row;
     float sc = 1.f;
     if (valid && a.by_token) {
@@ -224,7 +230,7 @@ __global__ void __launch_bounds__(256) pack_rows_kernel(PackArgs a) {
         for (int b = 0; b < nb; ++b) {
             uint2 w = make_uint2(0u, 0u);
             if (valid) w = *reinterpret_cast<const uint2 *>(xr + b * 128 + 4 * lane);
-            uint8_t *tile = a.dst + ((size_t)t * (a.K / 64) + 2 * b + ks_lo) * 16384u;
+            uint8_t *tile = tile_base + (size_t)(2 * b + ks_lo) * kblock;
             *reinterpret_cast<uint2 *>(tile + sw128_offset((uint32_t)i, (uint32_t)col)) = w;
         }
         return;
@@ -263,7 +269,7 @@ __global__ void __launch_bounds__(256) pack_rows_kernel(PackArgs a) {
             const int b = b0 + q;
             if (b >= nb) break;
             if (a.signs) fwht128_warp(v[q], lane);
-            uint8_t *tile = a.dst + ((size_t)t * (a.K / 64) + 2 * b + ks_lo) * 16384u;
+            uint8_t *tile = tile_base + (size_t)(2 * b + ks_lo) * kblock;
             uint2 w;
             w.x = pack_half2(v[q][0], v[q][1]);
             w.y = pack_half2(v[q][2], v[q][3]);
@@ -685,6 +691,8 @@ cudaError_t gemm_t(const GemmArgs &a, int sm_count, cudaStream_t s) {
 }  // namespace
 
 cudaError_t launch_moe_gemm(const GemmArgs &a, int mode, int sm_count, cudaStream_t s) {
+    if (gemm_ts_routed(a.type))
+        return gemm_ts_supports(a, mode) ? launch_moe_gemm_ts(a, mode, sm_count, s) : cudaErrorInvalidValue;
 #define GX_GEMM_CASE(TT)                                                                 \
     case TT:                                                                             \
         return mode == 0 ? gemm_t<TT, 0>(a, sm_count, s) : gemm_t<TT, 1>(a, sm_count, s);

@@ -16,7 +16,7 @@ PKG = Path(__file__).resolve().parent
 CSRC = PKG.parent / "csrc"
 ROOT = PKG.parents[1]
 LIB = PKG / "libgyromoe.so"
-SOURCES = ["gx_kernels.cu", "gx_decode_stack.cu", "gx_prefill.cu", "gx_router_tc.cu", "gx_ep.cu", "gx_shared.cu", "gx_hc.cu",
+SOURCES = ["gx_kernels.cu", "gx_decode_stack.cu", "gx_prefill.cu", "gx_gemm_ts.cu", "gx_router_tc.cu", "gx_ep.cu", "gx_shared.cu", "gx_hc.cu",
            "gx_comm.cu", "gx_abi.cu", "gx_gguf.cpp"]
 HEADERS = ["gx_tile.h", "gx_device.cuh", "gx_gemv.cuh", "gx_internal.h", "gx_umma.cuh", "gx_comm.h", "gx_dense.cuh"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
