@@ -1,26 +1,27 @@
 // gx_gemm_ts.cu — grouped GEMM of the routed experts with the decoded weights in tensor memory.
 //
-// D[weight row][token] = sum_k W[row][k] * X[token][k] per (token tile, weight tile) work item,
-// issued as tcgen05.mma.kind::f16 with A = the decoded Gyro weights in TMEM and B = the token
-// tile in shared memory:
+// D[weight row][token] = sum_k W[row][k] * X[token][k] per (token tile, weight pair) work item,
+// issued as tcgen05.mma.kind::f16 with A = decoded Gyro weights in TMEM and B = the token tile in
+// shared memory:
 //   - the weights are decoded straight from the packed codes into registers and stored into
 //     TMEM with tcgen05.st, so decoded weights never pass through shared memory (the codebook
 //     lookups are the only shared-memory reads of the decoders);
 //   - the MMA's N is the token count of the tile rounded up to 16, not a fixed 128;
-//   - one weight tile is 128 rows: gate/up = 64 gate rows (TMEM lanes 0-63) and the same 64
-//     columns of up (lanes 64-127), so the SwiGLU epilogue pairs lane i with lane i + 64; down
-//     = 128 consecutive rows of the down matrix.
-// The token tiles are the ones pack_rows_kernel writes for moe_gemm_kernel (128-row tiles,
-// [tile][K/64][128 rows x 128 B], 128-byte swizzle), and the outputs have its layout too:
+//   - a work item covers two 128-row weight tiles against one token tile, so each token byte
+//     brought in feeds 256 weight rows: gate/up = gate rows [f0, f0+128) in accumulator 0 and
+//     the same up rows in accumulator 1 (silu(g) * u pairs the same TMEM lane of the two), down
+//     = rows [e0, e0+256) as two tiles.
+// The token tiles are the 128-row tiles pack_rows_kernel writes in its compact form
+// ([tile][K/64][rows16 x 128 B], 128-byte swizzle); the outputs have moe_gemm_kernel's layout:
 // act [tiles*128][F] f32 (silu(g) * u) and Y [tiles*128][E] f16.
 //
 // Roles (704 threads):
-//   warp 0      token tiles: one bulk copy of the tile's rows per 64-wide k-step
-//   warp 1      TMEM allocation; one lane issues the MMAs (4 per k-step) and the commits
-//   warps 2-17  decoders in 4 sets of 4 warps: set j decodes the CTA's k-steps n = j, j + 4,
-//               ... (over its items in order), warp % 4 picks the TMEM lane quarter, and one
-//               thread decodes one weight row's 64 weights of a k-step
-//   warps 18-21 epilogue: TMEM accumulator (double-buffered) to act or Y
+//   warp 0      token tiles: as many 64-wide k-steps of the tile as fit 32 KB per bulk copy
+//   warp 1      TMEM allocation; one lane issues the MMAs (8 per k-step) and the commits
+//   warps 2-17  decoders in 2 sets of 8 warps: set j decodes the CTA's k-steps n = j, j + 2, ...
+//               (over its items in order); (warp - 2) / 4 % 2 picks the weight tile and warp % 4
+//               the TMEM lane quarter; one thread decodes one weight row's 64 weights of a k-step
+//   warps 18-21 epilogue: the accumulators to act or Y, then the MMAs of the next item start
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -35,26 +36,26 @@ namespace gx {
 
 namespace {
 
-constexpr int kTsSets = 4;                     // decoder sets (4 warps each)
+constexpr int kTsSets = 2;                     // decoder sets (8 warps each: 2 tiles x 4 lane quarters)
 constexpr int kTsTStages = 4;                  // token stages in shared memory (one bulk copy each)
-constexpr int kTsWStages = 8;                  // decoded weight tiles (one k-step each) in TMEM
+constexpr int kTsWStages = 4;                  // decoded k-steps (both weight tiles) in TMEM
 constexpr int kTsCopies = 8;
-constexpr int kTsDecWarps = 4 * kTsSets;
+constexpr int kTsDecWarps = 8 * kTsSets;
 constexpr int kTsEpiWarp = 2 + kTsDecWarps;
 constexpr int kTsThreads = 32 * (kTsEpiWarp + 4);
 constexpr int kTsTok = 32768;                  // as many k-steps of the tile's rows as fit (>= 2)
-// TMEM columns: accumulators at 0 and 128 (128 tokens each), weight stages at 256 + 32 s
-constexpr uint32_t kTsAcc = 128, kTsW = 256, kTsCols = 512;
-static_assert(kTsW + 32 * kTsWStages <= kTsCols, "TMEM plan");
+// TMEM columns: accumulators of tiles 0 and 1 at 0 and 128 (up to 128 tokens each), weight
+// stage s of tile w at 256 + 32 (2 s + w)
+constexpr uint32_t kTsW = 256, kTsCols = 512;
+static_assert(kTsW + 64 * kTsWStages <= kTsCols, "TMEM plan");
 static_assert(kTsWStages % kTsSets == 0, "each decoder set owns the weight stages s = set (mod sets)");
 static_assert((kTsTStages & (kTsTStages - 1)) == 0 && (kTsWStages & (kTsWStages - 1)) == 0, "ring sizes");
 
 struct TsSmem {
     static constexpr int TOK = 0;                                   // per stage +kTsTok
     static constexpr int CB = kTsTStages * kTsTok;
-    static constexpr int XCH = CB + Codebook<kTsCopies>::BYTES;     // 2 pairs x [2 halves][16 tokens][32 lanes] f32
-    static constexpr int BARS = XCH + 2 * 2 * 16 * 32 * 4;
-    static constexpr int BYTES = BARS + 512;
+    static constexpr int BARS = CB + Codebook<kTsCopies>::BYTES;
+    static constexpr int BYTES = BARS + 256;
 };
 
 __device__ __forceinline__ uint32_t tile_cols(int rows) { return rows <= 16 ? 16u : (uint32_t)((rows + 15) & ~15); }
@@ -77,16 +78,13 @@ __global__ void __launch_bounds__(kTsThreads, 1) moe_gemm_ts_kernel(GemmArgs a) 
     extern __shared__ __align__(1024) uint8_t tsm_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>(((uintptr_t)tsm_raw + 1023) & ~(uintptr_t)1023);
     uint32_t *cb = reinterpret_cast<uint32_t *>(sm + TsSmem::CB);
-    float *xch = reinterpret_cast<float *>(sm + TsSmem::XCH);
     uint64_t *full_tok = reinterpret_cast<uint64_t *>(sm + TsSmem::BARS);
     uint64_t *empty_tok = full_tok + kTsTStages;
     uint64_t *full_w = empty_tok + kTsTStages;
     uint64_t *empty_w = full_w + kTsWStages;
     uint64_t *acc_full = empty_w + kTsWStages;
-    uint64_t *acc_empty = acc_full + 2;
-    uint64_t *x_full = acc_empty + 2;          // per SwiGLU pair: both halves written to xch
-    uint64_t *x_free = x_full + 2;             // per SwiGLU pair: both halves read
-    uint64_t *done = x_free + 2;
+    uint64_t *acc_empty = acc_full + 1;
+    uint64_t *done = acc_empty + 1;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
@@ -94,22 +92,18 @@ __global__ void __launch_bounds__(kTsThreads, 1) moe_gemm_ts_kernel(GemmArgs a) 
     constexpr int TB = tile_bytes(T);
     const int NB = a.K / 128;
     const int KS = a.K / 64;
-    const int n_w = MODE == 0 ? a.F / 64 : a.E / 128;   // weight tiles per token tile
+    const int n_p = MODE == 0 ? a.F / 128 : a.E / 256;   // weight pairs per token tile
     if (tid == 0) {
         for (int s = 0; s < kTsTStages; ++s) {
             mbar_init(&full_tok[s], 1);
             mbar_init(&empty_tok[s], 1);
         }
         for (int s = 0; s < kTsWStages; ++s) {
-            mbar_init(&full_w[s], 4);
+            mbar_init(&full_w[s], 8);
             mbar_init(&empty_w[s], 1);
         }
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(&acc_full[b], 1);
-            mbar_init(&acc_empty[b], 4);
-            mbar_init(&x_full[b], 2);
-            mbar_init(&x_free[b], 2);
-        }
+        mbar_init(acc_full, 1);
+        mbar_init(acc_empty, 4);
         mbar_init(done, 1);
         *abort_flag = 0;
         fence_barrier_init();
@@ -120,7 +114,7 @@ __global__ void __launch_bounds__(kTsThreads, 1) moe_gemm_ts_kernel(GemmArgs a) 
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    const int n_items = *a.n_mtiles * n_w;
+    const int n_items = *a.n_mtiles * n_p;
 
     auto wait = [&](uint64_t *bar, uint32_t parity) -> bool {
         if (*abort_flag) return false;
@@ -139,7 +133,7 @@ __global__ void __launch_bounds__(kTsThreads, 1) moe_gemm_ts_kernel(GemmArgs a) 
         if (lane == 0) {
             int m = 0;
             for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
-                const int t = it / n_w;
+                const int t = it / n_p;
                 const uint32_t cols = tile_cols(rows_of(t)), kblock = cols * 128u;
                 const int kps = stage_ksteps(cols, KS);
                 const uint8_t *src = a.A + (size_t)t * KS * 16384u;
@@ -153,7 +147,7 @@ __global__ void __launch_bounds__(kTsThreads, 1) moe_gemm_ts_kernel(GemmArgs a) 
             }
         }
     } else if (warp == 1) {
-        // ---- MMA issuer: one lane; 4 MMAs (K = 16 each) per k-step -------------------------
+        // ---- MMA issuer: one lane; 8 MMAs (2 tiles x K = 16 x 4) per k-step -----------------
         if (lane == 0) {
             const uint64_t dtmpl = sw128_desc(0);
             const uint32_t tok0 = smem_u32(sm + TsSmem::TOK);
@@ -164,54 +158,56 @@ __global__ void __launch_bounds__(kTsThreads, 1) moe_gemm_ts_kernel(GemmArgs a) 
             int n = 0, m = 0, cnt = 0;
             bool ok = true;
             for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x, ++cnt) {
-                const uint32_t cols = tile_cols(rows_of(it / n_w)), kblock = cols * 128u;
+                const uint32_t cols = tile_cols(rows_of(it / n_p)), kblock = cols * 128u;
                 const int kps = stage_ksteps(cols, KS);
                 const uint32_t idesc = f16_idesc(128, cols);
-                const int ab = cnt & 1;
-                if (!wait(&acc_empty[ab], ((cnt >> 1) & 1) ^ 1)) break;
-                tc_fence_after();
-                const uint32_t d_tmem = tmem_base + (uint32_t)ab * kTsAcc;
                 for (int ks0 = 0; ok && ks0 < KS; ks0 += kps, ++m) {
                     const int st = m & (kTsTStages - 1);
                     if (!wait_q(&full_tok[st], (m / kTsTStages) & 1)) { ok = false; break; }
+                    // the accumulators are free once the previous item's epilogue has read them
+                    if (ks0 == 0 && !wait_q(acc_empty, (cnt & 1) ^ 1)) { ok = false; break; }
                     uint32_t baddr = tok0 + (uint32_t)st * kTsTok;
                     for (int j = 0; j < kps; ++j, ++n, baddr += kblock) {
                         const int sw = n & (kTsWStages - 1);
                         if (!wait_q(&full_w[sw], (n / kTsWStages) & 1)) { ok = false; break; }
                         tc_fence_after();
                         const uint64_t bd = dtmpl | (uint64_t)((baddr >> 4) & 0x3FFFu);
-                        const uint32_t at = tmem_base + kTsW + 32u * (uint32_t)sw;
+                        const uint32_t at = tmem_base + kTsW + 64u * (uint32_t)sw;
                         const uint32_t acc0 = (ks0 | j) != 0;
-                        umma_f16_ts(d_tmem, at, bd, idesc, acc0);
-                        umma_f16_ts(d_tmem, at + 8u, bd + 2u, idesc, 1u);
-                        umma_f16_ts(d_tmem, at + 16u, bd + 4u, idesc, 1u);
-                        umma_f16_ts(d_tmem, at + 24u, bd + 6u, idesc, 1u);
+                        umma_f16_ts(tmem_base, at, bd, idesc, acc0);
+                        umma_f16_ts(tmem_base + 128u, at + 32u, bd, idesc, acc0);
+                        umma_f16_ts(tmem_base, at + 8u, bd + 2u, idesc, 1u);
+                        umma_f16_ts(tmem_base + 128u, at + 40u, bd + 2u, idesc, 1u);
+                        umma_f16_ts(tmem_base, at + 16u, bd + 4u, idesc, 1u);
+                        umma_f16_ts(tmem_base + 128u, at + 48u, bd + 4u, idesc, 1u);
+                        umma_f16_ts(tmem_base, at + 24u, bd + 6u, idesc, 1u);
+                        umma_f16_ts(tmem_base + 128u, at + 56u, bd + 6u, idesc, 1u);
                         umma_commit(&empty_w[sw]);
                     }
                     if (ok) umma_commit(&empty_tok[st]);
                 }
-                if (ok) umma_commit(&acc_full[ab]);
+                if (ok) umma_commit(acc_full);
             }
             // all issued MMAs complete before TMEM is released
             umma_commit(done);
             mbar_wait(done, 0, nullptr);
         }
     } else if (warp < kTsEpiWarp) {
-        // ---- decoders: weight row i of the item's weight tile; the set's k-steps --------------
-        const int set = (warp - 2) >> 2, lg = warp & 3;
+        // ---- decoders: row i of weight tile w of the item's pair; the set's k-steps ----------
+        const int set = (warp - 2) >> 3, w = ((warp - 2) >> 2) & 1, lg = warp & 3;
         const int i = 32 * lg + lane;                      // TMEM lane = row of the weight tile
         const int r8 = i & 7;                              // the row's place in its 8-row code tile
         const uint32_t lane_off = 4u * CBk::copy_off(lane);
         const uint8_t *cbb = reinterpret_cast<const uint8_t *>(cb);
         auto rowtiles_of = [&](int it) -> const uint8_t * {
-            const int t = it / n_w, mt = it % n_w;
+            const int t = it / n_p, p = it % n_p;
             uint32_t e = (uint32_t)a.tile_expert[t];
             if (e >= (uint32_t)a.n_expert) {
                 atomicExch(a.err, KERR_BOUNDS);
                 e = 0;
             }
-            const uint8_t *mat = MODE == 0 ? (i < 64 ? a.w0 : a.w1) : a.w0;
-            const int row = MODE == 0 ? mt * 64 + (i & 63) : mt * 128 + i;
+            const uint8_t *mat = MODE == 0 ? (w == 0 ? a.w0 : a.w1) : a.w0;
+            const int row = MODE == 0 ? p * 128 + i : p * 256 + w * 128 + i;
             return mat + (uint64_t)e * a.expert_bytes + (size_t)(row >> 3) * NB * TB;
         };
         // Codes of one k-step (half h of a block): the two own quarters 2h, 2h+1, the neighbour
@@ -219,7 +215,7 @@ __global__ void __launch_bounds__(kTsThreads, 1) moe_gemm_ts_kernel(GemmArgs a) 
         // while this one is decoded (kTsSets k-steps of the CTA ahead), across items.
         struct Codes {
             uint32_t own0[4], own1[4], nbr[4];
-            uint32_t d, h;
+            uint32_t d;
         };
         int pf_cnt = 0, pf_ks = set;
         while (pf_ks >= KS) { pf_ks -= KS; ++pf_cnt; }
@@ -238,7 +234,6 @@ __global__ void __launch_bounds__(kTsThreads, 1) moe_gemm_ts_kernel(GemmArgs a) 
             load_run<T>(tile, 4 * r8 + 2 * h + 1, cd.own1);
             load_run<T>(tile, 4 * r8 + ((2 * h + 3) & 3), cd.nbr);
             cd.d = *reinterpret_cast<const uint16_t *>(tile + tile_code_bytes(T) + 2 * r8);
-            cd.h = (uint32_t)h;
             pf_ks += kTsSets;
             while (pf_ks >= KS) { pf_ks -= KS; ++pf_cnt; }
             return true;
@@ -248,9 +243,9 @@ __global__ void __launch_bounds__(kTsThreads, 1) moe_gemm_ts_kernel(GemmArgs a) 
         for (int n = set; have; n += kTsSets) {
             Codes nxt;
             const bool more = fetch(nxt);
-            const int s = n % kTsWStages, round = n / kTsWStages;
+            const int s = n & (kTsWStages - 1), round = n / kTsWStages;
             const __half2 d2 = __halves2half2(__ushort_as_half((uint16_t)cur.d), __ushort_as_half((uint16_t)cur.d));
-            const uint32_t taddr = tmem_base + ((uint32_t)(32 * lg) << 16) + kTsW + 32u * (uint32_t)s;
+            const uint32_t taddr = tmem_base + ((uint32_t)(32 * lg) << 16) + kTsW + 32u * (uint32_t)(2 * s + w);
             bool ok = true;
             // quarter qq of the k-step: column 16 qq + 2c holds weights 32 qq + 4c + {0, 1},
             // column 16 qq + 2c + 1 holds 32 qq + 4c + {2, 3} (the lower k in the low half)
@@ -284,79 +279,51 @@ __global__ void __launch_bounds__(kTsThreads, 1) moe_gemm_ts_kernel(GemmArgs a) 
             have = more;
         }
     } else {
-        // ---- epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 of the accumulator ---------
+        // ---- epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 of both accumulators --------
         const int lg = warp & 3;
-        int cnt = 0, chunk = 0;
+        int cnt = 0;
         for (int it = blockIdx.x; it < n_items; it += gridDim.x, ++cnt) {
-            const int t = it / n_w, mt = it % n_w;
+            const int t = it / n_p, p = it % n_p;
             const int rows = rows_of(t);
-            const int ab = cnt & 1;
-            if (!wait(&acc_full[ab], (cnt >> 1) & 1)) break;
+            if (!wait(acc_full, cnt & 1)) break;
             tc_fence_after();
-            const uint32_t base = tmem_base + ((uint32_t)(32 * lg) << 16) + (uint32_t)ab * kTsAcc;
-            bool ok = true;
+            const uint32_t base = tmem_base + ((uint32_t)(32 * lg) << 16);
             if (MODE == 0) {
-                // lanes 0-63: gate rows, 64-127: up rows of the same 64 columns. The gate warp
-                // (lg 0, 1) and the up warp (lg 2, 3) of a pair swap half of each 32-token chunk
-                // through xch: the gate warp computes tokens 0-15, the up warp tokens 16-31.
-                const int pair = lg & 1;
-                const bool up = lg >= 2;
-                float *give = xch + pair * 1024 + (up ? 512 : 0);   // [16 tokens][32 lanes]
-                const float *take = xch + pair * 1024 + (up ? 0 : 512);
-                const int f = mt * 64 + 32 * pair + lane;
-                const int half = up ? 16 : 0;
-                for (int c0 = 0; c0 < rows; c0 += 32, ++chunk) {
-                    uint32_t v[32];
-                    tmem_ld32(base + (uint32_t)c0, v);
-                    tmem_wait_ld();
-                    if (!wait(&x_free[pair], (chunk & 1) ^ 1)) { ok = false; break; }
-                    if (up) {
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) give[j * 32 + lane] = __uint_as_float(v[j]);
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) give[j * 32 + lane] = __uint_as_float(v[16 + j]);
-                    }
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&x_full[pair]);
-                    if (!wait(&x_full[pair], chunk & 1)) { ok = false; break; }
-                    float *dst = a.act + ((size_t)t * 128 + c0 + half) * a.F + f;
-                    const int n = min(16, rows - c0 - half);
-                    if (up) {
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) {
-                            if (j < n) *dst = silu_fast(take[j * 32 + lane]) * __uint_as_float(v[16 + j]);
-                            dst += a.F;
-                        }
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) {
-                            if (j < n) *dst = silu_fast(__uint_as_float(v[j])) * take[j * 32 + lane];
-                            dst += a.F;
-                        }
-                    }
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&x_free[pair]);
-                }
-            } else {
-                const int e = mt * 128 + 32 * lg + lane;
-                __half *dst = a.Y + (size_t)t * 128 * a.E + e;
+                // lane i: gate row and up row f of the pair, both in TMEM lane i
+                float *dst = a.act + (size_t)t * 128 * a.F + p * 128 + 32 * lg + lane;
                 for (int c0 = 0; c0 < rows; c0 += 16) {
-                    uint32_t v[16];
-                    tmem_ld16(base + (uint32_t)c0, v);
+                    uint32_t g[16], u[16];
+                    tmem_ld16(base + (uint32_t)c0, g);
+                    tmem_ld16(base + 128u + (uint32_t)c0, u);
                     tmem_wait_ld();
                     const int n = min(16, rows - c0);
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
-                        if (j < n) *dst = __float2half_rn(__uint_as_float(v[j]));
+                        if (j < n) *dst = silu_fast(__uint_as_float(g[j])) * __uint_as_float(u[j]);
+                        dst += a.F;
+                    }
+                }
+            } else {
+                __half *dst = a.Y + (size_t)t * 128 * a.E + p * 256 + 32 * lg + lane;
+                for (int c0 = 0; c0 < rows; c0 += 16) {
+                    uint32_t y0[16], y1[16];
+                    tmem_ld16(base + (uint32_t)c0, y0);
+                    tmem_ld16(base + 128u + (uint32_t)c0, y1);
+                    tmem_wait_ld();
+                    const int n = min(16, rows - c0);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        if (j < n) {
+                            dst[0] = __float2half_rn(__uint_as_float(y0[j]));
+                            dst[128] = __float2half_rn(__uint_as_float(y1[j]));
+                        }
                         dst += a.E;
                     }
                 }
             }
-            if (!ok) break;
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&acc_empty[ab]);
+            if (lane == 0) mbar_arrive(acc_empty);
         }
     }
     tc_fence_before();
@@ -389,7 +356,7 @@ bool gemm_ts_routed(uint32_t type) {
 
 bool gemm_ts_supports(const GemmArgs &a, int mode) {
     if (type_k(a.type) == 0 || a.K % 128 != 0) return false;
-    return mode == 0 ? a.F % 64 == 0 : a.E % 128 == 0;
+    return mode == 0 ? a.F % 128 == 0 : a.E % 256 == 0;
 }
 
 cudaError_t launch_moe_gemm_ts(const GemmArgs &a, int mode, int sm_count, cudaStream_t s) {
