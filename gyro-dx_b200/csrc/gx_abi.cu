@@ -738,6 +738,10 @@ gx_result enqueue_layer_prefill(gx_context *c, const Layer &L, const void *x, ui
     gm.E = (int)L.E;
     gm.codebook = c->codebook;
     gm.err = c->err;
+    if (gx::gemm_ts_routed(L.type)) {
+        gm.down_A = p.A2;   // the gate/up epilogue packs the down operand
+        gm.down_signs = L.down_signs;
+    }
     GX_CUDA(gx::launch_moe_gemm(gm, 0, c->sm_count, c->stream));
     if (ev) GX_CUDA(record_phase(ev[2], c->stream));
     gx::PackArgs pd{};
@@ -752,7 +756,7 @@ gx_result enqueue_layer_prefill(gx_context *c, const Layer &L, const void *x, ui
     pd.n_mtiles = p.n_mtiles;
     pd.dst = p.A2;
     pd.compact = gx::gemm_ts_routed(L.type);
-    GX_CUDA(gx::launch_pack_rows(pd, (int)p.max_tiles, c->stream));
+    if (!gx::gemm_ts_routed(L.type)) GX_CUDA(gx::launch_pack_rows(pd, (int)p.max_tiles, c->stream));
     gm.w0 = L.down;
     gm.w1 = nullptr;
     gm.expert_bytes = L.down_expert_bytes;
@@ -1111,6 +1115,10 @@ gx_result enqueue_layer_ep_peer(gx_context *c, const Layer &L, const void *x, in
     gm.E = (int)L.E;
     gm.codebook = c->codebook;
     gm.err = c->err;
+    if (gx::gemm_ts_routed(L.type)) {
+        gm.down_A = p.A2;   // the gate/up epilogue packs the down operand
+        gm.down_signs = L.down_signs;
+    }
     GX_CUDA(gx::launch_moe_gemm(gm, 0, c->sm_count, c->stream));
     if (ev) GX_CUDA(record_phase(ev[2], c->stream));
     gx::PackArgs pd{};
@@ -1124,7 +1132,7 @@ gx_result enqueue_layer_ep_peer(gx_context *c, const Layer &L, const void *x, in
     pd.n_mtiles = p.n_mtiles;
     pd.dst = p.A2;
     pd.compact = gx::gemm_ts_routed(L.type);
-    GX_CUDA(gx::launch_pack_rows(pd, (int)p.max_tiles, c->stream));
+    if (!gx::gemm_ts_routed(L.type)) GX_CUDA(gx::launch_pack_rows(pd, (int)p.max_tiles, c->stream));
     gm.w0 = L.down;
     gm.w1 = nullptr;
     gm.expert_bytes = L.down_expert_bytes;
@@ -1310,6 +1318,10 @@ gx_result enqueue_layer_ep(gx_context *c, const Layer &L, const void *x, uint32_
         gm.E = (int)L.E;
         gm.codebook = c->codebook;
         gm.err = c->err;
+        if (gx::gemm_ts_routed(L.type)) {
+            gm.down_A = p.A2;   // the gate/up epilogue packs the down operand
+            gm.down_signs = L.down_signs;
+        }
         GX_CUDA(gx::launch_moe_gemm(gm, 0, c->sm_count, c->stream));
         if (ev) GX_CUDA(record_phase(ev[2], c->stream));
         gx::PackArgs pd{};
@@ -1323,7 +1335,7 @@ gx_result enqueue_layer_ep(gx_context *c, const Layer &L, const void *x, uint32_
         pd.n_mtiles = p.n_mtiles;
         pd.dst = p.A2;
         pd.compact = gx::gemm_ts_routed(L.type);
-        GX_CUDA(gx::launch_pack_rows(pd, (int)p.max_tiles, c->stream));
+        if (!gx::gemm_ts_routed(L.type)) GX_CUDA(gx::launch_pack_rows(pd, (int)p.max_tiles, c->stream));
         gm.w0 = L.down;
         gm.w1 = nullptr;
         gm.expert_bytes = L.down_expert_bytes;

@@ -54,7 +54,8 @@ static_assert((kTsTStages & (kTsTStages - 1)) == 0 && (kTsWStages & (kTsWStages 
 struct TsSmem {
     static constexpr int TOK = 0;                                   // per stage +kTsTok
     static constexpr int CB = kTsTStages * kTsTok;
-    static constexpr int BARS = CB + Codebook<kTsCopies>::BYTES;
+    static constexpr int XT = CB + Codebook<kTsCopies>::BYTES;      // 2 x [16 tokens][128 columns] f32
+    static constexpr int BARS = XT + 2 * 16 * 128 * 4;
     static constexpr int BYTES = BARS + 256;
 };
 
@@ -84,7 +85,9 @@ __global__ void __launch_bounds__(kTsThreads, 1) moe_gemm_ts_kernel(GemmArgs a) 
     uint64_t *empty_w = full_w + kTsWStages;
     uint64_t *acc_full = empty_w + kTsWStages;
     uint64_t *acc_empty = acc_full + 1;
-    uint64_t *done = acc_empty + 1;
+    uint64_t *xt_full = acc_empty + 1;         // fused down packing: a chunk of act rows in xt
+    uint64_t *xt_free = xt_full + 2;           // ... and read by all four epilogue warps
+    uint64_t *done = xt_free + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
@@ -104,6 +107,10 @@ __global__ void __launch_bounds__(kTsThreads, 1) moe_gemm_ts_kernel(GemmArgs a) 
         }
         mbar_init(acc_full, 1);
         mbar_init(acc_empty, 4);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&xt_full[b], 4);
+            mbar_init(&xt_free[b], 4);
+        }
         mbar_init(done, 1);
         *abort_flag = 0;
         fence_barrier_init();
@@ -281,14 +288,58 @@ __global__ void __launch_bounds__(kTsThreads, 1) moe_gemm_ts_kernel(GemmArgs a) 
     } else {
         // ---- epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 of both accumulators --------
         const int lg = warp & 3;
-        int cnt = 0;
+        float *xt = reinterpret_cast<float *>(sm + TsSmem::XT);
+        int cnt = 0, ch = 0;
         for (int it = blockIdx.x; it < n_items; it += gridDim.x, ++cnt) {
             const int t = it / n_p, p = it % n_p;
             const int rows = rows_of(t);
             if (!wait(acc_full, cnt & 1)) break;
             tc_fence_after();
             const uint32_t base = tmem_base + ((uint32_t)(32 * lg) << 16);
-            if (MODE == 0) {
+            bool ok = true;
+            if (MODE == 0 && a.down_A) {
+                // act = silu(g) * u of columns [128 p, 128 p + 128) for 16 tokens at a time: each
+                // warp puts its 32 columns (times the down signs) into xt, then each warp takes 4
+                // tokens: 128-point Hadamard across the warp (with signs only, as pack_rows_kernel),
+                // f16, into the down operand tiles (k-steps 2p and 2p + 1 of the token tile;
+                // pack_rows_kernel's compact layout)
+                const int f = p * 128 + 32 * lg + lane;
+                const float sgn = a.down_signs ? a.down_signs[f] : 1.f;
+                const uint32_t kblock = tile_cols(rows) * 128u;
+                uint8_t *tile_out = a.down_A + (size_t)t * (a.F / 64) * 16384u;
+                for (int c0 = 0; c0 < rows; c0 += 16, ++ch) {
+                    const int b = ch & 1;
+                    uint32_t g[16], u[16];
+                    tmem_ld16(base + (uint32_t)c0, g);
+                    tmem_ld16(base + 128u + (uint32_t)c0, u);
+                    tmem_wait_ld();
+                    if (!wait(&xt_free[b], ((ch >> 1) & 1) ^ 1)) { ok = false; break; }
+                    float *xb = xt + b * 16 * 128;
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        xb[j * 128 + 32 * lg + lane] = silu_fast(__uint_as_float(g[j])) * __uint_as_float(u[j]) * sgn;
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&xt_full[b]);
+                    if (!wait(&xt_full[b], (ch >> 1) & 1)) { ok = false; break; }
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const int jj = 4 * lg + q;
+                        const float4 x4 = *reinterpret_cast<const float4 *>(xb + jj * 128 + 4 * lane);
+                        float v[4] = {x4.x, x4.y, x4.z, x4.w};
+                        if (a.down_signs) fwht128_warp(v, lane);   // unrotated layers: no transform
+                        if (c0 + jj < rows) {
+                            const int col = 4 * lane;             // column of the 128 block
+                            uint8_t *blk = tile_out + (size_t)(2 * p + (col >> 6)) * kblock;
+                            uint2 o;
+                            o.x = pack_half2(v[0], v[1]);
+                            o.y = pack_half2(v[2], v[3]);
+                            *reinterpret_cast<uint2 *>(blk + sw128_offset((uint32_t)(c0 + jj), (uint32_t)(col & 63))) = o;
+                        }
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&xt_free[b]);
+                }
+            } else if (MODE == 0) {
                 // lane i: gate row and up row f of the pair, both in TMEM lane i
                 float *dst = a.act + (size_t)t * 128 * a.F + p * 128 + 32 * lg + lane;
                 for (int c0 = 0; c0 < rows; c0 += 16) {
@@ -321,6 +372,7 @@ __global__ void __launch_bounds__(kTsThreads, 1) moe_gemm_ts_kernel(GemmArgs a) 
                     }
                 }
             }
+            if (!ok) break;
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(acc_empty);

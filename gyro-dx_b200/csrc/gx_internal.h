@@ -191,6 +191,11 @@ struct GemmArgs {
     int E;
     const uint32_t *codebook;
     int *err;
+    // moe_gemm_ts_kernel, mode 0: when set, the epilogue writes the down GEMM's operand tiles
+    // (act * down signs, 128-point Hadamard per block, f16, compact layout of pack_rows_kernel)
+    // instead of act
+    uint8_t *down_A;
+    const float *down_signs;
 };
 
 struct CombineArgs {
