@@ -548,32 +548,61 @@ def run_ep(args):
     ctx.wait(tickets[-1])
     (ms,) = d.reduce([ms], "max")
 
-    # parity (after the timed region): the stack on the unscaled batch, and layer 0's routing
+    # parity (after the timed region), per layer: the batch goes through the stack one layer at a
+    # time in f32 (the same pre-norm residual step, x_{l+1} = x_l + MoE_l(RMSNorm(x_l))), and for
+    # the sampled tokens the oracle computes MoE_l on the GPU's own input x_l of that layer. The
+    # whole-stack comparison (both sides run their own 40-layer chain) is reported as well: there
+    # a near tie in a deep layer's top-k can route a token differently on the two sides, which is
+    # not a per-layer error, so it is not the pass/fail criterion.
     ctx.wait(ctx.stack_forward(0, args.layers, xs[0], y))
-    got = y[torch.from_numpy(prow).to(dev)].float().cpu().numpy() if prow.size else np.zeros((0, E), np.float32)
+    got_chain = y[torch.from_numpy(prow).to(dev)].float().cpu().numpy() if prow.size else np.zeros((0, E), np.float32)
     ids = torch.empty((n_tok, U), dtype=torch.int32, device=dev)
     ctx.set_flags(abi.GX_FLAG_PROFILE)
     ctx.wait(ctx.forward(0, xs[0], y, ids))
     ph = ctx.timings()
     ctx.set_flags(0)
     ids_np = ids.cpu().numpy()
+    prow_t = torch.from_numpy(prow).to(dev)
+    xl = xs[0].float().contiguous()
+    yl = torch.empty_like(xl)
+    sample_in, sample_out = [], []
+    for l in range(args.layers):
+        ctx.wait(ctx.stack_forward(l, 1, xl, yl))
+        if prow.size:
+            sample_in.append(xl[prow_t].cpu().numpy())
+            sample_out.append(yl[prow_t].cpu().numpy())
+        xl, yl = yl, xl
+    worst_rel, worst_cos, sq_err, sq_ref = 0.0, 1.0, 0.0, 0.0
+    for l in range(args.layers if prow.size else 0):
+        layer = host_layers[l] if keep_host else synth.make_layer(LAYER_SEED + l, zipf=1.1)
+        want, _, _ = oracle.moe_ffn(layer, oracle.rms_norm(sample_in[l]))
+        have = sample_out[l].astype(np.float64) - sample_in[l].astype(np.float64)
+        m = metrics.compare(want, have)
+        worst_rel, worst_cos = max(worst_rel, m["rel_rms"]), min(worst_cos, m["cosine"])
+        sq_err += float(((want.astype(np.float64) - have) ** 2).sum())
+        sq_ref += float((want.astype(np.float64) ** 2).sum())
     if prow.size:
-        m = metrics.compare(ref_out, got)
         flips = metrics.topk_sets(ref_ids0, ids_np[prow])["flips"]
-        sq_err = float(((ref_out.astype(np.float64) - got) ** 2).sum())
-        sq_ref = float((ref_out.astype(np.float64) ** 2).sum())
-        worst_cos, worst_rel = m["cosine"], m["rel_rms"]
+        mc = metrics.compare(ref_out, got_chain)
+        c_err = float(((ref_out.astype(np.float64) - got_chain) ** 2).sum())
+        c_ref = float((ref_out.astype(np.float64) ** 2).sum())
     else:
-        flips, sq_err, sq_ref, worst_cos, worst_rel = 0, 0.0, 0.0, 1.0, 0.0
-    sq_err, sq_ref, flips_all, checked = d.reduce([sq_err, sq_ref, flips, prow.size], "sum")
-    (worst_cos,) = d.reduce([worst_cos], "min")
-    (worst_rel,) = d.reduce([worst_rel], "max")
-    parity = {"tokens_checked": int(checked), "rel_rms": float(np.sqrt(sq_err / sq_ref)) if sq_ref else 0.0,
-              "worst_rank_rel_rms": worst_rel, "worst_rank_cosine": worst_cos, "layer0_topk_flips": int(flips_all),
-              "oracle": "oracle/ CPU restatement of src/engine.zig:520-642 (strict build), the same tokens through "
-                        f"all {args.layers} layers (pre-norm residual), checked after the timed region",
-              "tolerance": {"rel_rms": 1e-2, "cosine": 0.9999}}
-    parity["ok"] = parity["rel_rms"] <= 1e-2 and worst_cos >= 0.9999 and parity["layer0_topk_flips"] == 0
+        flips, c_err, c_ref, mc = 0, 0.0, 0.0, {"cosine": 1.0, "rel_rms": 0.0}
+    sq_err, sq_ref, c_err, c_ref, flips_all, checked = d.reduce([sq_err, sq_ref, c_err, c_ref, flips, prow.size], "sum")
+    worst_cos, chain_cos = d.reduce([worst_cos, mc["cosine"]], "min")
+    worst_rel, chain_worst = d.reduce([worst_rel, mc["rel_rms"]], "max")
+    parity = {"tokens_checked": int(checked), "layers_checked": args.layers,
+              "rel_rms": float(np.sqrt(sq_err / sq_ref)) if sq_ref else 0.0,
+              "worst_layer_rel_rms": worst_rel, "worst_layer_cosine": worst_cos, "layer0_topk_flips": int(flips_all),
+              "oracle": "oracle/ CPU restatement of src/engine.zig:520-642 (strict build): MoE_l of every layer on "
+                        "the GPU's own f32 input of that layer, for the sampled tokens of every rank, after the "
+                        "timed region; layer 0's top-k sets against the oracle's",
+              "tolerance": {"rel_rms": 1e-2, "cosine": 0.9999},
+              "chain": {"rel_rms": float(np.sqrt(c_err / c_ref)) if c_ref else 0.0, "worst_rank_rel_rms": chain_worst,
+                        "worst_rank_cosine": chain_cos,
+                        "what": f"bf16 tokens through both sides' own {args.layers}-layer chains (informational: a "
+                                "routing near-tie in a deep layer moves a token's whole remaining chain)"}}
+    parity["ok"] = worst_rel <= 1e-2 and worst_cos >= 0.9999 and parity["layer0_topk_flips"] == 0
 
     # roofline: the gate/up grouped GEMM on every rank's received slots, one profiled layer-0 call
     per = NE // world
