@@ -15,13 +15,14 @@
 // ([tile][K/64][rows16 x 128 B], 128-byte swizzle); the outputs have moe_gemm_kernel's layout:
 // act [tiles*128][F] f32 (silu(g) * u) and Y [tiles*128][E] f16.
 //
-// Roles (704 threads):
+// Roles (832 threads):
 //   warp 0      token tiles: as many 64-wide k-steps of the tile as fit 32 KB per bulk copy
 //   warp 1      TMEM allocation; one lane issues the MMAs (8 per k-step) and the commits
 //   warps 2-17  decoders in 2 sets of 8 warps: set j decodes the CTA's k-steps n = j, j + 2, ...
 //               (over its items in order); (warp - 2) / 4 % 2 picks the weight tile and warp % 4
 //               the TMEM lane quarter; one thread decodes one weight row's 64 weights of a k-step
-//   warps 18-21 epilogue: the accumulators to act or Y, then the MMAs of the next item start
+//   warps 18-25 epilogue in two groups of 4 (alternate 16-token chunks): the accumulators to act,
+//               to the down operand tiles, or to Y; then the MMAs of the next item start
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -42,7 +43,8 @@ constexpr int kTsWStages = 4;                  // decoded k-steps (both weight t
 constexpr int kTsCopies = 8;
 constexpr int kTsDecWarps = 8 * kTsSets;
 constexpr int kTsEpiWarp = 2 + kTsDecWarps;
-constexpr int kTsThreads = 32 * (kTsEpiWarp + 4);
+constexpr int kTsEpiWarps = 8;                 // two groups of 4 (one warp per TMEM lane quarter)
+constexpr int kTsThreads = 32 * (kTsEpiWarp + kTsEpiWarps);
 constexpr int kTsTok = 32768;                  // as many k-steps of the tile's rows as fit (>= 2)
 // TMEM columns: accumulators of tiles 0 and 1 at 0 and 128 (up to 128 tokens each), weight
 // stage s of tile w at 256 + 32 (2 s + w)
@@ -54,8 +56,8 @@ static_assert((kTsTStages & (kTsTStages - 1)) == 0 && (kTsWStages & (kTsWStages 
 struct TsSmem {
     static constexpr int TOK = 0;                                   // per stage +kTsTok
     static constexpr int CB = kTsTStages * kTsTok;
-    static constexpr int XT = CB + Codebook<kTsCopies>::BYTES;      // 2 x [16 tokens][128 columns] f32
-    static constexpr int BARS = XT + 2 * 16 * 128 * 4;
+    static constexpr int XT = CB + Codebook<kTsCopies>::BYTES;      // 2 groups x 2 x [16 tokens][128 columns] f32
+    static constexpr int BARS = XT + 2 * 2 * 16 * 128 * 4;
     static constexpr int BYTES = BARS + 256;
 };
 
@@ -85,9 +87,9 @@ __global__ void __launch_bounds__(kTsThreads, 1) moe_gemm_ts_kernel(GemmArgs a) 
     uint64_t *empty_w = full_w + kTsWStages;
     uint64_t *acc_full = empty_w + kTsWStages;
     uint64_t *acc_empty = acc_full + 1;
-    uint64_t *xt_full = acc_empty + 1;         // fused down packing: a chunk of act rows in xt
-    uint64_t *xt_free = xt_full + 2;           // ... and read by all four epilogue warps
-    uint64_t *done = xt_free + 2;
+    uint64_t *xt_full = acc_empty + 1;         // fused down packing, per group and buffer: a chunk
+    uint64_t *xt_free = xt_full + 4;           // of act rows in xt / read by the group's 4 warps
+    uint64_t *done = xt_free + 4;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
@@ -106,8 +108,8 @@ __global__ void __launch_bounds__(kTsThreads, 1) moe_gemm_ts_kernel(GemmArgs a) 
             mbar_init(&empty_w[s], 1);
         }
         mbar_init(acc_full, 1);
-        mbar_init(acc_empty, 4);
-        for (int b = 0; b < 2; ++b) {
+        mbar_init(acc_empty, kTsEpiWarps);
+        for (int b = 0; b < 4; ++b) {
             mbar_init(&xt_full[b], 4);
             mbar_init(&xt_free[b], 4);
         }
@@ -286,9 +288,11 @@ __global__ void __launch_bounds__(kTsThreads, 1) moe_gemm_ts_kernel(GemmArgs a) 
             have = more;
         }
     } else {
-        // ---- epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 of both accumulators --------
-        const int lg = warp & 3;
-        float *xt = reinterpret_cast<float *>(sm + TsSmem::XT);
+        // ---- epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 of both accumulators; group g
+        // (4 warps) takes the 16-token chunks c with c % 2 == g ----------------------------------
+        const int lg = warp & 3, eg = (warp - kTsEpiWarp) >> 2;
+        float *xt = reinterpret_cast<float *>(sm + TsSmem::XT) + eg * 2 * 16 * 128;
+        uint64_t *xfull = xt_full + 2 * eg, *xfree = xt_free + 2 * eg;
         int cnt = 0, ch = 0;
         for (int it = blockIdx.x; it < n_items; it += gridDim.x, ++cnt) {
             const int t = it / n_p, p = it % n_p;
@@ -299,28 +303,28 @@ __global__ void __launch_bounds__(kTsThreads, 1) moe_gemm_ts_kernel(GemmArgs a) 
             bool ok = true;
             if (MODE == 0 && a.down_A) {
                 // act = silu(g) * u of columns [128 p, 128 p + 128) for 16 tokens at a time: each
-                // warp puts its 32 columns (times the down signs) into xt, then each warp takes 4
-                // tokens: 128-point Hadamard across the warp (with signs only, as pack_rows_kernel),
-                // f16, into the down operand tiles (k-steps 2p and 2p + 1 of the token tile;
-                // pack_rows_kernel's compact layout)
+                // warp of the group puts its 32 columns (times the down signs) into xt, then each
+                // takes 4 tokens: 128-point Hadamard across the warp (with signs only, as
+                // pack_rows_kernel), f16, into the down operand tiles (k-steps 2p and 2p + 1 of the
+                // token tile; pack_rows_kernel's compact layout)
                 const int f = p * 128 + 32 * lg + lane;
                 const float sgn = a.down_signs ? a.down_signs[f] : 1.f;
                 const uint32_t kblock = tile_cols(rows) * 128u;
                 uint8_t *tile_out = a.down_A + (size_t)t * (a.F / 64) * 16384u;
-                for (int c0 = 0; c0 < rows; c0 += 16, ++ch) {
+                for (int c0 = 16 * eg; c0 < rows; c0 += 32, ++ch) {
                     const int b = ch & 1;
                     uint32_t g[16], u[16];
                     tmem_ld16(base + (uint32_t)c0, g);
                     tmem_ld16(base + 128u + (uint32_t)c0, u);
                     tmem_wait_ld();
-                    if (!wait(&xt_free[b], ((ch >> 1) & 1) ^ 1)) { ok = false; break; }
+                    if (!wait(&xfree[b], ((ch >> 1) & 1) ^ 1)) { ok = false; break; }
                     float *xb = xt + b * 16 * 128;
 #pragma unroll
                     for (int j = 0; j < 16; ++j)
                         xb[j * 128 + 32 * lg + lane] = silu_fast(__uint_as_float(g[j])) * __uint_as_float(u[j]) * sgn;
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&xt_full[b]);
-                    if (!wait(&xt_full[b], (ch >> 1) & 1)) { ok = false; break; }
+                    if (lane == 0) mbar_arrive(&xfull[b]);
+                    if (!wait(&xfull[b], (ch >> 1) & 1)) { ok = false; break; }
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
                         const int jj = 4 * lg + q;
@@ -337,39 +341,43 @@ __global__ void __launch_bounds__(kTsThreads, 1) moe_gemm_ts_kernel(GemmArgs a) 
                         }
                     }
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&xt_free[b]);
+                    if (lane == 0) mbar_arrive(&xfree[b]);
                 }
             } else if (MODE == 0) {
                 // lane i: gate row and up row f of the pair, both in TMEM lane i
-                float *dst = a.act + (size_t)t * 128 * a.F + p * 128 + 32 * lg + lane;
-                for (int c0 = 0; c0 < rows; c0 += 16) {
+                float *dst = a.act + ((size_t)t * 128 + 16 * eg) * a.F + p * 128 + 32 * lg + lane;
+                for (int c0 = 16 * eg; c0 < rows; c0 += 32) {
                     uint32_t g[16], u[16];
                     tmem_ld16(base + (uint32_t)c0, g);
                     tmem_ld16(base + 128u + (uint32_t)c0, u);
                     tmem_wait_ld();
                     const int n = min(16, rows - c0);
+                    float *d0 = dst;
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
-                        if (j < n) *dst = silu_fast(__uint_as_float(g[j])) * __uint_as_float(u[j]);
-                        dst += a.F;
+                        if (j < n) *d0 = silu_fast(__uint_as_float(g[j])) * __uint_as_float(u[j]);
+                        d0 += a.F;
                     }
+                    dst += (size_t)32 * a.F;
                 }
             } else {
-                __half *dst = a.Y + (size_t)t * 128 * a.E + p * 256 + 32 * lg + lane;
-                for (int c0 = 0; c0 < rows; c0 += 16) {
+                __half *dst = a.Y + ((size_t)t * 128 + 16 * eg) * a.E + p * 256 + 32 * lg + lane;
+                for (int c0 = 16 * eg; c0 < rows; c0 += 32) {
                     uint32_t y0[16], y1[16];
                     tmem_ld16(base + (uint32_t)c0, y0);
                     tmem_ld16(base + 128u + (uint32_t)c0, y1);
                     tmem_wait_ld();
                     const int n = min(16, rows - c0);
+                    __half *d0 = dst;
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
                         if (j < n) {
-                            dst[0] = __float2half_rn(__uint_as_float(y0[j]));
-                            dst[128] = __float2half_rn(__uint_as_float(y1[j]));
+                            d0[0] = __float2half_rn(__uint_as_float(y0[j]));
+                            d0[128] = __float2half_rn(__uint_as_float(y1[j]));
                         }
-                        dst += a.E;
+                        d0 += a.E;
                     }
+                    dst += (size_t)32 * a.E;
                 }
             }
             if (!ok) break;
