@@ -219,12 +219,13 @@ gx_result wait_event(gx_context *c, cudaEvent_t ev, uint32_t timeout_ms) {
     cudaError_t e = cudaMemcpy(&err, c->err, sizeof(int), cudaMemcpyDeviceToHost);
     if (e != cudaSuccess) return fail_cuda(c, e);
     if (err != 0) {
-        if (debug_enabled()) std::fprintf(stderr, "gyro_moe: kernel error word %d (1 = expired wait, 2 = bad expert id)\n", err);
+        if (debug_enabled())
+            std::fprintf(stderr, "gyro_moe: kernel error word %d (1 = expired wait, 2 = bad expert id, 3 = output not finite)\n", err);
         cudaMemset(c->err, 0, sizeof(int));
         // an expired wait in an expert-parallel group means a peer fell out of step: the exchange
         // epochs of the ranks no longer agree, so the context takes no further calls
         if (c->world > 1 && err == gx::KERR_WAIT) c->broken = true;
-        return GX_E_KERNEL;
+        return err == gx::KERR_RANGE ? GX_E_RANGE : GX_E_KERNEL;
     }
     return GX_OK;
 }
@@ -765,6 +766,7 @@ gx_result enqueue_layer_prefill(gx_context *c, const Layer &L, const void *x, ui
     gm.A = p.A2;
     GX_CUDA(gx::launch_moe_gemm(gm, 1, c->sm_count, c->stream));
     gx::CombineArgs ca{};
+    ca.err = c->err;
     ca.Y = p.Y;
     ca.slot_row = p.slot_row;
     ca.weights = c->weights;
@@ -1143,6 +1145,7 @@ gx_result enqueue_layer_ep_peer(gx_context *c, const Layer &L, const void *x, in
     GX_CUDA(gx::launch_ep_return(pa, p.Y, p.slot_row, c->stream));
     GX_CUDA(gx::launch_ep_wait_ret(pa, c->stream));
     gx::EpCombineArgs ec{};
+    ec.err = c->err;
     ec.ret = reinterpret_cast<const __half *>(e.block + e.off.ret_rows);
     ec.pos_of = e.pos_of;
     ec.W = W;
@@ -1344,6 +1347,7 @@ gx_result enqueue_layer_ep(gx_context *c, const Layer &L, const void *x, uint32_
         gm.A = p.A2;
         GX_CUDA(gx::launch_moe_gemm(gm, 1, c->sm_count, c->stream));
         gx::CombineArgs ca{};
+        ca.err = c->err;
         ca.Y = p.Y;
         ca.slot_row = p.slot_row;
         ca.weights = e.recv_w;
@@ -1365,6 +1369,7 @@ gx_result enqueue_layer_ep(gx_context *c, const Layer &L, const void *x, uint32_
     r = comm_group_end(c, "combine");
     if (r != GX_OK) return r;
     gx::EpCombineArgs ec{};
+    ec.err = c->err;
     ec.ret = e.ret_rows;
     ec.pos_of = e.pos_of;
     ec.W = W;

@@ -554,6 +554,7 @@ __device__ __forceinline__ bool phase_down(const StackArgs &a, const StackLayer 
             }
             const size_t o = (size_t)t * g.E + row;
             if (a.residual) v = (s == 0 && r == tid ? resid0 : ldcg_act(cur, cur_bf16, o)) + v;
+            if (!(fabsf(v) <= 3.4028235e38f)) atomicExch(a.err, KERR_RANGE);   // Inf or NaN
             store_act(dst, dst_bf16, o, v);
         }
         __syncthreads();

@@ -169,14 +169,17 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(EpCombineArgs a) {
         v[3] += f1.y * g;
     }
     const size_t o = (size_t)t * a.E + c;
+    bool bad = false;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         if (a.resid) v[j] = load_act(a.resid, a.resid_bf16, o + j) + v[j];
+        bad |= !(fabsf(v[j]) <= 3.4028235e38f);   // Inf or NaN
         if (a.out_bf16)
             reinterpret_cast<__nv_bfloat16 *>(a.out)[o + j] = __float2bfloat16_rn(v[j]);
         else
             reinterpret_cast<float *>(a.out)[o + j] = v[j];
     }
+    if (bad && a.err) atomicExch(a.err, KERR_RANGE);
 }
 
 cudaError_t launch_ep_plan(const EpPlanArgs &a, cudaStream_t s) {

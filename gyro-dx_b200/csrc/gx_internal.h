@@ -8,7 +8,9 @@
 namespace gx {
 
 // Error codes a kernel can leave in the context's device error word.
-enum : int { KERR_NONE = 0, KERR_WAIT = 1, KERR_BOUNDS = 2 };
+// KERR_RANGE: a layer output is not finite (an f16 operand or intermediate overflowed, or the
+// input held Inf/NaN); the output writers record it.
+enum : int { KERR_NONE = 0, KERR_WAIT = 1, KERR_BOUNDS = 2, KERR_RANGE = 3 };
 
 // Shared-memory codebook copies of the decode-GEMV kernels (2 banks per copy, so at most two
 // lanes of a warp contend for a bank during a lookup).
@@ -210,6 +212,7 @@ struct CombineArgs {
     int out_bf16;
     int out_f16;             // f16 output (expert-parallel partial rows); overrides out_bf16
     int n_tok, U, E;
+    int *err;                // KERR_RANGE when an output is not finite (or beyond f16 for out_f16)
 };
 
 cudaError_t launch_router_gemm(const float *W, const void *x, int x_bf16, int n_tok, int NE, int E, float *C,
@@ -292,7 +295,7 @@ struct EpCombineArgs {
     int resid_bf16;
     void *out;               // [n_tok][E]
     int out_bf16;
-    int n_tok, E;
+    int n_tok, E;    int *err;                // KERR_RANGE when an output is not finite
 };
 
 // ---- expert-parallel exchange over NVLink peer memory -------------------------------------

@@ -769,6 +769,7 @@ __global__ void __launch_bounds__(512, 1) down_kernel(DownArgs a, int P) {
             const size_t o = (size_t)t * a.E + row;
             if (a.extra) v += a.extra[o];
             if (a.resid) v = load_act(a.resid, a.resid_bf16, o) + v;
+            if (!(fabsf(v) <= 3.4028235e38f)) atomicExch(a.err, KERR_RANGE);   // Inf or NaN
             if (a.out_bf16)
                 reinterpret_cast<__nv_bfloat16 *>(a.out)[o] = __float2bfloat16_rn(v);
             else

@@ -638,9 +638,11 @@ __global__ void __launch_bounds__(256) combine_kernel(CombineArgs a) {
         v[3] += f1.y * g;
     }
     const size_t o = (size_t)t * a.E + c;
+    bool bad = false;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         if (a.resid) v[j] = load_act(a.resid, a.resid_bf16, o + j) + v[j];
+        bad |= !(fabsf(v[j]) <= (a.out_f16 ? 65504.f : 3.4028235e38f));   // NaN fails the test too
         if (a.out_f16)
             reinterpret_cast<__half *>(a.out)[o + j] = __float2half_rn(v[j]);
         else if (a.out_bf16)
@@ -648,6 +650,7 @@ __global__ void __launch_bounds__(256) combine_kernel(CombineArgs a) {
         else
             reinterpret_cast<float *>(a.out)[o + j] = v[j];
     }
+    if (bad && a.err) atomicExch(a.err, KERR_RANGE);
 }
 
 // ------------------------------------------------------------------------------------------

@@ -18,7 +18,8 @@ CODEBOOK_PATH = PKG / "data" / "gyro_codebook.f16"
 
 GX_OK = 0
 ERRORS = {-1: "GX_E_INVALIDARG", -2: "GX_E_OUTOFMEMORY", -3: "GX_E_TIMEOUT", -4: "GX_E_DEVICE",
-          -5: "GX_E_UNSUPPORTED", -6: "GX_E_STATE", -7: "GX_E_MISMATCH", -8: "GX_E_COMM", -9: "GX_E_KERNEL"}
+          -5: "GX_E_UNSUPPORTED", -6: "GX_E_STATE", -7: "GX_E_MISMATCH", -8: "GX_E_COMM", -9: "GX_E_KERNEL",
+          -10: "GX_E_RANGE"}
 GX_F32, GX_Q8_0, GX_BF16 = 0, 8, 30
 GX_FLAG_PROFILE = 1
 GX_EP_NONE, GX_EP_NCCL, GX_EP_PEER = 0, 1, 2     # gx_caps.ep_exchange

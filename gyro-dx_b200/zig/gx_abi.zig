@@ -16,6 +16,7 @@ pub const e_state: gx_result = -6;
 pub const e_mismatch: gx_result = -7;
 pub const e_comm: gx_result = -8;
 pub const e_kernel: gx_result = -9;
+pub const e_range: gx_result = -10;
 
 pub const dtype_f32: u32 = 0;
 pub const dtype_q8_0: u32 = 8;

@@ -51,7 +51,10 @@ enum {
     GX_E_STATE = -6,        /* call out of order (layer not uploaded, context closed) */
     GX_E_MISMATCH = -7,     /* gx_decode_blocks: an output differs from the expected bits */
     GX_E_COMM = -8,         /* NCCL failure or peer loss in the expert-parallel group */
-    GX_E_KERNEL = -9        /* a kernel's bounded wait expired; its outputs are invalid */
+    GX_E_KERNEL = -9,       /* a kernel's bounded wait expired; its outputs are invalid */
+    GX_E_RANGE = -10        /* a layer output is not finite: the input held Inf/NaN, or an
+                               activation outgrew the f16 operands of the tensor-core path (or the
+                               f16 hi/lo split of the decode path); the outputs are invalid */
 };
 
 /* Activation encodings, and the weight encodings of a shared expert (the type ids of
