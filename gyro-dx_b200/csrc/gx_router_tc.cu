@@ -15,6 +15,8 @@
 // drain the accumulator; warp 4 streams the pre-swizzled weight parts with one bulk copy per
 // step; warp 5 owns TMEM and issues the MMAs. Every wait is bounded.
 #include <cuda_bf16.h>
+
+#include <algorithm>
 #include <cuda_runtime.h>
 
 #include "gx_device.cuh"
@@ -226,11 +228,15 @@ cudaError_t router_tc_t(const RtArgs &a, dim3 grid, cudaStream_t s) {
 
 }  // namespace
 
+// K splits of the router GEMM: as many as keep the grid to one wave of CTAs (each CTA streams
+// its slice of the three router parts, so more CTAs means more SMs pulling them in), limited by
+// the partial-logit scratch of the context (4 x 512 columns per token) and by E / 64.
 int router_tc_splits(int n_tok, int NE, int E, int sm_count) {
     const int tiles = ((n_tok + 127) / 128) * ((NE + 127) / 128);
     const int KS = E / 64;
+    const int cap = std::min(16, 4 * 512 / (((NE + 127) / 128) * 128));
     int splits = 1;
-    while (splits < 4 && tiles * splits * 2 <= sm_count + tiles && KS % (splits * 2) == 0) splits *= 2;
+    while (splits * 2 <= cap && tiles * splits * 2 <= sm_count && KS % (splits * 2) == 0) splits *= 2;
     return splits;
 }
 
