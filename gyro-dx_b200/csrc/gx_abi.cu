@@ -24,6 +24,7 @@ constexpr int kEvents = 64;
 // Token count from which a forward call takes the tensor-core prefill path (grouped GEMM over
 // expert row tiles) instead of the per-slot decode GEMVs.
 constexpr uint32_t kPrefillMinTokens = 64;
+constexpr uint32_t kChainPdlMaxTokens = 2048;
 // RMSNorm epsilon of the stack's pre-norm residual x_{l+1} = x_l + MoE_l(RMSNorm(x_l)).
 constexpr float kStackNormEps = 1e-6f;
 
@@ -387,6 +388,8 @@ gx_result ensure_prefill(gx_context *c, const Layer &L, size_t slots) {
     GX_CUDA(cudaMalloc(&p.xh, (size_t)c->max_tokens * L.E * sizeof(__half)));
     const size_t n_ints = 1024 + 2 * tiles + 1 + tiles * 128 + slots;
     GX_CUDA(cudaMalloc(&p.ints, n_ints * sizeof(int)));
+    // the per-expert counts start at zero; the grouping's scan kernel leaves them at zero
+    GX_CUDA(cudaMemsetAsync(p.ints, 0, 512 * sizeof(int), c->stream));
     p.expert_count = p.ints;
     p.cursor = p.expert_count + 512;
     p.tile_expert = p.cursor + 512;
@@ -1393,6 +1396,10 @@ gx_result enqueue_layer_ep(gx_context *c, const Layer &L, const void *x, uint32_
 gx_result enqueue_layer(gx_context *c, const Layer &L, const void *x, uint32_t x_dtype, uint32_t n_tok,
                         const void *resid, uint32_t resid_dtype, void *out, uint32_t out_dtype, int prof_slot,
                         float norm_eps, bool chained) {
+    // programmatic dependent launch along the many-token chain for calls of up to
+    // kChainPdlMaxTokens tokens on this rank, where its kernels are short enough for the launch
+    // gaps to matter
+    gx::set_chain_pdl(n_tok <= kChainPdlMaxTokens);
     if (c->world > 1) {
         cudaEvent_t *pev = prof_slot >= 0 ? &c->prof[4 * (size_t)prof_slot] : nullptr;
         return enqueue_layer_ep(c, L, x, x_dtype, n_tok, resid, resid_dtype, out, out_dtype, norm_eps, pev);

@@ -41,6 +41,8 @@ __device__ __forceinline__ uint32_t local_expert(const EpPlanArgs &a, uint32_t e
 // [count, pad_rows) are marked empty, since with NCCL rows a destination receives pad_rows rows
 // from every source without learning the count first.
 __global__ void __launch_bounds__(kPlanTok) ep_plan_mask_kernel(EpPlanArgs a) {
+    pdl_launch_dependents();
+    pdl_wait();
     __shared__ int cnt[kMaxEpWorld];
     const int tid = threadIdx.x, lane = tid & 31;
     const int t = blockIdx.x * kPlanTok + tid;
@@ -76,6 +78,8 @@ __global__ void __launch_bounds__(kPlanTok) ep_plan_mask_kernel(EpPlanArgs a) {
 }
 
 __global__ void __launch_bounds__(kPlanTok) ep_plan_place_kernel(EpPlanArgs a) {
+    pdl_launch_dependents();
+    pdl_wait();
     constexpr int kWarps = kPlanTok / 32;
     __shared__ int base[kMaxEpWorld], total[kMaxEpWorld];
     __shared__ int wcnt[kMaxEpWorld][kWarps];
@@ -141,6 +145,8 @@ __global__ void __launch_bounds__(kPlanTok) ep_plan_place_kernel(EpPlanArgs a) {
 // out[t] = resid[t] + sum over destinations of the returned partial row of (t, d) (+ the gated
 // shared-expert row of t).
 __global__ void __launch_bounds__(256) ep_combine_kernel(EpCombineArgs a) {
+    pdl_launch_dependents();
+    pdl_wait();
     const long long i = (long long)blockIdx.x * 256 + threadIdx.x;
     const int per_row = a.E / 4;
     if (i >= (long long)a.n_tok * per_row) return;
@@ -185,16 +191,15 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(EpCombineArgs a) {
 cudaError_t launch_ep_plan(const EpPlanArgs &a, cudaStream_t s) {
     if (a.W <= 0 || a.W > kMaxEpWorld || a.NE % a.W || a.n_tok < 0) return cudaErrorInvalidValue;
     const int grid = std::max(1, ep_plan_ctas(a.n_tok));
-    ep_plan_mask_kernel<<<grid, kPlanTok, 0, s>>>(a);
-    ep_plan_place_kernel<<<grid, kPlanTok, 0, s>>>(a);
-    return cudaGetLastError();
+    cudaError_t e = launch_chain(ep_plan_mask_kernel, dim3(grid), dim3(kPlanTok), 0, s, a);
+    if (e == cudaSuccess) e = launch_chain(ep_plan_place_kernel, dim3(grid), dim3(kPlanTok), 0, s, a);
+    return e;
 }
 
 cudaError_t launch_ep_combine(const EpCombineArgs &a, cudaStream_t s) {
     const long long n = (long long)a.n_tok * (a.E / 4);
     if (n == 0) return cudaSuccess;
-    ep_combine_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(a);
-    return cudaGetLastError();
+    return launch_chain(ep_combine_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, s, a);
 }
 
 // ---- exchange over NVLink peer memory -------------------------------------------------------
@@ -250,6 +255,8 @@ __device__ bool last_cta(unsigned *done) {
 }
 
 __global__ void __launch_bounds__(256) ep_push_kernel(EpPushArgs a, int row_ctas) {
+    pdl_launch_dependents();
+    pdl_wait();
     const EpPeerArgs &p = a.p;
     const int lane = threadIdx.x & 31;
     if ((int)blockIdx.x < row_ctas) {
@@ -322,6 +329,8 @@ __global__ void __launch_bounds__(256) ep_push_kernel(EpPushArgs a, int row_ctas
 }
 
 __global__ void __launch_bounds__(1024) ep_wait_rx_kernel(EpPeerArgs a) {
+    pdl_launch_dependents();
+    pdl_wait();
     __shared__ int failed[kMaxPeers];
     __shared__ int any_failed;
     uint8_t *own = a.peer[a.rank];
@@ -351,6 +360,8 @@ __global__ void __launch_bounds__(1024) ep_wait_rx_kernel(EpPeerArgs a) {
 // One warp per received row (grid-stride): the row's U slots are read once (lane k holds slot k)
 // and every lane sums 8 columns at a time into one 16-byte store to the source's ret region.
 __global__ void __launch_bounds__(256) ep_return_kernel(EpPeerArgs a, const __half *Y, const int *slot_row) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     uint8_t *own = a.peer[a.rank];
     const int *cnt = reinterpret_cast<const int *>(own + a.off.rx_count);
@@ -399,6 +410,8 @@ __global__ void __launch_bounds__(256) ep_return_kernel(EpPeerArgs a, const __ha
 }
 
 __global__ void ep_wait_ret_kernel(EpPeerArgs a) {
+    pdl_launch_dependents();
+    pdl_wait();
     if (threadIdx.x < (unsigned)a.W)
         wait_flag(reinterpret_cast<const unsigned *>(a.peer[a.rank] + a.off.ret_flag) + threadIdx.x, a.epoch,
                   a.wait_ns, a.err);
@@ -435,14 +448,12 @@ cudaError_t launch_ep_push(const EpPushArgs &a, cudaStream_t s) {
     const int row_ctas = (int)std::min<long long>((warps + 7) / 8, kPushRowCtas);
     const int meta_ctas = (int)std::min<long long>(((long long)a.p.W * a.p.T + 255) / 256, kPushMetaCtas);
     const int grid = row_ctas + meta_ctas > 0 ? row_ctas + meta_ctas : 1;
-    ep_push_kernel<<<grid, 256, 0, s>>>(a, row_ctas);
-    return cudaGetLastError();
+    return launch_chain(ep_push_kernel, dim3(grid), dim3(256), 0, s, a, row_ctas);
 }
 
 cudaError_t launch_ep_wait_rx(const EpPeerArgs &a, cudaStream_t s) {
     if (a.W > kMaxPeers) return cudaErrorInvalidValue;
-    ep_wait_rx_kernel<<<1, 1024, 0, s>>>(a);
-    return cudaGetLastError();
+    return launch_chain(ep_wait_rx_kernel, dim3(1), dim3(1024), 0, s, a);
 }
 
 cudaError_t launch_ep_return(const EpPeerArgs &a, const __half *Y, const int *slot_row, cudaStream_t s) {
@@ -450,14 +461,12 @@ cudaError_t launch_ep_return(const EpPeerArgs &a, const __half *Y, const int *sl
     if (a.E % 8 || a.U > 32) return cudaErrorInvalidValue;
     const long long warps = (long long)a.W * a.T;
     const unsigned grid = (unsigned)std::max<long long>(1, std::min<long long>((warps + 7) / 8, kReturnCtas));
-    ep_return_kernel<<<grid, 256, 0, s>>>(a, Y, slot_row);
-    return cudaGetLastError();
+    return launch_chain(ep_return_kernel, dim3(grid), dim3(256), 0, s, a, Y, slot_row);
 }
 
 cudaError_t launch_ep_wait_ret(const EpPeerArgs &a, cudaStream_t s) {
     if (a.W > kMaxPeers) return cudaErrorInvalidValue;
-    ep_wait_ret_kernel<<<1, 32, 0, s>>>(a);
-    return cudaGetLastError();
+    return launch_chain(ep_wait_ret_kernel, dim3(1), dim3(32), 0, s, a);
 }
 
 }  // namespace gx

@@ -117,11 +117,14 @@ __global__ void __launch_bounds__(kTsThreads, 1) moe_gemm_ts_kernel(GemmArgs a) 
         *abort_flag = 0;
         fence_barrier_init();
     }
+    pdl_launch_dependents();
     if (warp == 1) tmem_alloc(tmem_slot, kTsCols);
     CBk::stage(cb, a.codebook, tid, kTsThreads);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    // everything above is independent of the predecessor kernels; their outputs are read below
+    pdl_wait();
     const uint32_t tmem_base = *tmem_slot;
     const int n_items = *a.n_mtiles * n_p;
 
@@ -400,8 +403,7 @@ cudaError_t gemm_ts_t(const GemmArgs &a, int sm_count, cudaStream_t s) {
     static const cudaError_t once =
         cudaFuncSetAttribute(moe_gemm_ts_kernel<T, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (once != cudaSuccess) return once;
-    moe_gemm_ts_kernel<T, MODE><<<sm_count, kTsThreads, smem, s>>>(a);
-    return cudaGetLastError();
+    return launch_chain(moe_gemm_ts_kernel<T, MODE>, dim3(sm_count), dim3(kTsThreads), smem, s, a);
 }
 
 }  // namespace

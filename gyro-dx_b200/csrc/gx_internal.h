@@ -363,6 +363,10 @@ cudaError_t launch_moe_gemm(const GemmArgs &a, int mode, int sm_count, cudaStrea
 // launch_moe_gemm uses it for the Gyro types (gemm_ts_routed) unless GX_GEMM_SMEM=1 selects
 // moe_gemm_kernel; its token tiles are packed compact (PackArgs::compact).
 bool gemm_ts_routed(uint32_t type);
+// Programmatic dependent launch of the many-token chain's kernels, chosen per forward call by the
+// calling thread (launch_chain in gx_device.cuh).
+bool chain_pdl_enabled();
+void set_chain_pdl(bool on);
 bool gemm_ts_supports(const GemmArgs &a, int mode);
 cudaError_t launch_moe_gemm_ts(const GemmArgs &a, int mode, int sm_count, cudaStream_t s);
 cudaError_t launch_combine(const CombineArgs &a, cudaStream_t s);

@@ -1096,7 +1096,7 @@ cudaError_t launch_router(const RouterArgs &a, cudaStream_t s, bool pdl, bool wi
 
 cudaError_t launch_topk(const RouterArgs &a, cudaStream_t s) {
     if (a.n_tok == 0) return cudaSuccess;
-    return launch(topk_kernel, (a.n_tok + 7) / 8, 256, 0, s, false, a);
+    return launch(topk_kernel, (a.n_tok + 7) / 8, 256, 0, s, chain_pdl_enabled(), a);
 }
 
 cudaError_t launch_gate_up(const GateUpArgs &a, int sm_count, cudaStream_t s, bool pdl) {

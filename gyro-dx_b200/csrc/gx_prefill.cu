@@ -32,6 +32,8 @@ namespace gx {
 // ------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) router_gemm_kernel(const float *__restrict__ W, const void *__restrict__ x,
                                                           int x_bf16, int n_tok, int NE, int E, float *__restrict__ C) {
+    pdl_launch_dependents();
+    pdl_wait();
     __shared__ __align__(16) float xs[32][64 + 4];
     __shared__ __align__(16) float ws[32][32 + 4];
     const int t0 = blockIdx.y * 64, e0 = blockIdx.x * 32;
@@ -88,12 +90,15 @@ __global__ void __launch_bounds__(256) router_gemm_kernel(const float *__restric
 // Grouping (the counting sort of src/engine.zig:553-564 without its stable order, which no
 // result depends on: every output row is computed from its own input row). Three kernels:
 //   count  per-expert slot counts (warp-aggregated atomics)
-//   scan   one CTA: 128-row tiles per expert, tile list, each expert's first row
+//   scan   one CTA: 128-row tiles per expert, tile list, each expert's first row; it leaves
+//          the counts at zero for the next grouping (they start at zero when allocated)
 //   place  each slot takes the next row of its expert (warp-aggregated atomics)
 // Slots whose id is kNoSlot (expert-parallel rows carry them for experts of other ranks) get no
 // row; any other id outside [0, NE) is reported as KERR_BOUNDS.
 // ------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(1024) group_count_kernel(GroupArgs a) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int s = blockIdx.x * 1024 + threadIdx.x;
     const bool live = s < a.n_slots;
     const uint32_t e = live ? a.ids[s] : kNoSlot;
@@ -104,9 +109,12 @@ __global__ void __launch_bounds__(1024) group_count_kernel(GroupArgs a) {
 }
 
 __global__ void __launch_bounds__(512) group_scan_kernel(GroupArgs a) {
+    pdl_launch_dependents();
+    pdl_wait();
     __shared__ int wsum[16];
     const int e = threadIdx.x, lane = e & 31, warp = e >> 5;
     const int cnt = e < a.NE ? a.expert_count[e] : 0;
+    if (e < a.NE) a.expert_count[e] = 0;       // zero again for the next grouping (no memset node)
     const int nt = (cnt + 127) / 128;
     int incl = nt;
 #pragma unroll
@@ -130,6 +138,8 @@ __global__ void __launch_bounds__(512) group_scan_kernel(GroupArgs a) {
 }
 
 __global__ void __launch_bounds__(1024) group_place_kernel(GroupArgs a) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int s = blockIdx.x * 1024 + threadIdx.x, lane = threadIdx.x & 31;
     const bool live = s < a.n_slots;
     const uint32_t e = live ? a.ids[s] : kNoSlot;
@@ -157,6 +167,8 @@ __global__ void __launch_bounds__(1024) group_place_kernel(GroupArgs a) {
 __global__ void __launch_bounds__(256) rotate_tokens_kernel(const void *x, int x_bf16, const float *xscale,
                                                             const float *signs, int n_tok, int E, __half *xh,
                                                             const int *scatter, int n_dst) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     const long long w = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
     const int nb = E / 128, groups = (nb + 3) / 4;
@@ -202,6 +214,8 @@ __global__ void __launch_bounds__(256) rotate_tokens_kernel(const void *x, int x
 // [tile][K/64][128 rows x 64 cols]. Four blocks' loads are in flight at a time.
 // ------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) pack_rows_kernel(PackArgs a) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     const long long row = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
     const int nb = a.K / 128;
@@ -334,11 +348,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) moe_gemm_kernel(GemmArgs a) {
         *abort_flag = 0;
         fence_barrier_init();
     }
+    pdl_launch_dependents();
     if (warp == 1) tmem_alloc(tmem_slot, 512);
     CBk::stage(cb, a.codebook, tid, kGemmThreads);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    // everything above is independent of the predecessor kernels; their outputs are read below
+    pdl_wait();
     const uint32_t tmem_base = *tmem_slot;
     const int n_items = *a.n_mtiles * a.n_ntiles;
 
@@ -609,6 +626,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) moe_gemm_kernel(GemmArgs a) {
 // without a row (row < 0: served by another rank) add nothing.
 // ------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) combine_kernel(CombineArgs a) {
+    pdl_launch_dependents();
+    pdl_wait();
     const long long i = (long long)blockIdx.x * 256 + threadIdx.x;
     const int per_row = a.E / 4;
     if (i >= (long long)a.n_tok * per_row) return;
@@ -656,29 +675,38 @@ __global__ void __launch_bounds__(256) combine_kernel(CombineArgs a) {
 // ------------------------------------------------------------------------------------------
 // Host launchers
 // ------------------------------------------------------------------------------------------
+namespace {
+thread_local bool t_chain_pdl = false;   // the calling thread's current forward call
+}
+void set_chain_pdl(bool on) {
+    static const bool allowed = [] {
+        const char *v = getenv("GX_PDL");
+        return !(v && v[0] == '0');
+    }();
+    t_chain_pdl = allowed && on;
+}
+bool chain_pdl_enabled() { return t_chain_pdl; }
+
 cudaError_t launch_router_gemm(const float *W, const void *x, int x_bf16, int n_tok, int NE, int E, float *C,
                                int splits, cudaStream_t s) {
     dim3 grid((NE + 31) / 32, (n_tok + 63) / 64, splits);
-    router_gemm_kernel<<<grid, 256, 0, s>>>(W, x, x_bf16, n_tok, NE, E, C);
-    return cudaGetLastError();
+    return launch_chain(router_gemm_kernel, grid, dim3(256), 0, s, W, x, x_bf16, n_tok, NE, E, C);
 }
 
 cudaError_t launch_group(const GroupArgs &a, cudaStream_t s) {
     if (a.NE > 512) return cudaErrorInvalidValue;
-    cudaError_t e = cudaMemsetAsync(a.expert_count, 0, (size_t)a.NE * sizeof(int), s);
-    if (e != cudaSuccess) return e;
     const unsigned blocks = (unsigned)((a.n_slots + 1023) / 1024);
-    if (blocks) group_count_kernel<<<blocks, 1024, 0, s>>>(a);
-    group_scan_kernel<<<1, 512, 0, s>>>(a);
-    if (blocks) group_place_kernel<<<blocks, 1024, 0, s>>>(a);
-    return cudaGetLastError();
+    cudaError_t e = cudaSuccess;
+    if (blocks) e = launch_chain(group_count_kernel, dim3(blocks), dim3(1024), 0, s, a);
+    if (e == cudaSuccess) e = launch_chain(group_scan_kernel, dim3(1), dim3(512), 0, s, a);
+    if (e == cudaSuccess && blocks) e = launch_chain(group_place_kernel, dim3(blocks), dim3(1024), 0, s, a);
+    return e;
 }
 
 cudaError_t launch_pack_rows(const PackArgs &a, int max_tiles, cudaStream_t s) {
     const long long warps = (long long)max_tiles * 128;
     if (warps == 0) return cudaSuccess;
-    pack_rows_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(a);
-    return cudaGetLastError();
+    return launch_chain(pack_rows_kernel, dim3((unsigned)((warps + 7) / 8)), dim3(256), 0, s, a);
 }
 
 namespace {
@@ -688,8 +716,7 @@ cudaError_t gemm_t(const GemmArgs &a, int sm_count, cudaStream_t s) {
     static const cudaError_t once =
         cudaFuncSetAttribute(moe_gemm_kernel<T, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (once != cudaSuccess) return once;
-    moe_gemm_kernel<T, MODE><<<sm_count, kGemmThreads, smem, s>>>(a);
-    return cudaGetLastError();
+    return launch_chain(moe_gemm_kernel<T, MODE>, dim3(sm_count), dim3(kGemmThreads), smem, s, a);
 }
 }  // namespace
 
@@ -720,16 +747,14 @@ cudaError_t launch_rotate_tokens(const void *x, int x_bf16, const float *xscale,
                                 int E, __half *xh, cudaStream_t s, const int *scatter, int n_dst) {
     const long long warps = (long long)n_tok * ((E / 128 + 3) / 4);
     if (warps == 0) return cudaSuccess;
-    rotate_tokens_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(x, x_bf16, xscale, signs, n_tok, E, xh,
-                                                                      scatter, n_dst);
-    return cudaGetLastError();
+    return launch_chain(rotate_tokens_kernel, dim3((unsigned)((warps + 7) / 8)), dim3(256), 0, s, x, x_bf16, xscale,
+                        signs, n_tok, E, xh, scatter, n_dst);
 }
 
 cudaError_t launch_combine(const CombineArgs &a, cudaStream_t s) {
     const long long n = (long long)a.n_tok * (a.E / 4);
     if (n == 0) return cudaSuccess;
-    combine_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(a);
-    return cudaGetLastError();
+    return launch_chain(combine_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, s, a);
 }
 
 }  // namespace gx

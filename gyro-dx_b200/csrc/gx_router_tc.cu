@@ -72,10 +72,13 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(RtArgs a) {
         *abort_flag = 0;
         fence_barrier_init();
     }
+    pdl_launch_dependents();
     if (warp == 5) tmem_alloc(tmem_slot, 128);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    // everything above is independent of the predecessor kernels; their outputs are read below
+    pdl_wait();
     const uint32_t tmem_base = *tmem_slot;
 
     auto wait = [&](uint64_t *bar, uint32_t parity) -> bool {
@@ -222,8 +225,7 @@ cudaError_t router_tc_t(const RtArgs &a, dim3 grid, cudaStream_t s) {
     static const cudaError_t once =
         cudaFuncSetAttribute(router_tc_kernel<AP>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
     if (once != cudaSuccess) return once;
-    router_tc_kernel<AP><<<grid, kRtThreads, SMEM, s>>>(a);
-    return cudaGetLastError();
+    return launch_chain(router_tc_kernel<AP>, grid, dim3(kRtThreads), SMEM, s, a);
 }
 
 }  // namespace
