@@ -91,7 +91,6 @@ struct gx_context {
     struct Prefill {
         size_t max_tiles = 0, E = 0, F = 0, slots = 0;
         uint8_t *A = nullptr, *A2 = nullptr;
-        __half *xh = nullptr;
         float *act = nullptr;
         __half *Y = nullptr;
         int *ints = nullptr;  // expert_count | cursor | tile_expert | tile_rows | n_mtiles | row_slot | slot_row
@@ -323,7 +322,7 @@ void release_all(gx_context *c) {
                   c->hc.xn, c->hc.lo, c->hc.inj, c->hc.cur, c->hc.y, c->hc.A, c->hc.A2, c->hc.Ylo, c->hc.gate,
                   c->hc.ints};
     for (void *p : sh) if (p) cudaFree(p);
-    void *pf[] = {c->pf.A, c->pf.A2, c->pf.act, c->pf.Y, c->pf.ints, c->pf.xh};
+    void *pf[] = {c->pf.A, c->pf.A2, c->pf.act, c->pf.Y, c->pf.ints};
     for (void *p : pf) if (p) cudaFree(p);
     for (auto &m : c->mats) if (m.tiles) cudaFree(m.tiles);
     void *dev[] = {c->codebook, c->codebook_image, c->router_done, c->logits, c->weights, c->xscale, c->ss, c->ids,
@@ -370,7 +369,7 @@ gx_result ensure_prefill(gx_context *c, const Layer &L, size_t slots) {
     const size_t tiles = (slots + 127) / 128 + std::min<size_t>(L.local_experts + L.replica_slots, slots);
     auto &p = c->pf;
     if (p.max_tiles >= tiles && p.E >= L.E && p.F >= L.F && p.slots >= slots) return GX_OK;
-    void *old[] = {p.A, p.A2, p.act, p.Y, p.ints, p.xh};
+    void *old[] = {p.A, p.A2, p.act, p.Y, p.ints};
     bool had = false;
     for (void *q : old) if (q) { cudaFree(q); had = true; }
     p = gx_context::Prefill{};
@@ -385,7 +384,6 @@ gx_result ensure_prefill(gx_context *c, const Layer &L, size_t slots) {
     GX_CUDA(cudaMalloc(&p.A2, tiles * (L.F / 64) * 16384));
     GX_CUDA(cudaMalloc(&p.act, tiles * 128 * L.F * sizeof(float)));
     GX_CUDA(cudaMalloc(&p.Y, tiles * 128 * L.E * sizeof(__half)));
-    GX_CUDA(cudaMalloc(&p.xh, (size_t)c->max_tokens * L.E * sizeof(__half)));
     const size_t n_ints = 1024 + 2 * tiles + 1 + tiles * 128 + slots;
     GX_CUDA(cudaMalloc(&p.ints, n_ints * sizeof(int)));
     // the per-expert counts start at zero; the grouping's scan kernel leaves them at zero
@@ -708,21 +706,20 @@ gx_result enqueue_layer_prefill(gx_context *c, const Layer &L, const void *x, ui
     ga.slot_row = p.slot_row;
     ga.err = c->err;
     GX_CUDA(gx::launch_group(ga, c->stream));
-    gx::PackArgs pa{};
-    pa.src = x;
-    pa.src_bf16 = xb;
-    pa.by_token = 1;
-    pa.U = (int)L.U;
-    pa.K = (int)L.E;
-    GX_CUDA(gx::launch_rotate_tokens(x, xb, norm_eps > 0.f ? c->xscale : nullptr, L.gate_signs, (int)n_tok,
-                                     (int)L.E, p.xh, c->stream));
-    pa.xh = p.xh;
-    pa.row_slot = p.row_slot;
-    pa.tile_rows = p.tile_rows;
-    pa.n_mtiles = p.n_mtiles;
-    pa.dst = p.A;
-    pa.compact = gx::gemm_ts_routed(L.type);
-    GX_CUDA(gx::launch_pack_rows(pa, (int)p.max_tiles, c->stream));
+    // each token rotated once and stored into the tile rows of its slots
+    gx::RotPackArgs rp{};
+    rp.x = x;
+    rp.x_bf16 = xb;
+    rp.xscale = norm_eps > 0.f ? c->xscale : nullptr;
+    rp.signs = L.gate_signs;
+    rp.n_tok = (int)n_tok;
+    rp.E = (int)L.E;
+    rp.U = (int)L.U;
+    rp.slot_row = p.slot_row;
+    rp.tile_rows = p.tile_rows;
+    rp.dst = p.A;
+    rp.compact = gx::gemm_ts_routed(L.type);
+    GX_CUDA(gx::launch_rotate_pack(rp, c->stream));
     if (ev) GX_CUDA(record_phase(ev[1], c->stream));
     gx::GemmArgs gm{};
     gm.type = L.type;

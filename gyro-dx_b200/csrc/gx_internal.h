@@ -179,6 +179,20 @@ struct PackArgs {
                              // (moe_gemm_ts_kernel), instead of 16384 B each
 };
 
+// Token rotation fused with the token pack (single-GPU many-token path): each token is rotated
+// once and its f16 row written straight into the tile row of each of its slots.
+struct RotPackArgs {
+    const void *x;
+    int x_bf16;
+    const float *xscale;     // [n_tok] per-token scale, or nullptr
+    const float *signs;      // [E] or nullptr (then no Hadamard transform)
+    int n_tok, E, U;
+    const int *slot_row;     // [n_tok * U] padded row of each slot, -1 for none
+    const int *tile_rows;    // rows of each 128-row tile
+    uint8_t *dst;            // token tiles [tiles][E/64][16384]
+    int compact;             // as PackArgs::compact
+};
+
 struct GemmArgs {
     uint32_t type;           // Gyro type id, or W_Q8 / W_F16 for the shared expert's matrices
     const uint8_t *w0, *w1;  // gate + up (mode 0) or down (mode 1) tiles of local expert 0
@@ -358,6 +372,7 @@ cudaError_t launch_ep_wait_ret(const EpPeerArgs &a, cudaStream_t s);
 cudaError_t launch_ep_combine(const EpCombineArgs &a, cudaStream_t s);
 cudaError_t launch_group(const GroupArgs &a, cudaStream_t s);
 cudaError_t launch_pack_rows(const PackArgs &a, int max_tiles, cudaStream_t s);
+cudaError_t launch_rotate_pack(const RotPackArgs &a, cudaStream_t s);
 cudaError_t launch_moe_gemm(const GemmArgs &a, int mode, int sm_count, cudaStream_t s);
 // The routed experts' grouped GEMM with the decoded weights in tensor memory (gx_gemm_ts.cu):
 // launch_moe_gemm uses it for the Gyro types (gemm_ts_routed) unless GX_GEMM_SMEM=1 selects

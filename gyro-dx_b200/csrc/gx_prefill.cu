@@ -208,6 +208,57 @@ __global__ void __launch_bounds__(256) rotate_tokens_kernel(const void *x, int x
 }
 
 // ------------------------------------------------------------------------------------------
+// Rotation and packing in one pass (the single-GPU many-token path): one warp per (token, 4
+// blocks) rotates as rotate_tokens_kernel does and stores the f16 row into the tile row of each
+// of the token's slots, in the layout pack_rows_kernel writes. The rows a tile has past its
+// tokens are not written: the MMA columns they feed are never stored.
+// ------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) rotate_pack_kernel(RotPackArgs a) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int lane = threadIdx.x & 31;
+    const long long w = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int nb = a.E / 128, groups = (nb + 3) / 4;
+    if (w >= (long long)a.n_tok * groups) return;
+    const int t = (int)(w / groups), b0 = (int)(w % groups) * 4;
+    const float sc = a.xscale ? a.xscale[t] : 1.f;
+    uint2 o[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const int b = b0 + q;
+        if (b >= nb) break;
+        const size_t base = (size_t)t * a.E + b * 128 + 4 * lane;
+        float v[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[j] = load_act(a.x, a.x_bf16, base + j) * sc;
+        if (a.signs) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) v[j] *= a.signs[b * 128 + 4 * lane + j];
+            fwht128_warp(v, lane);
+        }
+        o[q].x = pack_half2(v[0], v[1]);
+        o[q].y = pack_half2(v[2], v[3]);
+    }
+    const int ks_lo = lane >> 4, col = 4 * (lane & 15);
+    for (int k = 0; k < a.U; ++k) {
+        const int row = a.slot_row[(size_t)t * a.U + k];
+        if (row < 0) continue;
+        const int tile = row >> 7, i = row & 127;
+        const int rows_t = a.tile_rows[tile];
+        const int np = a.compact ? (rows_t <= 16 ? 16 : (rows_t + 15) & ~15) : 128;
+        uint8_t *base = a.dst + (size_t)tile * (a.E / 64) * 16384u;
+        const size_t kblock = (size_t)np * 128u;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int b = b0 + q;
+            if (b >= nb) break;
+            *reinterpret_cast<uint2 *>(base + (size_t)(2 * b + ks_lo) * kblock + sw128_offset((uint32_t)i, (uint32_t)col)) =
+                o[q];
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------------
 // Row packing: one warp per padded row. Source row = token of the slot (gate/up input, x) or
 // the padded row itself (down input, act). v = src * scale, * signs, then H128 / sqrt(128) per
 // 128-column block when signs are given; f16 into the swizzled K-major tile layout
@@ -701,6 +752,12 @@ cudaError_t launch_group(const GroupArgs &a, cudaStream_t s) {
     if (e == cudaSuccess) e = launch_chain(group_scan_kernel, dim3(1), dim3(512), 0, s, a);
     if (e == cudaSuccess && blocks) e = launch_chain(group_place_kernel, dim3(blocks), dim3(1024), 0, s, a);
     return e;
+}
+
+cudaError_t launch_rotate_pack(const RotPackArgs &a, cudaStream_t s) {
+    const long long warps = (long long)a.n_tok * ((a.E / 128 + 3) / 4);
+    if (warps == 0) return cudaSuccess;
+    return launch_chain(rotate_pack_kernel, dim3((unsigned)((warps + 7) / 8)), dim3(256), 0, s, a);
 }
 
 cudaError_t launch_pack_rows(const PackArgs &a, int max_tiles, cudaStream_t s) {
