@@ -377,7 +377,7 @@ def measure_prefill(torch, dev, T: int, K: int, W: int) -> dict:
         "value": K * T / (ms / 1e3), "unit": "tok/s", "ms_per_step": ms / K, "steps": K, "warmup": W,
         "experts_hit": int((counts > 0).sum()), "max_segment": int(counts.max()), "row_tiles": tiles,
         "roofline": {
-            "kernel": "moe_gemm_kernel<gate/up> (tcgen05 grouped GEMM, in-smem trellis decode, SwiGLU epilogue)",
+            "kernel": "moe_gemm_ts_kernel<gate/up> (tcgen05 grouped GEMM, decoded weights in TMEM, SwiGLU epilogue)",
             "bound": "tensor", "achieved": achieved, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
             "frac": achieved / pk["bf16_tflops"], "traffic": traffic_bytes("moe_gemm_gateup_prefill_per_launch"),
             "algorithmic_flops_per_launch": gu_flops, "launch_us": gu_s * 1e6,
@@ -390,7 +390,7 @@ def measure_prefill(torch, dev, T: int, K: int, W: int) -> dict:
         "e2e": {"value": e2e_steps * T / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": T * E * 2,
                 "d2h_bytes_per_step": T * E * 2, "steps": e2e_steps,
                 "api": "gx_moe_forward_host (host bf16 in, host bf16 out)"},
-        "gpu_launches": K * 11,
+        "gpu_launches": K * 9,
         "clocks": clocks,
         "l2": "inputs larger than L2: a step reads every touched expert (up to 214 MB)",
     }
@@ -630,10 +630,12 @@ def run_ep(args):
     (h2d_max,) = d.reduce([n_tok * E * 2], "max")
     ctx.close()
 
-    # router, top-k, rotation (push with peer memory), three grouping kernels, two packs, two
-    # GEMMs, combine (return with peer memory); expert parallel adds the two plan kernels and the
-    # sum of partial rows, and with peer memory the two bounded waits
-    launches_per_layer = 11 if world == 1 else 16 if exchange == abi.GX_EP_PEER else 14
+    # one GPU: router, top-k, three grouping kernels, rotation + pack (one kernel), two GEMMs (the
+    # gate/up epilogue writes the down operand), combine = 9. Expert parallel: router, top-k, plan,
+    # three grouping kernels, pack, two GEMMs, sum of the partial rows, plus push, bounded wait,
+    # return, bounded wait with peer memory (14) or rotation and combine with NCCL (12; NCCL's
+    # own kernels not counted)
+    launches_per_layer = 9 if world == 1 else 14 if exchange == abi.GX_EP_PEER else 12
     line = {
         "metric": METRIC, "value": K * T / (ms / 1e3), "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
         "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
@@ -649,7 +651,7 @@ def run_ep(args):
                    "tokens_per_rank_max": max_tok,
                    "l2": "inputs larger than L2: a step reads every touched expert of 40 layers"},
         "roofline": {
-            "kernel": "moe_gemm_kernel<gate/up> on each rank's received slots (tcgen05 grouped GEMM)",
+            "kernel": "moe_gemm_ts_kernel<gate/up> on each rank's received slots (tcgen05 grouped GEMM)",
             "bound": "tensor", "achieved": achieved, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
             "frac": achieved / pk["bf16_tflops"] if achieved else None,
             "traffic": traffic_bytes("moe_gemm_gateup_ep_per_launch"),
