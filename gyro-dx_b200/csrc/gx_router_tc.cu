@@ -184,31 +184,36 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(RtArgs a) {
             }
         }
     } else {
-        // ---- MMA issuer ----------------------------------------------------------------------
-        if (lane == 0) {
-            const uint32_t idesc = f16_idesc(128, 128) | (1u << 7) | (1u << 10);  // A and B bf16
-            bool ok = true, first = true;
-            for (int i = 0; i < nks; ++i) {
-                const int s = i % ST, round = i / ST;
-                if (!wait(&full_a[s], round & 1) || !wait(&full_b[s], round & 1)) { ok = false; break; }
-                tc_fence_after();
-                const uint32_t at = smem_u32(sm + s * STAGE), bt = at + AP * kRtPart;
+        // ---- MMA issuer: the whole warp runs the loop and takes the waits (a warp vote makes
+        // each outcome uniform); one elected lane issues the MMAs and the commits ---------------
+        const bool leader = elect_one();
+        const uint32_t idesc = f16_idesc(128, 128) | (1u << 7) | (1u << 10);  // A and B bf16
+        bool ok = true;
+        for (int i = 0; i < nks; ++i) {
+            const int s = i % ST, round = i / ST;
+            const bool ready = wait(&full_a[s], round & 1) && wait(&full_b[s], round & 1);
+            if (!__all_sync(0xffffffffu, ready)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t at = smem_u32(sm + s * STAGE), bt = at + AP * kRtPart;
+            if (leader) {
 #pragma unroll
                 for (int k = 0; k < 4; ++k)
 #pragma unroll
                     for (int xi = 0; xi < AP; ++xi)
 #pragma unroll
-                        for (int wj = 0; wj < 3 - xi; ++wj) {
+                        for (int wj = 0; wj < 3 - xi; ++wj)
                             umma_f16(tmem_base, sw128_desc(at + xi * kRtPart + 32 * k),
-                                     sw128_desc(bt + wj * kRtPart + 32 * k), idesc, first ? 0u : 1u);
-                            first = false;
-                        }
+                                     sw128_desc(bt + wj * kRtPart + 32 * k), idesc, (i | k | xi | wj) != 0 ? 1u : 0u);
                 umma_commit(&empty[s]);
             }
+            __syncwarp();
+        }
+        if (leader) {
             if (ok) umma_commit(acc_full);
             umma_commit(done);
             mbar_wait(done, 0, nullptr);
         }
+        __syncwarp();
     }
     tc_fence_before();
     __syncthreads();
