@@ -17,7 +17,8 @@
 //
 // Roles (832 threads):
 //   warp 0      token tiles: as many 64-wide k-steps of the tile as fit 32 KB per bulk copy
-//   warp 1      TMEM allocation; one lane issues the MMAs (8 per k-step) and the commits
+//   warp 1      TMEM allocation; the whole warp runs the issue loop, one elected lane issues the
+//               MMAs (8 per k-step) and the commits
 //   warps 2-17  decoders in 2 sets of 8 warps: set j decodes the CTA's k-steps n = j, j + 2, ...
 //               (over its items in order); (warp - 2) / 4 % 2 picks the weight tile and warp % 4
 //               the TMEM lane quarter; one thread decodes one weight row's 64 weights of a k-step
